@@ -1,0 +1,168 @@
+/*
+ * rola_b200.h -- C ABI of the B200 (sm_100a) RoLa attention forward.
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer to
+ * bf16 (`void*`), fp32 (`float*`) or int32 data in the layout stated beside it,
+ * every size is an integer, and `stream` is a cudaStream_t passed as void*.
+ * Every entry point returns ROLA_OK (0) or an error code; the message of the
+ * last error on the calling thread is available from rola_b200_last_error().
+ * Nothing is launched when argument validation fails.  There is no CPU
+ * fallback: every entry point launches CUDA kernels built for sm_100a.
+ *
+ * Shapes: B batch, L tokens, H heads, D = 128 head dim, dim = H*D,
+ * blk block size, NB = ceil(L/blk), k = kept key blocks, R low-rank rank (64).
+ * "token-major" = [B*L rows, row stride ld] with head h in columns
+ * [h*D, h*D + D).  The reference's own layouts are noted per entry point.
+ *
+ * Reference = AlibabaResearch/SparkDiffusion, paths relative to its root.
+ */
+#ifndef ROLA_B200_H_
+#define ROLA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* rola_stream_t;
+
+#define ROLA_B200_ABI_VERSION 1
+
+#define ROLA_OK 0
+#define ROLA_ERR_INVALID 1 /* bad shape, size, alignment or null pointer */
+#define ROLA_ERR_CUDA 2    /* a CUDA runtime/driver call or a launch failed */
+#define ROLA_ERR_DEVICE 3  /* a kernel recorded a device-side error */
+
+/* device-side error codes reported by rola_b200_device_status() */
+#define ROLA_DEV_OK 0
+#define ROLA_DEV_TIMEOUT_LOAD 1    /* a bounded wait for a TMA load expired */
+#define ROLA_DEV_TIMEOUT_MMA 2     /* a bounded wait for an MMA completion expired */
+#define ROLA_DEV_TIMEOUT_SOFTMAX 3 /* a bounded wait for the softmax hand-off expired */
+#define ROLA_DEV_BAD_INDEX 4       /* a LUT entry outside [0, NB) (clamped) */
+
+int rola_b200_abi_version(void);
+const char* rola_b200_last_error(void);
+
+/* Read (and optionally clear) the device-side error flag of the current device.
+ * Synchronises the device.  Returns the ROLA_DEV_* code, or -1 on a CUDA error. */
+int rola_b200_device_status(int clear);
+
+/* (a4) QKV projection: out[M, N] (row stride N) = x[M, K] . w[N, K]^T + bias[N].
+ * bias may be NULL.  N % 256 == 0, K % 64 == 0.
+ * Replaces the three F.linear calls of fused_qkv_gemm_rope
+ * (sparkdiffusion/ops/fused_kernel/fused_qkv_rope.py:287-289) with one GEMM over
+ * the concatenated weight [Wq; Wk; Wv]. */
+int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out, int64_t M, int64_t N, int64_t K,
+                       rola_stream_t stream);
+
+/* (a4 epilogue, a5 q-pool, a6 block sums, a10 gate) in one pass over the rows.
+ * q_raw/k_raw: token-major, row stride ld_raw.  x: token-major [B*L, dim] (gate
+ * input; NULL skips the gate).  norm_wq/norm_wk: [dim] (both NULL = no norm).
+ * cos_sin: [L, D] fp32 interleaved (cos0, sin0, cos1, ...).  gate_w: [D],
+ * gate_b: [H] bf16.  Outputs (any may be NULL): q_rope, k_rope, q_normed,
+ * k_normed token-major [B*L, dim]; gate_out [B*L, H]; pooled_q [B, H, NB, D]
+ * bf16; ksum [B, NB, dim] fp32 block sums of k_rope.  H <= 64.
+ * Replaces _epilogue_kernel (fused_qkv_rope.py:53-225, layout [B*H, L, D] there),
+ * mean_pool(q) (utils.py:272-297 via fused_sparse_attn.py:179) and the gate
+ * logits of _gate_fusion_kernel (fused_gate.py:97-114). */
+int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw, const void* x, const void* norm_wq,
+                           const void* norm_wk, const float* cos_sin, const void* gate_w, const void* gate_b, int B,
+                           int L, int H, int blk, float eps, void* q_rope, void* k_rope, void* q_normed,
+                           void* k_normed, void* gate_out, void* pooled_q, float* ksum, rola_stream_t stream);
+
+/* Sequence-parallel half of the prologue epilogue (before the Ulysses
+ * all-to-all): qk-RMSNorm and gate on a sequence shard, writing q_normed,
+ * k_normed and v into send buffers laid out [H/heads_per_chunk][B*L][heads_per_chunk*D]
+ * (one contiguous chunk per destination rank).  Same reference interface as
+ * rola_b200_qk_norm_rope. */
+int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_raw, int64_t ld_raw, const void* x,
+                           const void* norm_wq, const void* norm_wk, const void* gate_w, const void* gate_b, int B,
+                           int L, int H, int heads_per_chunk, float eps, void* q_send, void* k_send, void* v_send,
+                           void* gate_out, rola_stream_t stream);
+
+/* Head-parallel half (after the all-to-all): RoPE, q-pool and k block sums from
+ * the normed q/k (token-major, row stride ld).  Same reference interface as
+ * rola_b200_qk_norm_rope. */
+int rola_b200_rope_pool(const void* q_normed, const void* k_normed, int64_t ld, const float* cos_sin, int B, int L,
+                        int H, int blk, void* q_rope, void* k_rope, void* pooled_q, float* ksum,
+                        rola_stream_t stream);
+
+/* (a5) block mean pooling, mean_pool (sparkdiffusion/ops/fused_kernel/utils.py:272-297).
+ * Element (b, h, t, d) of x sits at x + b*sB + h*sH + t*sT + d (elements).
+ * center: [B, H, D] or NULL; out: [B, H, NB, D] bf16.  Rows are summed in order. */
+int rola_b200_mean_pool(const void* x, int64_t sB, int64_t sH, int64_t sT, int B, int H, int L, int blk,
+                        const void* center, void* out, rola_stream_t stream);
+
+/* (a6) smooth-K centre, k.mean(dim=-2) (fused_sparse_attn.py:180): center [B, H, D] bf16.
+ * ksum_ws: fp32 scratch of B*NB*H*D floats (block sums). */
+int rola_b200_smooth_k_center(const void* k, int64_t sB, int64_t sH, int64_t sT, int B, int H, int L, int blk,
+                              float* ksum_ws, void* center, rola_stream_t stream);
+
+/* (a6) centre from precomputed block sums ksum [B, NB, dim]. */
+int rola_b200_center_from_sums(const float* ksum, int B, int NB, int dim, int L, void* center,
+                               rola_stream_t stream);
+
+/* (a7) pooled scores (fp32) and top-k selection: pooled_q [BH, NBq, D],
+ * pooled_k [BH, NBk, D] bf16 -> lut [BH, NBq, topk] int32 ascending, ties toward
+ * the lower block index.  scores_ws: fp32 scratch of BH*NBq*NBk floats.
+ * Replaces `pooled_q @ pooled_k^T` + torch.topk (fused_sparse_attn.py:181-198). */
+int rola_b200_block_select(const void* pooled_q, const void* pooled_k, int BH, int NBq, int NBk, int topk,
+                           float* scores_ws, int32_t* lut, rola_stream_t stream);
+
+/* (a9) q_lr = RoPE_rank(SiLU(q_normed . proj_q^T)).  Element (b, h, t, d) of
+ * q_normed sits at q_normed + sB*b + sH*h + sT*t + d (elements; 16-byte rows).
+ * proj_q [R, D], lr_cos/lr_sin [L, rope_dim] bf16 -> q_lr [B*L, H*R] bf16.  R == 64.
+ * Replaces _proj_silu_rope_kernel (sparkdiffusion/ops/fused_kernel/fused_lowrank.py:31-152). */
+int rola_b200_lowrank_q(const void* q_normed, int64_t sB, int64_t sH, int64_t sT, const void* proj_q,
+                        const void* lr_cos, const void* lr_sin, int rope_dim, int B, int L, int H, int R, void* q_lr,
+                        rola_stream_t stream);
+
+/* (a9) C = k_lr^T v per (b, h).  k_normed and v are strided views as in
+ * rola_b200_lowrank_q (k_s* and v_s* strides) -> C [B*H, R, D] and
+ * Ct [B*H, D, R] bf16 (either may be NULL).  c_partial_ws: fp32 scratch of
+ * splits*B*H*R*D floats.  R == 64.
+ * Replaces fused_lowrank.py:331-358 (k_lr projection + cuBLAS k_lr^T v). */
+int rola_b200_lowrank_kv(const void* k_normed, int64_t k_sB, int64_t k_sH, int64_t k_sT, const void* v, int64_t v_sB,
+                         int64_t v_sH, int64_t v_sT, const void* proj_k, const void* lr_cos, const void* lr_sin,
+                         int rope_dim, int B, int L, int H, int R, int splits, float* c_partial_ws, void* C, void* Ct,
+                         rola_stream_t stream);
+
+/* (a8 + a9 o_lr + a10) block-sparse attention with the fused low-rank + gate
+ * epilogue.  q and k share strides (qk_s*), v has its own (v_s*), out and
+ * o_sparse share o_s*: element (b, h, t, d) at p + sB*b + sH*h + sT*t + d, all
+ * strides multiples of 8 elements.  lut [B*H, NBq, topk] int32; q_lr [B*L, H*R]
+ * and Ct [B*H, D, R] (both NULL: no low-rank branch and out = o_sparse);
+ * gate [B*L, H] bf16 (NULL: gate 0).  out / o_sparse may be NULL (not both).
+ * blk == 128, R == 64.
+ * Replaces _rola_fwd_kernel (fused_sparse_attn.py:55-144), the o_lr matmul
+ * (fused_lowrank.py:360-362) and _gate_fusion_kernel (fused_gate.py:27-127). */
+int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT, const void* v,
+                          int64_t v_sB, int64_t v_sH, int64_t v_sT, const int32_t* lut, int B, int L, int H, int blk,
+                          int topk, const void* q_lr, const void* Ct, const void* gate, float eps_lr, void* out,
+                          void* o_sparse, int64_t o_sB, int64_t o_sH, int64_t o_sT, rola_stream_t stream);
+
+/* Workspace bytes needed by rola_b200_rola_forward for these sizes. */
+size_t rola_b200_forward_workspace_bytes(int B, int L, int H, int blk, int R, int splits);
+
+/* Whole RoLa attention forward up to (excluding) the output projection, from
+ * the hidden states: WanSelfAttentionRoLa.fused_forward minus self.o
+ * (sparkdiffusion/networks/wan_rola_attention.py:414-446).
+ * x [B*L, dim]; w_qkv [3*dim, dim] (= [Wq; Wk; Wv]); b_qkv [3*dim] or NULL;
+ * norm_wq/norm_wk [dim]; cos_sin [L, D] fp32; lr_cos/lr_sin [L, rope_dim];
+ * proj_q/proj_k [R, D]; gate_w [D]; gate_b [H] bf16; out [B*L, dim] bf16.
+ * workspace: device memory of rola_b200_forward_workspace_bytes() bytes
+ * (256-byte aligned); lut_out [B*H, NB, topk] int32 may be NULL. */
+int rola_b200_rola_forward(const void* x, const void* w_qkv, const void* b_qkv, const void* norm_wq,
+                           const void* norm_wk, const float* cos_sin, const void* lr_cos, const void* lr_sin,
+                           int rope_dim, const void* proj_q, const void* proj_k, const void* gate_w,
+                           const void* gate_b, int B, int L, int H, int blk, int topk, int R, int splits, float eps,
+                           void* workspace, size_t workspace_bytes, void* out, int32_t* lut_out,
+                           rola_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ROLA_B200_H_ */

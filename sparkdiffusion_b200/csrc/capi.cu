@@ -1,0 +1,491 @@
+// extern "C" entry points of librola_b200.so (declared in include/rola_b200.h).
+//
+// Each entry point validates its arguments on the host (returning
+// ROLA_ERR_INVALID with a message and launching nothing), builds the TMA
+// tensor maps it needs, and launches the kernels on the caller's stream.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/rola_b200.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_status(int launch_rc, const char* what) {
+  if (launch_rc == 0) return ROLA_OK;
+  if (launch_rc < 0) return fail(ROLA_ERR_INVALID, "%s: unsupported configuration", what);
+  return fail(ROLA_ERR_CUDA, "%s: %s", what, cudaGetErrorString((cudaError_t)launch_rc));
+}
+
+#define ROLA_CHECK(cond, ...)                          \
+  do {                                                 \
+    if (!(cond)) return fail(ROLA_ERR_INVALID, __VA_ARGS__); \
+  } while (0)
+
+#define ROLA_TRY(expr)            \
+  do {                            \
+    int _rc = (expr);             \
+    if (_rc != ROLA_OK) return _rc; \
+  } while (0)
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline cudaStream_t S(rola_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+inline const __nv_bfloat16* BF(const void* p) { return reinterpret_cast<const __nv_bfloat16*>(p); }
+inline __nv_bfloat16* BFm(void* p) { return reinterpret_cast<__nv_bfloat16*>(p); }
+
+// ---------------------------------------------------------------------------
+// TMA descriptors through the driver entry point (no libcuda link dependency)
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// bf16 tensor of rank 2 or 3: dims innermost first, strides (bytes) of dims 1.., box innermost first
+int make_map(CUtensorMap* m, const void* ptr, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
+             const uint32_t* box, const char* what) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(ROLA_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", what);
+  ROLA_CHECK(aligned16(ptr), "%s: base address must be 16-byte aligned", what);
+  for (int i = 0; i < rank - 1; ++i)
+    ROLA_CHECK(strides_bytes[i] % 16 == 0, "%s: row strides must be multiples of 16 bytes", what);
+  cuuint64_t gd[5], gs[4];
+  cuuint32_t bd[5], es[5] = {1, 1, 1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    bd[i] = box[i];
+  }
+  for (int i = 0; i < rank - 1; ++i) gs[i] = strides_bytes[i];
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(ptr), gd, gs, bd, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ROLA_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
+  return ROLA_OK;
+}
+
+// token-major [B, L, cols] view (row stride ld elements) with [64 x 128 x 1] boxes
+int make_token_map(CUtensorMap* m, const void* ptr, int64_t cols, int64_t ld, int L, int B, const char* what) {
+  const uint64_t dims[3] = {(uint64_t)cols, (uint64_t)L, (uint64_t)B};
+  const uint64_t strides[2] = {(uint64_t)ld * 2, (uint64_t)ld * 2 * (uint64_t)L};
+  const uint32_t box[3] = {64, 128, 1};
+  return make_map(m, ptr, 3, dims, strides, box, what);
+}
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace
+
+using namespace rola;
+
+extern "C" {
+
+int rola_b200_abi_version(void) { return ROLA_B200_ABI_VERSION; }
+
+const char* rola_b200_last_error(void) { return g_last_error.c_str(); }
+
+int rola_b200_device_status(int clear) {
+  int v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return -1;
+  if (clear) {
+    int z = 0;
+    if (cudaMemcpyToSymbol(g_device_error, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+
+int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out, int64_t M, int64_t N, int64_t K,
+                       rola_stream_t stream) {
+  ROLA_CHECK(x && w && out, "qkv_gemm: null pointer");
+  ROLA_CHECK(M > 0 && M < (1ll << 31), "qkv_gemm: M out of range");
+  ROLA_CHECK(N > 0 && N % 256 == 0 && N <= 65536, "qkv_gemm: N must be a positive multiple of 256");
+  ROLA_CHECK(K > 0 && K % 64 == 0 && K <= 65536, "qkv_gemm: K must be a positive multiple of 64");
+  ROLA_CHECK(aligned16(out), "qkv_gemm: out must be 16-byte aligned");
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)K * 2};
+    const uint32_t box[2] = {64, 128};
+    ROLA_TRY(make_map(&ta, x, 2, dims, strides, box, "qkv_gemm: x"));
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint64_t strides[1] = {(uint64_t)K * 2};
+    const uint32_t box[2] = {64, 256};
+    ROLA_TRY(make_map(&tb, w, 2, dims, strides, box, "qkv_gemm: w"));
+  }
+  return cuda_status(launch_gemm_bf16(ta, tb, BF(bias), BFm(out), N, (int)M, (int)N, (int)K, S(stream)),
+                     "qkv_gemm");
+}
+
+int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw, const void* x, const void* norm_wq,
+                           const void* norm_wk, const float* cos_sin, const void* gate_w, const void* gate_b, int B,
+                           int L, int H, int blk, float eps, void* q_rope, void* k_rope, void* q_normed,
+                           void* k_normed, void* gate_out, void* pooled_q, float* ksum, rola_stream_t stream) {
+  ROLA_CHECK(q_raw && k_raw && cos_sin, "qk_norm_rope: null input");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 48 && blk > 0, "qk_norm_rope: bad sizes (H <= 48)");
+  ROLA_CHECK((norm_wq == nullptr) == (norm_wk == nullptr), "qk_norm_rope: give both norm weights or neither");
+  ROLA_CHECK(ld_raw % 8 == 0 && aligned16(q_raw) && aligned16(k_raw), "qk_norm_rope: 16-byte aligned rows required");
+  ROLA_CHECK((pooled_q == nullptr) == (ksum == nullptr), "qk_norm_rope: pooled_q and ksum go together");
+  ROLA_CHECK(x == nullptr || (gate_w && gate_b && gate_out), "qk_norm_rope: the gate needs gate_w, gate_b, gate_out");
+  NormRopeParams p{};
+  p.q_in = BF(q_raw);
+  p.k_in = BF(k_raw);
+  p.ld_in = ld_raw;
+  p.x = BF(x);
+  p.ld_x = (int64_t)H * 128;
+  p.norm_wq = BF(norm_wq);
+  p.norm_wk = BF(norm_wk);
+  p.cos_sin = cos_sin;
+  p.gate_w = BF(gate_w);
+  p.gate_b = BF(gate_b);
+  p.q_rope = BFm(q_rope);
+  p.k_rope = BFm(k_rope);
+  p.q_normed = BFm(q_normed);
+  p.k_normed = BFm(k_normed);
+  p.gate_out = x ? BFm(gate_out) : nullptr;
+  p.pooled_q = BFm(pooled_q);
+  p.ksum = ksum;
+  p.B = B;
+  p.L = L;
+  p.H = H;
+  p.blk = blk;
+  p.NB = (L + blk - 1) / blk;
+  p.heads_per_chunk = H;
+  p.chunk_stride = 0;
+  p.eps = eps;
+  const bool norm = norm_wq != nullptr;
+  const bool pool = pooled_q != nullptr;
+  if (!norm && !pool) {
+    // rope only
+    return cuda_status(launch_norm_rope_pool(p, false, true, false, S(stream)), "qk_norm_rope");
+  }
+  return cuda_status(launch_norm_rope_pool(p, norm, true, pool, S(stream)), "qk_norm_rope");
+}
+
+int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_raw, int64_t ld_raw, const void* x,
+                           const void* norm_wq, const void* norm_wk, const void* gate_w, const void* gate_b, int B,
+                           int L, int H, int heads_per_chunk, float eps, void* q_send, void* k_send, void* v_send,
+                           void* gate_out, rola_stream_t stream) {
+  ROLA_CHECK(q_raw && k_raw && v_raw && norm_wq && norm_wk && q_send && k_send && v_send,
+             "qk_norm_pack: null pointer");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 48 && heads_per_chunk > 0 && H % heads_per_chunk == 0,
+             "qk_norm_pack: bad sizes");
+  ROLA_CHECK(ld_raw % 8 == 0, "qk_norm_pack: 16-byte aligned rows required");
+  ROLA_CHECK(x == nullptr || (gate_w && gate_b && gate_out), "qk_norm_pack: the gate needs gate_w, gate_b, gate_out");
+  NormRopeParams p{};
+  p.q_in = BF(q_raw);
+  p.k_in = BF(k_raw);
+  p.v_in = BF(v_raw);
+  p.ld_in = ld_raw;
+  p.x = BF(x);
+  p.ld_x = (int64_t)H * 128;
+  p.norm_wq = BF(norm_wq);
+  p.norm_wk = BF(norm_wk);
+  p.gate_w = BF(gate_w);
+  p.gate_b = BF(gate_b);
+  p.q_normed = BFm(q_send);
+  p.k_normed = BFm(k_send);
+  p.v_out = BFm(v_send);
+  p.gate_out = x ? BFm(gate_out) : nullptr;
+  p.B = B;
+  p.L = L;
+  p.H = H;
+  p.blk = 128;
+  p.NB = (L + 127) / 128;
+  p.heads_per_chunk = heads_per_chunk;
+  p.chunk_stride = (int64_t)B * L * heads_per_chunk * 128;
+  p.eps = eps;
+  return cuda_status(launch_norm_rope_pool(p, true, false, false, S(stream)), "qk_norm_pack");
+}
+
+int rola_b200_rope_pool(const void* q_normed, const void* k_normed, int64_t ld, const float* cos_sin, int B, int L,
+                        int H, int blk, void* q_rope, void* k_rope, void* pooled_q, float* ksum,
+                        rola_stream_t stream) {
+  ROLA_CHECK(q_normed && k_normed && cos_sin && q_rope && k_rope, "rope_pool: null pointer");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 48 && blk > 0, "rope_pool: bad sizes");
+  ROLA_CHECK((pooled_q == nullptr) == (ksum == nullptr), "rope_pool: pooled_q and ksum go together");
+  ROLA_CHECK(ld % 8 == 0, "rope_pool: 16-byte aligned rows required");
+  NormRopeParams p{};
+  p.q_in = BF(q_normed);
+  p.k_in = BF(k_normed);
+  p.ld_in = ld;
+  p.cos_sin = cos_sin;
+  p.q_rope = BFm(q_rope);
+  p.k_rope = BFm(k_rope);
+  p.pooled_q = BFm(pooled_q);
+  p.ksum = ksum;
+  p.B = B;
+  p.L = L;
+  p.H = H;
+  p.blk = blk;
+  p.NB = (L + blk - 1) / blk;
+  p.heads_per_chunk = H;
+  return cuda_status(launch_norm_rope_pool(p, false, true, pooled_q != nullptr, S(stream)), "rope_pool");
+}
+
+int rola_b200_mean_pool(const void* x, int64_t sB, int64_t sH, int64_t sT, int B, int H, int L, int blk,
+                        const void* center, void* out, rola_stream_t stream) {
+  ROLA_CHECK(x && out, "mean_pool: null pointer");
+  ROLA_CHECK(B > 0 && H > 0 && L > 0 && blk > 0, "mean_pool: bad sizes");
+  ROLA_CHECK(aligned16(x) && sB % 8 == 0 && sH % 8 == 0 && sT % 8 == 0, "mean_pool: 16-byte aligned rows required");
+  return cuda_status(launch_block_pool(BF(x), sB, sH, sT, B, H, L, blk, BF(center), BFm(out), nullptr, S(stream)),
+                     "mean_pool");
+}
+
+int rola_b200_smooth_k_center(const void* k, int64_t sB, int64_t sH, int64_t sT, int B, int H, int L, int blk,
+                              float* ksum_ws, void* center, rola_stream_t stream) {
+  ROLA_CHECK(k && ksum_ws && center, "smooth_k_center: null pointer");
+  ROLA_CHECK(B > 0 && H > 0 && L > 0 && blk > 0, "smooth_k_center: bad sizes");
+  ROLA_CHECK(aligned16(k) && sB % 8 == 0 && sH % 8 == 0 && sT % 8 == 0,
+             "smooth_k_center: 16-byte aligned rows required");
+  ROLA_TRY(cuda_status(launch_block_pool(BF(k), sB, sH, sT, B, H, L, blk, nullptr, nullptr, ksum_ws, S(stream)),
+                       "smooth_k_center"));
+  const int NB = (L + blk - 1) / blk;
+  return cuda_status(launch_center(ksum_ws, B, NB, H * 128, L, BFm(center), S(stream)), "smooth_k_center");
+}
+
+int rola_b200_center_from_sums(const float* ksum, int B, int NB, int dim, int L, void* center,
+                               rola_stream_t stream) {
+  ROLA_CHECK(ksum && center, "center_from_sums: null pointer");
+  ROLA_CHECK(B > 0 && NB > 0 && dim > 0 && L > 0, "center_from_sums: bad sizes");
+  return cuda_status(launch_center(ksum, B, NB, dim, L, BFm(center), S(stream)), "center_from_sums");
+}
+
+int rola_b200_block_select(const void* pooled_q, const void* pooled_k, int BH, int NBq, int NBk, int topk,
+                           float* scores_ws, int32_t* lut, rola_stream_t stream) {
+  ROLA_CHECK(pooled_q && pooled_k && scores_ws && lut, "block_select: null pointer");
+  ROLA_CHECK(BH > 0 && NBq > 0 && NBk > 0 && NBk <= 2048, "block_select: bad sizes (NBk <= 2048)");
+  ROLA_CHECK(topk >= 1 && topk <= NBk, "block_select: topk must be in [1, NBk]");
+  ROLA_TRY(cuda_status(launch_scores(BF(pooled_q), BF(pooled_k), BH, NBq, NBk, scores_ws, S(stream)),
+                       "block_select/scores"));
+  return cuda_status(launch_topk(scores_ws, BH * NBq, NBk, topk, lut, S(stream)), "block_select/topk");
+}
+
+int rola_b200_lowrank_q(const void* q_normed, int64_t sB, int64_t sH, int64_t sT, const void* proj_q,
+                        const void* lr_cos, const void* lr_sin, int rope_dim, int B, int L, int H, int R, void* q_lr,
+                        rola_stream_t stream) {
+  ROLA_CHECK(q_normed && proj_q && q_lr, "lowrank_q: null pointer");
+  ROLA_CHECK(R == 64, "lowrank_q: rank must be 64");
+  ROLA_CHECK(rope_dim >= 0 && rope_dim <= R / 2 && (rope_dim == 0 || (lr_cos && lr_sin)), "lowrank_q: bad rope_dim");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0, "lowrank_q: bad sizes");
+  ROLA_CHECK(aligned16(q_normed) && sB % 8 == 0 && sH % 8 == 0 && sT % 8 == 0, "lowrank_q: 16-byte aligned rows required");
+  LowrankParams p{};
+  p.x = BF(q_normed);
+  p.x_sB = sB;
+  p.x_sH = sH;
+  p.x_sT = sT;
+  p.proj = BF(proj_q);
+  p.cos = BF(lr_cos);
+  p.sin = BF(lr_sin);
+  p.lr_out = BFm(q_lr);
+  p.B = B;
+  p.L = L;
+  p.H = H;
+  p.R = R;
+  p.rope_dim = rope_dim;
+  return cuda_status(launch_lowrank_q(p, S(stream)), "lowrank_q");
+}
+
+int rola_b200_lowrank_kv(const void* k_normed, int64_t k_sB, int64_t k_sH, int64_t k_sT, const void* v, int64_t v_sB,
+                         int64_t v_sH, int64_t v_sT, const void* proj_k, const void* lr_cos, const void* lr_sin,
+                         int rope_dim, int B, int L, int H, int R, int splits, float* c_partial_ws, void* C, void* Ct,
+                         rola_stream_t stream) {
+  ROLA_CHECK(k_normed && v && proj_k && c_partial_ws && (C || Ct), "lowrank_kv: null pointer");
+  ROLA_CHECK(R == 64, "lowrank_kv: rank must be 64");
+  ROLA_CHECK(rope_dim >= 0 && rope_dim <= R / 2 && (rope_dim == 0 || (lr_cos && lr_sin)), "lowrank_kv: bad rope_dim");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && splits > 0 && splits <= 4096, "lowrank_kv: bad sizes");
+  ROLA_CHECK(aligned16(k_normed) && aligned16(v) && k_sB % 8 == 0 && k_sH % 8 == 0 && k_sT % 8 == 0 &&
+                 v_sB % 8 == 0 && v_sH % 8 == 0 && v_sT % 8 == 0,
+             "lowrank_kv: 16-byte aligned rows required");
+  LowrankParams p{};
+  p.x = BF(k_normed);
+  p.x_sB = k_sB;
+  p.x_sH = k_sH;
+  p.x_sT = k_sT;
+  p.v = BF(v);
+  p.v_sB = v_sB;
+  p.v_sH = v_sH;
+  p.v_sT = v_sT;
+  p.proj = BF(proj_k);
+  p.cos = BF(lr_cos);
+  p.sin = BF(lr_sin);
+  p.c_partial = c_partial_ws;
+  p.B = B;
+  p.L = L;
+  p.H = H;
+  p.R = R;
+  p.rope_dim = rope_dim;
+  p.splits = splits;
+  ROLA_TRY(cuda_status(launch_lowrank_kv(p, S(stream)), "lowrank_kv"));
+  return cuda_status(launch_lowrank_reduce(c_partial_ws, splits, B * H, R, BFm(C), BFm(Ct), S(stream)),
+                     "lowrank_kv/reduce");
+}
+
+// head-view 4-D map: dims (d = 128, t = L, h = H, b = B) with element strides (1, sT, sH, sB)
+static int make_head_map(CUtensorMap* m, const void* ptr, int cols, int64_t sB, int64_t sH, int64_t sT, int L, int H,
+                         int B, const char* what) {
+  const uint64_t dims[4] = {(uint64_t)cols, (uint64_t)L, (uint64_t)H, (uint64_t)B};
+  const uint64_t strides[3] = {(uint64_t)sT * 2, (uint64_t)sH * 2, (uint64_t)sB * 2};
+  const uint32_t box[4] = {64, 128, 1, 1};
+  return make_map(m, ptr, 4, dims, strides, box, what);
+}
+
+int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT, const void* v,
+                          int64_t v_sB, int64_t v_sH, int64_t v_sT, const int32_t* lut, int B, int L, int H, int blk,
+                          int topk, const void* q_lr, const void* Ct, const void* gate, float eps_lr, void* out,
+                          void* o_sparse, int64_t o_sB, int64_t o_sH, int64_t o_sT, rola_stream_t stream) {
+  ROLA_CHECK(q && k && v && lut, "sparse_attn: null pointer");
+  ROLA_CHECK(out || o_sparse, "sparse_attn: no output requested");
+  ROLA_CHECK(blk == 128, "sparse_attn: block size must be 128");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && (int64_t)B * H < 65536, "sparse_attn: bad sizes");
+  const int NB = (L + blk - 1) / blk;
+  ROLA_CHECK(topk >= 1 && topk <= NB, "sparse_attn: topk must be in [1, NB]");
+  ROLA_CHECK((q_lr == nullptr) == (Ct == nullptr), "sparse_attn: q_lr and Ct go together");
+  ROLA_CHECK(o_sB % 8 == 0 && o_sH % 8 == 0 && o_sT % 8 == 0 && (out == nullptr || aligned16(out)) &&
+                 (o_sparse == nullptr || aligned16(o_sparse)),
+             "sparse_attn: 16-byte aligned output rows required");
+  CUtensorMap tq, tk, tv, tqlr, tct;
+  memset(&tqlr, 0, sizeof(tqlr));
+  memset(&tct, 0, sizeof(tct));
+  ROLA_TRY(make_head_map(&tq, q, 128, qk_sB, qk_sH, qk_sT, L, H, B, "sparse_attn: q"));
+  ROLA_TRY(make_head_map(&tk, k, 128, qk_sB, qk_sH, qk_sT, L, H, B, "sparse_attn: k"));
+  ROLA_TRY(make_head_map(&tv, v, 128, v_sB, v_sH, v_sT, L, H, B, "sparse_attn: v"));
+  if (q_lr) {
+    ROLA_TRY(make_head_map(&tqlr, q_lr, 64, (int64_t)L * H * 64, 64, (int64_t)H * 64, L, H, B, "sparse_attn: q_lr"));
+    const uint64_t dims[3] = {64, 128, (uint64_t)B * H};
+    const uint64_t strides[2] = {64 * 2, 64 * 128 * 2};
+    const uint32_t box[3] = {64, 128, 1};
+    ROLA_TRY(make_map(&tct, Ct, 3, dims, strides, box, "sparse_attn: Ct"));
+  }
+  AttnParams p{};
+  p.lut = lut;
+  p.gate = BF(gate);
+  p.out = BFm(out);
+  p.o_sB = o_sB;
+  p.o_sH = o_sH;
+  p.o_sT = o_sT;
+  p.o_sparse = BFm(o_sparse);
+  p.B = B;
+  p.L = L;
+  p.H = H;
+  p.NBq = NB;
+  p.NBk = NB;
+  p.topk = topk;
+  p.has_lowrank = q_lr != nullptr;
+  p.qk_scale = (float)(0.08838834764831845 * 1.4426950408889634);  // 128^-0.5 * log2(e)
+  p.eps_lr = eps_lr;
+  p.rescale_threshold = 0.0f;
+  return cuda_status(launch_sparse_attn(tq, tk, tv, tqlr, tct, p, S(stream)), "sparse_attn");
+}
+
+// ---------------------------------------------------------------------------
+// whole layer
+// ---------------------------------------------------------------------------
+struct FwdLayout {
+  size_t qkv, q_rope, k_rope, q_normed, k_normed, gate, pooled_q, pooled_k, ksum, center, scores, lut, q_lr,
+      c_partial, ct, total;
+};
+
+static FwdLayout fwd_layout(int B, int L, int H, int blk, int R, int splits, int topk) {
+  const size_t BL = (size_t)B * L, dim = (size_t)H * 128, NB = (size_t)(L + blk - 1) / blk;
+  FwdLayout f{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  f.qkv = take(BL * 3 * dim * 2);
+  f.q_rope = take(BL * dim * 2);
+  f.k_rope = take(BL * dim * 2);
+  f.q_normed = take(BL * dim * 2);
+  f.k_normed = take(BL * dim * 2);
+  f.gate = take(BL * H * 2);
+  f.pooled_q = take((size_t)B * H * NB * 128 * 2);
+  f.pooled_k = take((size_t)B * H * NB * 128 * 2);
+  f.ksum = take((size_t)B * NB * dim * 4);
+  f.center = take((size_t)B * dim * 2);
+  f.scores = take((size_t)B * H * NB * NB * 4);
+  f.lut = take((size_t)B * H * NB * (size_t)topk * 4);
+  f.q_lr = take(BL * H * R * 2);
+  f.c_partial = take((size_t)splits * B * H * R * 128 * 4);
+  f.ct = take((size_t)B * H * 128 * R * 2);
+  f.total = off;
+  return f;
+}
+
+size_t rola_b200_forward_workspace_bytes(int B, int L, int H, int blk, int R, int splits) {
+  if (B <= 0 || L <= 0 || H <= 0 || blk <= 0 || R <= 0 || splits <= 0) return 0;
+  const int NB = (L + blk - 1) / blk;
+  return fwd_layout(B, L, H, blk, R, splits, NB).total;  // sized for the largest topk
+}
+
+int rola_b200_rola_forward(const void* x, const void* w_qkv, const void* b_qkv, const void* norm_wq,
+                           const void* norm_wk, const float* cos_sin, const void* lr_cos, const void* lr_sin,
+                           int rope_dim, const void* proj_q, const void* proj_k, const void* gate_w,
+                           const void* gate_b, int B, int L, int H, int blk, int topk, int R, int splits, float eps,
+                           void* workspace, size_t workspace_bytes, void* out, int32_t* lut_out,
+                           rola_stream_t stream) {
+  ROLA_CHECK(x && w_qkv && norm_wq && norm_wk && cos_sin && proj_q && proj_k && gate_w && gate_b && workspace && out,
+             "rola_forward: null pointer");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 48 && blk == 128 && R == 64 && splits > 0, "rola_forward: bad sizes");
+  const int NB = (L + blk - 1) / blk;
+  ROLA_CHECK(topk >= 1 && topk <= NB, "rola_forward: topk must be in [1, NB]");
+  const FwdLayout f = fwd_layout(B, L, H, blk, R, splits, NB);
+  ROLA_CHECK(workspace_bytes >= f.total, "rola_forward: workspace too small (%zu < %zu)", workspace_bytes, f.total);
+  ROLA_CHECK((reinterpret_cast<uintptr_t>(workspace) & 255u) == 0, "rola_forward: workspace must be 256-byte aligned");
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  const int64_t dim = (int64_t)H * 128;
+  const int64_t M = (int64_t)B * L;
+  __nv_bfloat16* qkv = reinterpret_cast<__nv_bfloat16*>(ws + f.qkv);
+  int32_t* lut = lut_out ? lut_out : reinterpret_cast<int32_t*>(ws + f.lut);
+  ROLA_TRY(rola_b200_qkv_gemm(x, w_qkv, b_qkv, qkv, M, 3 * dim, dim, stream));
+  ROLA_TRY(rola_b200_qk_norm_rope(qkv, qkv + dim, 3 * dim, x, norm_wq, norm_wk, cos_sin, gate_w, gate_b, B, L, H,
+                                  blk, eps, ws + f.q_rope, ws + f.k_rope, ws + f.q_normed, ws + f.k_normed,
+                                  ws + f.gate, ws + f.pooled_q, reinterpret_cast<float*>(ws + f.ksum), stream));
+  ROLA_TRY(rola_b200_center_from_sums(reinterpret_cast<float*>(ws + f.ksum), B, NB, (int)dim, L, ws + f.center,
+                                      stream));
+  ROLA_TRY(rola_b200_mean_pool(ws + f.k_rope, (int64_t)L * dim, 128, dim, B, H, L, blk, ws + f.center,
+                               ws + f.pooled_k, stream));
+  ROLA_TRY(rola_b200_block_select(ws + f.pooled_q, ws + f.pooled_k, B * H, NB, NB, topk,
+                                  reinterpret_cast<float*>(ws + f.scores), lut, stream));
+  const int64_t Ld = (int64_t)L * dim;
+  ROLA_TRY(rola_b200_lowrank_kv(ws + f.k_normed, Ld, 128, dim, qkv + 2 * dim, 3 * Ld, 128, 3 * dim, proj_k, lr_cos,
+                                lr_sin, rope_dim, B, L, H, R, splits, reinterpret_cast<float*>(ws + f.c_partial),
+                                nullptr, ws + f.ct, stream));
+  ROLA_TRY(rola_b200_lowrank_q(ws + f.q_normed, Ld, 128, dim, proj_q, lr_cos, lr_sin, rope_dim, B, L, H, R,
+                               ws + f.q_lr, stream));
+  return rola_b200_sparse_attn(ws + f.q_rope, ws + f.k_rope, Ld, 128, dim, qkv + 2 * dim, 3 * Ld, 128, 3 * dim, lut,
+                               B, L, H, blk, topk, ws + f.q_lr, ws + f.ct, ws + f.gate, 0.0078125f, out, nullptr, Ld,
+                               128, dim, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,94 @@
+// Internal kernel launchers of the RoLa B200 library (not part of the C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rola {
+
+// prologue.cu
+struct NormRopeParams {
+  const __nv_bfloat16* q_in;
+  const __nv_bfloat16* k_in;
+  const __nv_bfloat16* v_in;  // only read when v_out != nullptr
+  int64_t ld_in;              // row stride (elements) of q_in/k_in/v_in
+  const __nv_bfloat16* x;     // gate input [B*L, dim] (row stride ld_x) or nullptr
+  int64_t ld_x;
+  const __nv_bfloat16* norm_wq;  // [dim] or nullptr (no norm)
+  const __nv_bfloat16* norm_wk;
+  const float* cos_sin;          // [L, D] interleaved fp32, row t = token position t
+  const __nv_bfloat16* gate_w;   // [D]
+  const __nv_bfloat16* gate_b;   // [H] (already in the data dtype)
+  // outputs (any may be nullptr)
+  __nv_bfloat16* q_rope;  // [B*L, dim]
+  __nv_bfloat16* k_rope;
+  __nv_bfloat16* q_normed;  // chunked layout, see out_offset()
+  __nv_bfloat16* k_normed;
+  __nv_bfloat16* v_out;
+  __nv_bfloat16* gate_out;  // [B*L, H]
+  __nv_bfloat16* pooled_q;  // [B, H, NB, D]
+  float* ksum;              // [B, NB, dim]
+  int B, L, H, blk, NB;
+  int heads_per_chunk;     // chunked output layout for the all-to-all send buffers
+  int64_t chunk_stride;    // elements between chunks
+  float eps;
+};
+int launch_norm_rope_pool(const NormRopeParams& p, bool norm, bool rope, bool pool, cudaStream_t s);
+
+// select.cu ---------------------------------------------------------------
+// Generic strided block pooling: element (b, h, t, d) of x sits at
+// x + b*sB + h*sH + t*sT + d.  mode 0: out_bf16[b,h,m,:] = bf16(sum/nx) (with
+// optional centre [B,H,D] subtracted and rounded per row); mode 1:
+// out_f32[b,m,h*D+d] = fp32 block sums (no centre).
+int launch_block_pool(const __nv_bfloat16* x, int64_t sB, int64_t sH, int64_t sT, int B, int H, int L, int blk,
+                      const __nv_bfloat16* center, __nv_bfloat16* out_bf16, float* out_f32, cudaStream_t s);
+// centre[b, c] = bf16(sum_m ksum[b, m, c] / L) (sequential over m)
+int launch_center(const float* ksum, int B, int NB, int dim, int L, __nv_bfloat16* center, cudaStream_t s);
+// scores[bh, m, j] = sum_d pq[bh, m, d] * pk[bh, j, d] (sequential fp32 FMA over d)
+int launch_scores(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH, int NBq, int NBk, float* scores,
+                  cudaStream_t s);
+// lut[bh, m, :] = top-k of scores[bh, m, :] (ties -> lower index), ascending int32
+int launch_topk(const float* scores, int rows, int NBk, int k, int32_t* lut, cudaStream_t s);
+
+// lowrank.cu --------------------------------------------------------------
+struct LowrankParams {
+  const __nv_bfloat16* x;  // q_normed or k_normed: element (b,h,t,d) at x + b*x_sB + h*x_sH + t*x_sT + d
+  int64_t x_sB, x_sH, x_sT;
+  const __nv_bfloat16* proj;  // [R, D]
+  const __nv_bfloat16* cos;   // [L, rope_dim]
+  const __nv_bfloat16* sin;
+  const __nv_bfloat16* v;     // element (b,h,t,d) at v + b*v_sB + h*v_sH + t*v_sT + d
+  int64_t v_sB, v_sH, v_sT;
+  __nv_bfloat16* lr_out;      // q_lr: element (b,t,h,r) at lr_out + (b*L+t)*H*R + h*R + r
+  float* c_partial;           // [splits, B*H, R, D]
+  int B, L, H, R, rope_dim, splits;
+};
+int launch_lowrank_q(const LowrankParams& p, cudaStream_t s);
+int launch_lowrank_kv(const LowrankParams& p, cudaStream_t s);
+// C[bh, r, d] and Ct[bh, d, r] (bf16) from the fp32 partials (sequential over splits)
+int launch_lowrank_reduce(const float* c_partial, int splits, int BH, int R, __nv_bfloat16* C, __nv_bfloat16* Ct,
+                          cudaStream_t s);
+
+// gemm.cu -----------------------------------------------------------------
+// out[M, N] (row stride ldo) = A[M, K] * W[N, K]^T (+ bias[N]), bf16 in/out, fp32 accumulate
+int launch_gemm_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const __nv_bfloat16* bias, __nv_bfloat16* out,
+                     int64_t ldo, int M, int N, int K, cudaStream_t s);
+
+// attn.cu -----------------------------------------------------------------
+struct AttnParams {
+  const int32_t* lut;  // [B*H, NBq, topk]
+  const __nv_bfloat16* gate;  // [B*L, H] or nullptr
+  __nv_bfloat16* out;         // fused output, element (b,h,t,d) at out + b*o_sB + h*o_sH + t*o_sT + d (nullptr: skip)
+  int64_t o_sB, o_sH, o_sT;
+  __nv_bfloat16* o_sparse;    // optional, same layout as out
+  int B, L, H, NBq, NBk, topk, has_lowrank;
+  float qk_scale;  // D^-1/2 * log2(e)
+  float eps_lr;    // finfo(dtype).eps
+  float rescale_threshold;  // log2 growth of the running max that triggers an O rescale (0 = always)
+};
+int launch_sparse_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tqlr,
+                       const CUtensorMap& tct, const AttnParams& p, cudaStream_t s);
+
+}  // namespace rola

@@ -1,0 +1,252 @@
+// Low-rank correction branch: lr = RoPE_rank(bf16(SiLU(bf16(x . P^T)))) for the
+// pre-RoPE normed q and k, and C = bf16(k_lr^T . v) per (batch, head).
+//
+// Restates `_proj_silu_rope_kernel` (sparkdiffusion/ops/fused_kernel/
+// fused_lowrank.py:31-152, HAS_NORM=False as called from
+// networks/wan_rola_attention.py:432-439) and the cuBLAS `C = k_lr^T v`
+// (fused_lowrank.py:355-358).  The product o_lr = q_lr . C is done inside the
+// attention epilogue (attn.cu).
+//
+// These contractions are small (K = 128 or the 128-token block, N = rank), so
+// they use warp-level mma.sync m16n8k16 with ldmatrix fragments.  C is summed
+// over the sequence in `splits` fp32 partials (one per CTA column) that a
+// second kernel adds in a fixed order, so C is deterministic.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rola {
+
+constexpr int kLrT = 128;       // tokens per tile
+constexpr int kPadX = 128 + 8;  // padded row (elements) of 128-wide tiles
+constexpr int kPadR = 64 + 8;   // padded row of the rank tile
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// copy a [128 tokens x 128] bf16 tile of head h into padded smem, zeroing rows >= L;
+// element (b,h,t,d) of src sits at src + b*sB + h*sH + t*sT + d
+__device__ __forceinline__ void load_tile(__nv_bfloat16* dst, const __nv_bfloat16* src, int64_t sB, int64_t sH,
+                                          int64_t sT, int b, int t0, int L, int h) {
+  const __nv_bfloat16* base = src + (int64_t)b * sB + (int64_t)h * sH;
+  for (int i = threadIdx.x; i < kLrT * 16; i += blockDim.x) {
+    const int r = i >> 4, c = (i & 15) * 8;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (t0 + r < L) u = *reinterpret_cast<const uint4*>(base + (int64_t)(t0 + r) * sT + c);
+    *reinterpret_cast<uint4*>(dst + r * kPadX + c) = u;
+  }
+}
+
+// Projection of 32 tokens (warp w: tokens 32w..32w+31 of the tile) onto rank 64:
+// acc[mt][nt][4] in the m16n8 accumulator layout.
+__device__ __forceinline__ void project_warp(const __nv_bfloat16* sX, const __nv_bfloat16* sP, float (&acc)[2][8][4]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[mt][nt][e] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    uint32_t a[2][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      const int mi = lane >> 3;
+      const int row = warp * 32 + mt * 16 + (lane & 7) + (mi & 1) * 8;
+      const int col = ks * 16 + (mi >> 1) * 8;
+      ldsm_x4(smem_u32(sX + row * kPadX + col), a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
+    }
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {  // pairs of n-tiles
+      const int mi = lane >> 3;
+      const int n = np * 16 + (lane & 7) + (mi >> 1) * 8;
+      const int k = ks * 16 + (mi & 1) * 8;
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(smem_u32(sP + n * kPadX + k), b0, b1, b2, b3);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        mma16816(acc[mt][2 * np], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b0, b1);
+        mma16816(acc[mt][2 * np + 1], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b2, b3);
+      }
+    }
+  }
+}
+
+// SiLU + rank-RoPE on one (even, odd) rank pair of token t; returns packed bf16x2
+__device__ __forceinline__ uint32_t silu_rope_pair(float l0, float l1, int t, int pair, const LowrankParams& p) {
+  float e = rbf(l0), o = rbf(l1);                      // bf16 linear output (fused_lowrank.py:97)
+  e = rbf(e * (1.0f / (1.0f + expf(-e))));             // silu in fp32, then bf16 (:99-102)
+  o = rbf(o * (1.0f / (1.0f + expf(-o))));
+  if (pair < p.rope_dim) {                             // rotated pairs (:104-135)
+    const float c = bf2f(p.cos[(int64_t)t * p.rope_dim + pair]);
+    const float s = bf2f(p.sin[(int64_t)t * p.rope_dim + pair]);
+    const float ec = rbf(e * c), os = rbf(o * s), es = rbf(e * s), oc = rbf(o * c);
+    return pack_bf2(ec - os, es + oc);
+  }
+  return pack_bf2(e, o);
+}
+
+// q_lr = RoPE_rank(SiLU(q_normed . P^T)) -> [B*L, H, R]
+__global__ void __launch_bounds__(128) lowrank_q_kernel(LowrankParams p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __nv_bfloat16* sX = reinterpret_cast<__nv_bfloat16*>(smem_raw);
+  __nv_bfloat16* sP = sX + kLrT * kPadX;
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int t0 = blockIdx.x * kLrT;
+  for (int i = threadIdx.x; i < 64 * 16; i += blockDim.x) {
+    const int r = i >> 4, c = (i & 15) * 8;
+    *reinterpret_cast<uint4*>(sP + r * kPadX + c) = *reinterpret_cast<const uint4*>(p.proj + r * 128 + c);
+  }
+  load_tile(sX, p.x, p.x_sB, p.x_sH, p.x_sT, b, t0, p.L, h);
+  __syncthreads();
+  float acc[2][8][4];
+  project_warp(sX, sP, acc);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, tig = lane & 3;
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int t = t0 + warp * 32 + mt * 16 + g + half * 8;
+      if (t >= p.L) continue;
+      __nv_bfloat16* dst = p.lr_out + ((int64_t)b * p.L + t) * p.H * 64 + h * 64;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int r = nt * 8 + tig * 2;
+        const uint32_t v = silu_rope_pair(acc[mt][nt][half * 2], acc[mt][nt][half * 2 + 1], t, r >> 1, p);
+        *reinterpret_cast<uint32_t*>(dst + r) = v;
+      }
+    }
+}
+
+// partial C = sum over this CTA's token tiles of k_lr^T v (fp32)
+__global__ void __launch_bounds__(128) lowrank_kv_kernel(LowrankParams p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __nv_bfloat16* sX = reinterpret_cast<__nv_bfloat16*>(smem_raw);
+  __nv_bfloat16* sV = sX + kLrT * kPadX;
+  __nv_bfloat16* sP = sV + kLrT * kPadX;
+  __nv_bfloat16* sK = sP + 64 * kPadX;  // k_lr [128 t][64 r] (padded)
+  const int split = blockIdx.x;
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, tig = lane & 3;
+  for (int i = threadIdx.x; i < 64 * 16; i += blockDim.x) {
+    const int r = i >> 4, c = (i & 15) * 8;
+    *reinterpret_cast<uint4*>(sP + r * kPadX + c) = *reinterpret_cast<const uint4*>(p.proj + r * 128 + c);
+  }
+  float cacc[16][4];
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) cacc[nt][e] = 0.f;
+
+  const int ntiles = (p.L + kLrT - 1) / kLrT;
+  for (int tile = split; tile < ntiles; tile += p.splits) {
+    const int t0 = tile * kLrT;
+    __syncthreads();  // previous tile fully consumed
+    load_tile(sX, p.x, p.x_sB, p.x_sH, p.x_sT, b, t0, p.L, h);
+    load_tile(sV, p.v, p.v_sB, p.v_sH, p.v_sT, b, t0, p.L, h);
+    __syncthreads();
+    float acc[2][8][4];
+    project_warp(sX, sP, acc);
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int tl = warp * 32 + mt * 16 + g + half * 8;
+        const int t = t0 + tl;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          const int r = nt * 8 + tig * 2;
+          uint32_t v = 0u;
+          if (t < p.L) v = silu_rope_pair(acc[mt][nt][half * 2], acc[mt][nt][half * 2 + 1], t, r >> 1, p);
+          *reinterpret_cast<uint32_t*>(sK + tl * kPadR + r) = v;
+        }
+      }
+    __syncthreads();
+    // C[r, d] += sum_t k_lr[t, r] v[t, d]; warp w owns r in [16w, 16w + 16)
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t a0, a1, a2, a3;
+      {
+        const int mi = lane >> 3;
+        const int t = ks * 16 + (lane & 7) + (mi >> 1) * 8;
+        const int r = warp * 16 + (mi & 1) * 8;
+        ldsm_x4_t(smem_u32(sK + t * kPadR + r), a0, a1, a2, a3);
+      }
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {
+        const int mi = lane >> 3;
+        const int t = ks * 16 + (lane & 7) + (mi & 1) * 8;
+        const int d = np * 16 + (mi >> 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(sV + t * kPadX + d), b0, b1, b2, b3);
+        mma16816(cacc[2 * np], a0, a1, a2, a3, b0, b1);
+        mma16816(cacc[2 * np + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+  }
+  float* dst = p.c_partial + (((int64_t)split * p.B * p.H + bh) * 64) * 128;
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    const int d = nt * 8 + tig * 2;
+    const int r0 = warp * 16 + g;
+    *reinterpret_cast<float2*>(dst + r0 * 128 + d) = make_float2(cacc[nt][0], cacc[nt][1]);
+    *reinterpret_cast<float2*>(dst + (r0 + 8) * 128 + d) = make_float2(cacc[nt][2], cacc[nt][3]);
+  }
+}
+
+__global__ void lowrank_reduce_kernel(const float* __restrict__ part, int splits, int BH, int R,
+                                      __nv_bfloat16* __restrict__ C, __nv_bfloat16* __restrict__ Ct) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t per = (int64_t)R * 128;
+  if (i >= (int64_t)BH * per) return;
+  const int64_t bh = i / per;
+  const int r = (int)((i % per) / 128), d = (int)(i % 128);
+  float acc = 0.f;
+  for (int s = 0; s < splits; ++s) acc += part[(int64_t)s * BH * per + i];
+  const __nv_bfloat16 v = f2bf(acc);
+  if (C) C[i] = v;
+  if (Ct) Ct[bh * per + (int64_t)d * R + r] = v;
+}
+
+int launch_lowrank_q(const LowrankParams& p, cudaStream_t s) {
+  const int smem = (kLrT * kPadX + 64 * kPadX) * 2;
+  cudaFuncSetAttribute(lowrank_q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  dim3 grid((p.L + kLrT - 1) / kLrT, p.B * p.H);
+  lowrank_q_kernel<<<grid, 128, smem, s>>>(p);
+  return (int)cudaGetLastError();
+}
+
+int launch_lowrank_kv(const LowrankParams& p, cudaStream_t s) {
+  const int smem = (2 * kLrT * kPadX + 64 * kPadX + kLrT * kPadR) * 2;
+  cudaFuncSetAttribute(lowrank_kv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  dim3 grid(p.splits, p.B * p.H);
+  lowrank_kv_kernel<<<grid, 128, smem, s>>>(p);
+  return (int)cudaGetLastError();
+}
+
+int launch_lowrank_reduce(const float* c_partial, int splits, int BH, int R, __nv_bfloat16* C, __nv_bfloat16* Ct,
+                          cudaStream_t s) {
+  const int64_t total = (int64_t)BH * R * 128;
+  lowrank_reduce_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(c_partial, splits, BH, R, C, Ct);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace rola

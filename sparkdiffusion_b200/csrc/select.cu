@@ -1,0 +1,239 @@
+// Block-mask selection: block mean pooling, smooth-K centre, pooled scores
+// and top-k.
+//
+// Restates `mean_pool`/`compress_kernel` (sparkdiffusion/ops/fused_kernel/
+// utils.py:19-82), the smooth-K centre `k.mean(dim=-2)` and the selection
+// `pooled_q @ pooled_k^T` + `torch.topk` (ops/fused_kernel/
+// fused_sparse_attn.py:179-198) with build-defined orders so that the LUT is
+// bit-exact against the CPU oracle:
+//   * block sums add rows sequentially (row 0 first), fp32;
+//   * the centre adds block sums sequentially over blocks, then divides by L;
+//   * a score is a chain of fp32 FMAs over d = 0..D-1 (bf16 products are exact);
+//   * top-k keeps the k largest scores, ties toward the lower block index, and
+//     writes the kept indices in ascending order as int32.
+// All of these kernels are HBM/L2 bound integer-and-fp32 work on CUDA cores.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rola {
+
+// ---------------------------------------------------------------------------
+// generic strided block pooling; one thread per (b, m, h, 8-column chunk)
+// ---------------------------------------------------------------------------
+__global__ void block_pool_kernel(const __nv_bfloat16* __restrict__ x, int64_t sB, int64_t sH, int64_t sT, int B,
+                                  int H, int L, int blk, int NB, const __nv_bfloat16* __restrict__ center,
+                                  __nv_bfloat16* __restrict__ out_bf16, float* __restrict__ out_f32) {
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)B * NB * H * 16;
+  if (gid >= total) return;
+  const int chunk = (int)(gid & 15);
+  int64_t r = gid >> 4;
+  const int h = (int)(r % H);
+  r /= H;
+  const int m = (int)(r % NB);
+  const int b = (int)(r / NB);
+  const int d0 = chunk * 8;
+  const int t0 = m * blk, t1 = min(L, t0 + blk);
+  float c[8];
+  if (center) {
+    const __nv_bfloat16* cp = center + ((int64_t)b * H + h) * 128 + d0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c[i] = bf2f(cp[i]);
+  }
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  const __nv_bfloat16* base = x + b * sB + h * sH + d0;
+  for (int t = t0; t < t1; ++t) {
+    uint4 u = *reinterpret_cast<const uint4*>(base + (int64_t)t * sT);
+    float v[8];
+    unpack_bf2(u.x, v[0], v[1]);
+    unpack_bf2(u.y, v[2], v[3]);
+    unpack_bf2(u.z, v[4], v[5]);
+    unpack_bf2(u.w, v[6], v[7]);
+    if (center) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = rbf(v[i] - c[i]);  // bf16(k - c), utils.py:261-265
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += v[i];
+  }
+  if (out_bf16) {
+    const float nx = (float)(t1 - t0);
+    uint4 u;
+    u.x = pack_bf2(__fdiv_rn(acc[0], nx), __fdiv_rn(acc[1], nx));
+    u.y = pack_bf2(__fdiv_rn(acc[2], nx), __fdiv_rn(acc[3], nx));
+    u.z = pack_bf2(__fdiv_rn(acc[4], nx), __fdiv_rn(acc[5], nx));
+    u.w = pack_bf2(__fdiv_rn(acc[6], nx), __fdiv_rn(acc[7], nx));
+    *reinterpret_cast<uint4*>(out_bf16 + (((int64_t)b * H + h) * NB + m) * 128 + d0) = u;
+  }
+  if (out_f32) {
+    float4* o = reinterpret_cast<float4*>(out_f32 + ((int64_t)b * NB + m) * H * 128 + h * 128 + d0);
+    o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  }
+}
+
+int launch_block_pool(const __nv_bfloat16* x, int64_t sB, int64_t sH, int64_t sT, int B, int H, int L, int blk,
+                      const __nv_bfloat16* center, __nv_bfloat16* out_bf16, float* out_f32, cudaStream_t s) {
+  const int NB = (L + blk - 1) / blk;
+  const int64_t total = (int64_t)B * NB * H * 16;
+  const int threads = 256;
+  const int64_t blocks = (total + threads - 1) / threads;
+  block_pool_kernel<<<(unsigned)blocks, threads, 0, s>>>(x, sB, sH, sT, B, H, L, blk, NB, center, out_bf16, out_f32);
+  return (int)cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// smooth-K centre from block sums
+// ---------------------------------------------------------------------------
+__global__ void center_kernel(const float* __restrict__ ksum, int B, int NB, int dim, int L,
+                              __nv_bfloat16* __restrict__ center) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.y;
+  if (c >= dim) return;
+  const float* src = ksum + (int64_t)b * NB * dim + c;
+  float acc = 0.f;
+  for (int m = 0; m < NB; ++m) acc += src[(int64_t)m * dim];
+  center[(int64_t)b * dim + c] = f2bf(__fdiv_rn(acc, (float)L));
+}
+
+int launch_center(const float* ksum, int B, int NB, int dim, int L, __nv_bfloat16* center, cudaStream_t s) {
+  dim3 grid((dim + 255) / 256, B);
+  center_kernel<<<grid, 256, 0, s>>>(ksum, B, NB, dim, L, center);
+  return (int)cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// pooled scores: 64x64 tile per CTA, 4x4 per thread, d-sequential FMA chains
+// ---------------------------------------------------------------------------
+constexpr int kSt = 64;
+__global__ void __launch_bounds__(256) scores_kernel(const __nv_bfloat16* __restrict__ pq,
+                                                     const __nv_bfloat16* __restrict__ pk, int NBq, int NBk,
+                                                     float* __restrict__ scores) {
+  extern __shared__ float scores_smem[];
+  float (*sq)[kSt] = reinterpret_cast<float (*)[kSt]>(scores_smem);               // transposed: [d][m]
+  float (*sk)[kSt] = reinterpret_cast<float (*)[kSt]>(scores_smem + 128 * kSt);  // [d][j]
+  const int bh = blockIdx.z;
+  const int m0 = blockIdx.x * kSt, j0 = blockIdx.y * kSt;
+  const __nv_bfloat16* qb = pq + (int64_t)bh * NBq * 128;
+  const __nv_bfloat16* kb = pk + (int64_t)bh * NBk * 128;
+  for (int i = threadIdx.x; i < kSt * 128; i += blockDim.x) {
+    const int r = i >> 7, d = i & 127;
+    sq[d][r] = (m0 + r < NBq) ? bf2f(qb[(int64_t)(m0 + r) * 128 + d]) : 0.f;
+    sk[d][r] = (j0 + r < NBk) ? bf2f(kb[(int64_t)(j0 + r) * 128 + d]) : 0.f;
+  }
+  __syncthreads();
+  const int tm = (threadIdx.x >> 4) * 4;  // 16 x 16 threads, 4 x 4 each
+  const int tj = (threadIdx.x & 15) * 4;
+  float acc[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc[a][c] = 0.f;
+#pragma unroll 4
+  for (int d = 0; d < 128; ++d) {
+    const float4 qv = *reinterpret_cast<const float4*>(&sq[d][tm]);
+    const float4 kv = *reinterpret_cast<const float4*>(&sk[d][tj]);
+    const float qa[4] = {qv.x, qv.y, qv.z, qv.w};
+    const float ka[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[a][c] = __fmaf_rn(qa[a], ka[c], acc[a][c]);
+  }
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int m = m0 + tm + a;
+    if (m >= NBq) continue;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int jj = j0 + tj + c;
+      if (jj < NBk) scores[((int64_t)bh * NBq + m) * NBk + jj] = acc[a][c];
+    }
+  }
+}
+
+int launch_scores(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH, int NBq, int NBk, float* scores,
+                  cudaStream_t s) {
+  dim3 grid((NBq + kSt - 1) / kSt, (NBk + kSt - 1) / kSt, BH);
+  const int smem = 2 * 128 * kSt * (int)sizeof(float);
+  cudaFuncSetAttribute(scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  scores_kernel<<<grid, 256, smem, s>>>(pq, pk, NBq, NBk, scores);
+  return (int)cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// top-k: one warp per row; k rounds of a warp arg-max over 64-bit keys
+// (orderable score << 32 | ~index), so ties go to the lower index.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t orderable(float f) {
+  if (f == 0.f) f = 0.f;  // -0 and +0 compare equal
+  uint32_t u = __float_as_uint(f);
+  if (f != f) return 0u;  // NaN ranks last
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+constexpr int kTopkMaxPerLane = 64;  // NBk <= 2048
+__global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ scores, int rows, int NBk, int k,
+                                                   int32_t* __restrict__ lut) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const float* src = scores + (int64_t)warp * NBk;
+  const int per = (NBk + 31) / 32;
+  uint32_t key[kTopkMaxPerLane];
+  uint64_t selected_lo = 0, selected_hi = 0;  // bit i: element lane + 32 i kept
+#pragma unroll
+  for (int i = 0; i < kTopkMaxPerLane; ++i) {
+    const int j = lane + 32 * i;
+    key[i] = (i < per && j < NBk) ? orderable(src[j]) : 0u;
+  }
+  for (int r = 0; r < k; ++r) {
+    // local best: highest key, then lowest index (lowest i for this lane)
+    uint64_t best = 0;
+#pragma unroll
+    for (int i = 0; i < kTopkMaxPerLane; ++i) {
+      if (i >= per) break;
+      const int j = lane + 32 * i;
+      const bool taken = (i < 64) ? ((i < 32 ? (selected_lo >> i) : (selected_hi >> (i - 32))) & 1ull) : false;
+      if (j < NBk && !taken) {
+        const uint64_t cand = ((uint64_t)key[i] << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)j);
+        best = cand > best ? cand : best;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    const uint32_t jbest = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu);
+    if ((int)(jbest & 31) == lane) {
+      const int i = (int)(jbest >> 5);
+      if (i < 32) selected_lo |= 1ull << i;
+      else selected_hi |= 1ull << (i - 32);
+    }
+  }
+  // emit kept indices in ascending order
+  int32_t* dst = lut + (int64_t)warp * k;
+  int written = 0;
+  for (int i = 0; i < per; ++i) {
+    const bool kept = (i < 32 ? (selected_lo >> i) : (selected_hi >> (i - 32))) & 1ull;
+    const uint32_t ballot = __ballot_sync(0xffffffffu, kept);
+    if (kept) {
+      const int pos = written + __popc(ballot & ((1u << lane) - 1u));
+      dst[pos] = lane + 32 * i;
+    }
+    written += __popc(ballot);
+  }
+}
+
+int launch_topk(const float* scores, int rows, int NBk, int k, int32_t* lut, cudaStream_t s) {
+  if (NBk > 32 * kTopkMaxPerLane || k > NBk || k < 1) return -1;
+  const int threads = 128;
+  const int64_t blocks = ((int64_t)rows * 32 + threads - 1) / threads;
+  topk_kernel<<<(unsigned)blocks, threads, 0, s>>>(scores, rows, NBk, k, lut);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace rola

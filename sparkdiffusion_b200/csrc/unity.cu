@@ -1,0 +1,9 @@
+// Single translation unit of librola_b200.so: the kernels share one device
+// error flag (defined in capi.cu), which needs them in one unit without
+// relocatable device code.
+#include "prologue.cu"
+#include "select.cu"
+#include "lowrank.cu"
+#include "gemm.cu"
+#include "attn.cu"
+#include "capi.cu"

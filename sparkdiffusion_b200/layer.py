@@ -1,0 +1,144 @@
+"""Drop-in RoLa self-attention layer backed by the B200 kernels.
+
+``WanSelfAttentionRoLaB200`` has the constructor signature, parameter names
+and shapes of the reference's ``WanSelfAttentionRoLa``
+(sparkdiffusion/networks/wan_rola_attention.py:209-287), so RoLa checkpoints
+load into it, and the forward contract of the sparse-attention plugin
+interface: ``forward(x [B, L, dim], seq_lens, freqs [L, D/2], rope_cache=None)
+-> [B, L, dim]`` (sparse_attn_registry.py:16-18, wan2pt1.py:468-472).  It is
+registered as ``"rola_b200"``.
+
+Inference only (the reference's fused path has the same gating,
+wan_rola_attention.py:467-477): the forward raises under autograd or on CPU
+tensors instead of falling back.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+from .registry import register_sparse_attn
+from .rope import prepare_cos_sin, prepare_lowrank_cos_sin
+
+
+class RMSNormWeight(nn.Module):
+    """Holds ``weight [dim]`` like ``WanRMSNorm`` (wan2pt1.py:188-206); the
+    normalisation itself runs inside the fused prologue kernel."""
+
+    def __init__(self, dim: int, eps: float = 1e-6):
+        super().__init__()
+        self.dim = dim
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def reset_parameters(self):
+        self.weight.data.fill_(1.0)
+
+
+@register_sparse_attn("rola_b200", sparse_param_names=["proj_q", "proj_k", "gate_proj", "gate_bias"])
+class WanSelfAttentionRoLaB200(nn.Module):
+    def __init__(self, dim: int, num_heads: int, qk_norm: bool = True, eps: float = 1e-6,
+                 rola_topk_ratio: float = 0.1, rola_rank: int = 64, rola_blkq: int = 128, rola_blkk: int = 128,
+                 attn_precision: str = "bf16"):
+        super().__init__()
+        assert dim % num_heads == 0
+        if attn_precision not in ("bf16", "int8"):
+            raise ValueError(f"attn_precision must be bf16/int8, got {attn_precision!r}")
+        self.dim = dim
+        self.num_heads = num_heads
+        self.head_dim = dim // num_heads
+        self.qk_norm = qk_norm
+        self.eps = eps
+        self.rola_topk_ratio = rola_topk_ratio
+        self.rola_rank = rola_rank
+        self.rola_blkq = rola_blkq
+        self.rola_blkk = rola_blkk
+        self.attn_precision = attn_precision
+        self.q = nn.Linear(dim, dim)
+        self.k = nn.Linear(dim, dim)
+        self.v = nn.Linear(dim, dim)
+        self.o = nn.Linear(dim, dim)
+        if qk_norm:
+            self.norm_q = RMSNormWeight(dim, eps=eps)
+            self.norm_k = RMSNormWeight(dim, eps=eps)
+        else:
+            self.norm_q = nn.Identity()
+            self.norm_k = nn.Identity()
+        h, r = self.head_dim, rola_rank
+        self.proj_q = nn.Linear(h, r, bias=False)
+        self.proj_k = nn.Linear(h, r, bias=False)
+        self.gate_proj = nn.Linear(h, 1, bias=False)
+        self.gate_bias = nn.Parameter(torch.full((1, num_heads, 1, 1), -1.946))
+        self.init_weights()
+        self._layer_name = "RoLaB200"
+        self._use_fused_inference = True
+        self._pg = None
+        self._qkv_cache = None
+
+    def init_weights(self):
+        """Re-apply the RoLa-specific init after WanModel's xavier pass
+        (wan_rola_attention.py:278-287)."""
+        nn.init.kaiming_uniform_(self.proj_q.weight, a=math.sqrt(5))
+        nn.init.kaiming_uniform_(self.proj_k.weight, a=math.sqrt(5))
+        nn.init.zeros_(self.gate_proj.weight)
+        self.gate_bias.data.fill_(-1.946)
+
+    def set_context_parallel_group(self, process_group, ranks, stream):
+        """Receives the sequence-parallel group (wan2pt1.py:942-960); with more
+        than one rank the forward runs the Ulysses sequence<->head exchange."""
+        del ranks, stream
+        self._pg = process_group
+
+    def _fused_qkv(self):
+        key = tuple((p.data_ptr(), p._version) for p in (self.q.weight, self.k.weight, self.v.weight,
+                                                         self.q.bias, self.k.bias, self.v.bias))
+        if self._qkv_cache is None or self._qkv_cache[0] != key:
+            w = torch.cat([self.q.weight, self.k.weight, self.v.weight], 0).to(torch.bfloat16).contiguous()
+            b = torch.cat([self.q.bias, self.k.bias, self.v.bias], 0).to(torch.bfloat16).contiguous()
+            self._qkv_cache = (key, w, b)
+        return self._qkv_cache[1], self._qkv_cache[2]
+
+    def attention_core(self, x: torch.Tensor, freqs: torch.Tensor, rope_cache=None) -> torch.Tensor:
+        """Everything of the forward except the output projection."""
+        if torch.is_grad_enabled() and self.training:
+            raise RuntimeError("WanSelfAttentionRoLaB200 is inference-only (no backward kernels)")
+        if not x.is_cuda:
+            raise RuntimeError("WanSelfAttentionRoLaB200 runs on CUDA tensors only")
+        if self.attn_precision != "bf16":
+            raise ValueError("the B200 path implements attn_precision='bf16'")
+        if self.rola_blkq != 128 or self.rola_blkk != 128:
+            raise ValueError("the B200 attention kernel supports rola_blkq == rola_blkk == 128")
+        B, L, dim = x.shape
+        if L < max(self.rola_blkq, self.rola_blkk):
+            raise ValueError("sequence shorter than one block")
+        x = x.to(torch.bfloat16).contiguous()
+        D = self.head_dim
+        if rope_cache is not None and rope_cache[0] is not None:
+            cos_sin = rope_cache[0]
+        else:
+            cos_sin = prepare_cos_sin(freqs, freqs.shape[0], D)
+        if rope_cache is not None and rope_cache[1] is not None:
+            lr_cos, lr_sin, rope_dim = rope_cache[1][0], rope_cache[1][1], rope_cache[1][2]
+        else:
+            lr_cos, lr_sin, rope_dim = prepare_lowrank_cos_sin(freqs, freqs.shape[0], self.rola_rank, torch.bfloat16)
+        w_qkv, b_qkv = self._fused_qkv()
+        nwq = self.norm_q.weight if self.qk_norm else None
+        nwk = self.norm_k.weight if self.qk_norm else None
+        if self._pg is not None and torch.distributed.get_world_size(self._pg) > 1:
+            from .ulysses import ulysses_rola_attention
+            return ulysses_rola_attention(self, x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, nwq, nwk)
+        NB = (L + 127) // 128
+        topk = ops.topk_count(self.rola_topk_ratio, NB)
+        return ops.rola_attention_core(x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, nwq, nwk,
+                                       self.proj_q.weight, self.proj_k.weight, self.gate_proj.weight,
+                                       self.gate_bias, self.num_heads, 128, topk, self.eps)
+
+    def forward(self, x: torch.Tensor, seq_lens: torch.Tensor, freqs: torch.Tensor, rope_cache=None) -> torch.Tensor:
+        del seq_lens
+        out = self.attention_core(x, freqs, rope_cache)
+        return F.linear(out.to(self.o.weight.dtype), self.o.weight, self.o.bias)

@@ -1,0 +1,323 @@
+"""Host-side ops of the B200 RoLa attention forward.
+
+Two layers of API:
+
+* ``rola_attention_core`` / ``rola_attention_from_qkv``: the fused B200 path
+  used by the drop-in layer.  Activations stay token-major ``[B, L, H*D]``
+  from the QKV GEMM to the gated output; the kernels gather per-head tiles
+  with TMA, so no layout transform is ever materialised.
+* reference-named functions mirroring ``sparkdiffusion.ops.fused_kernel``
+  (``fused_qkv_gemm_rope``, ``mean_pool``, ``fused_sparse_attn``) with the
+  reference's argument meaning, layouts and ``ValueError``s, so callers and
+  tests written against the reference read the same.
+
+Every function launches librola_b200 kernels on the current CUDA stream and
+raises if the library is missing or the tensors are not on a CUDA device:
+there is no CPU or PyTorch fallback.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .rope import prepare_cos_sin
+
+BF16 = torch.bfloat16
+HEAD_DIM = 128
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _require_cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("sparkdiffusion_b200 ops run on CUDA tensors only (no CPU fallback)")
+        if t.dtype not in (torch.bfloat16, torch.float32, torch.int32):
+            raise ValueError(f"unsupported dtype {t.dtype}")
+
+
+def _bf16_vec(t: torch.Tensor, n: int, name: str) -> torch.Tensor:
+    t = t.reshape(-1).to(BF16).contiguous()
+    if t.numel() != n:
+        raise ValueError(f"{name} must have {n} elements, got {t.numel()}")
+    return t
+
+
+def topk_count(topk_ratio: float, nb: int) -> int:
+    """k = max(1, min(NB, int(ratio*NB))) (fused_sparse_attn.py:197)."""
+    return max(1, min(nb, int(topk_ratio * nb)))
+
+
+def default_splits(B: int, H: int, L: int) -> int:
+    """Sequence splits of the low-rank C reduction: about two CTAs per SM."""
+    tiles = (L + 127) // 128
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return max(1, min(tiles, (2 * sms + B * H - 1) // (B * H)))
+
+
+# ---------------------------------------------------------------------------
+# fused B200 path
+# ---------------------------------------------------------------------------
+def qkv_gemm(x2d: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M, N] = x[M, K] w[N, K]^T (+ bias) on tcgen05 (bf16 in/out, fp32 accumulate)."""
+    _require_cuda(x2d, w, bias)
+    if x2d.dtype != BF16 or w.dtype != BF16:
+        raise ValueError("qkv_gemm: bf16 operands required")
+    x2d = x2d.contiguous()
+    w = w.contiguous()
+    M, K = x2d.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"qkv_gemm: weight {tuple(w.shape)} does not match x {tuple(x2d.shape)}")
+    out = torch.empty(M, N, device=x2d.device, dtype=BF16)
+    b = None if bias is None else bias.to(BF16).contiguous()
+    _lib.call("rola_b200_qkv_gemm", _ptr(x2d), _ptr(w), _ptr(b), _ptr(out), M, N, K, _stream())
+    return out
+
+
+def rola_attention_from_qkv(q_raw, k_raw, v_raw, x, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk,
+                            proj_q, proj_k, gate_w, gate_b, num_heads: int, blk: int = 128, topk: int = 1,
+                            eps: float = 1e-6, splits: int | None = None, keep: bool = False, lut=None):
+    """RoLa forward from projected q/k/v (token-major ``[B, L, H*D]`` views
+    with unit column stride; q and k share a row stride) to the gated output
+    ``[B, L, H*D]``.  ``keep`` returns the intermediates too.  ``lut`` (int32
+    ``[B*H, NB, k]``) replaces the kernel's own selection.
+    """
+    _require_cuda(q_raw, k_raw, v_raw, x)
+    B, L, dim = q_raw.shape
+    H = num_heads
+    if dim != H * HEAD_DIM:
+        raise ValueError(f"hidden size {dim} != num_heads*128")
+    if blk != 128:
+        raise ValueError("the B200 attention kernel supports block size 128")
+    for t in (q_raw, k_raw, v_raw):
+        if t.stride(2) != 1:
+            raise ValueError("q/k/v must have unit column stride")
+    if q_raw.stride() != k_raw.stride():
+        raise ValueError("q_raw and k_raw must share strides")
+    dev = q_raw.device
+    NB = (L + blk - 1) // blk
+    if not 1 <= topk <= NB:
+        raise ValueError(f"topk must be in [1, {NB}]")
+    R = proj_q.shape[0]
+    splits = splits or default_splits(B, H, L)
+    st = _stream()
+    e = lambda *s, dt=BF16: torch.empty(*s, device=dev, dtype=dt)  # noqa: E731
+    q_rope, k_rope = e(B, L, dim), e(B, L, dim)
+    q_normed, k_normed = e(B, L, dim), e(B, L, dim)
+    gate = e(B, L, H)
+    pooled_q, pooled_k = e(B, H, NB, HEAD_DIM), e(B, H, NB, HEAD_DIM)
+    ksum = e(B, NB, dim, dt=torch.float32)
+    center = e(B, H, HEAD_DIM)
+    scores = e(B * H, NB, NB, dt=torch.float32)
+    q_lr = e(B, L, H * R)
+    c_part = e(splits, B * H, R, HEAD_DIM, dt=torch.float32)
+    C = e(B * H, R, HEAD_DIM) if keep else None
+    Ct = e(B * H, HEAD_DIM, R)
+    out = e(B, L, dim)
+    o_sparse = e(B, L, dim) if keep else None
+    gw = _bf16_vec(gate_w, HEAD_DIM, "gate_w")
+    gb = _bf16_vec(gate_b, H, "gate_b")
+    nwq = None if norm_wq is None else _bf16_vec(norm_wq, dim, "norm_wq")
+    nwk = None if norm_wk is None else _bf16_vec(norm_wk, dim, "norm_wk")
+    cos_sin = cos_sin.to(torch.float32).contiguous()
+    ld_qk = q_raw.stride(1)
+    _lib.call("rola_b200_qk_norm_rope", _ptr(q_raw), _ptr(k_raw), ld_qk, _ptr(x.contiguous()), _ptr(nwq),
+              _ptr(nwk), _ptr(cos_sin), _ptr(gw), _ptr(gb), B, L, H, blk, eps, _ptr(q_rope), _ptr(k_rope),
+              _ptr(q_normed), _ptr(k_normed), _ptr(gate), _ptr(pooled_q), _ptr(ksum), st)
+    _lib.call("rola_b200_center_from_sums", _ptr(ksum), B, NB, dim, L, _ptr(center), st)
+    _lib.call("rola_b200_mean_pool", _ptr(k_rope), L * dim, HEAD_DIM, dim, B, H, L, blk, _ptr(center),
+              _ptr(pooled_k), st)
+    if lut is None:
+        lut = e(B * H, NB, topk, dt=torch.int32)
+        _lib.call("rola_b200_block_select", _ptr(pooled_q), _ptr(pooled_k), B * H, NB, NB, topk, _ptr(scores),
+                  _ptr(lut), st)
+    else:
+        lut = lut.to(device=dev, dtype=torch.int32).reshape(B * H, NB, -1).contiguous()
+        topk = lut.shape[-1]
+    pq_, pk_ = proj_q.to(BF16).contiguous(), proj_k.to(BF16).contiguous()
+    lc = None if lr_cos is None else lr_cos.to(BF16).contiguous()
+    ls = None if lr_sin is None else lr_sin.to(BF16).contiguous()
+    vs = v_raw.stride()
+    _lib.call("rola_b200_lowrank_kv", _ptr(k_normed), L * dim, HEAD_DIM, dim, _ptr(v_raw), vs[0], HEAD_DIM, vs[1],
+              _ptr(pk_), _ptr(lc), _ptr(ls), rope_dim, B, L, H, R, splits, _ptr(c_part), _ptr(C), _ptr(Ct), st)
+    _lib.call("rola_b200_lowrank_q", _ptr(q_normed), L * dim, HEAD_DIM, dim, _ptr(pq_), _ptr(lc), _ptr(ls),
+              rope_dim, B, L, H, R, _ptr(q_lr), st)
+    eps_lr = float(torch.finfo(BF16).eps)
+    _lib.call("rola_b200_sparse_attn", _ptr(q_rope), _ptr(k_rope), L * dim, HEAD_DIM, dim, _ptr(v_raw), vs[0],
+              HEAD_DIM, vs[1], _ptr(lut), B, L, H, blk, topk, _ptr(q_lr), _ptr(Ct), _ptr(gate), eps_lr, _ptr(out),
+              _ptr(o_sparse), L * dim, HEAD_DIM, dim, st)
+    if not keep:
+        return out
+    return out, dict(q_rope=q_rope, k_rope=k_rope, q_normed=q_normed, k_normed=k_normed, gate=gate,
+                     pooled_q=pooled_q, pooled_k=pooled_k, ksum=ksum, center=center, scores=scores, lut=lut,
+                     q_lr=q_lr, C=C, Ct=Ct, o_sparse=o_sparse, v=v_raw)
+
+
+def rola_attention_core(x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk, proj_q, proj_k,
+                        gate_w, gate_b, num_heads: int, blk: int = 128, topk: int = 1, eps: float = 1e-6,
+                        splits: int | None = None, keep: bool = False):
+    """RoLa forward from hidden states ``x [B, L, H*D]`` up to (excluding) the
+    output projection: ``WanSelfAttentionRoLa.fused_forward`` minus ``self.o``
+    (sparkdiffusion/networks/wan_rola_attention.py:414-446).  ``w_qkv`` is the
+    concatenated ``[Wq; Wk; Wv]`` of shape ``[3*dim, dim]``."""
+    B, L, dim = x.shape
+    qkv = qkv_gemm(x.reshape(B * L, dim), w_qkv, b_qkv).view(B, L, 3 * dim)
+    res = rola_attention_from_qkv(qkv[..., :dim], qkv[..., dim:2 * dim], qkv[..., 2 * dim:], x, cos_sin, lr_cos,
+                                  lr_sin, rope_dim, norm_wq, norm_wk, proj_q, proj_k, gate_w, gate_b, num_heads,
+                                  blk, topk, eps, splits, keep)
+    if keep:
+        out, extra = res
+        extra["qkv"] = qkv
+        return out, extra
+    return res
+
+
+def rola_forward_capi(x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk, proj_q, proj_k,
+                      gate_w, gate_b, num_heads: int, topk: int, eps: float = 1e-6, splits: int | None = None,
+                      workspace: torch.Tensor | None = None, out: torch.Tensor | None = None):
+    """Same forward through the single C entry point ``rola_b200_rola_forward``."""
+    B, L, dim = x.shape
+    H = num_heads
+    R = proj_q.shape[0]
+    splits = splits or default_splits(B, H, L)
+    need = _lib.lib().rola_b200_forward_workspace_bytes(B, L, H, 128, R, splits)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, device=x.device, dtype=torch.uint8)
+    if out is None:
+        out = torch.empty(B, L, dim, device=x.device, dtype=BF16)
+    _lib.call("rola_b200_rola_forward", _ptr(x), _ptr(w_qkv), _ptr(b_qkv), _ptr(_bf16_vec(norm_wq, dim, "norm_wq")),
+              _ptr(_bf16_vec(norm_wk, dim, "norm_wk")), _ptr(cos_sin), _ptr(lr_cos), _ptr(lr_sin), rope_dim,
+              _ptr(proj_q), _ptr(proj_k), _ptr(_bf16_vec(gate_w, HEAD_DIM, "gate_w")),
+              _ptr(_bf16_vec(gate_b, H, "gate_b")), B, L, H, 128, topk, R, splits, eps, _ptr(workspace), need,
+              _ptr(out), None, _stream())
+    return out
+
+
+# ---------------------------------------------------------------------------
+# reference-named API (sparkdiffusion.ops.fused_kernel)
+# ---------------------------------------------------------------------------
+def mean_pool(x: torch.Tensor, BLK: int, *, center: torch.Tensor | None = None) -> torch.Tensor:
+    """Block mean pooling of ``x [B, H, L, D]`` -> ``[B, H, NB, D]``
+    (sparkdiffusion/ops/fused_kernel/utils.py:272-297)."""
+    _require_cuda(x, center)
+    B, H, L, D = x.shape
+    if D != HEAD_DIM:
+        raise ValueError("head dim must be 128")
+    if center is not None:
+        if center.shape != (B, H, D):
+            raise ValueError(f"center must have shape {(B, H, D)}, got {tuple(center.shape)}")
+        if center.device != x.device or center.dtype != x.dtype:
+            raise ValueError("center must have the same device and dtype as x")
+        center = center.contiguous()
+    if x.dtype != BF16:
+        raise ValueError("mean_pool: bf16 input required")
+    if x.stride(3) != 1:
+        x = x.contiguous()
+    NB = (L + BLK - 1) // BLK
+    out = torch.empty(B, H, NB, D, device=x.device, dtype=x.dtype)
+    sB, sH, sT, _ = x.stride()
+    _lib.call("rola_b200_mean_pool", _ptr(x), sB, sH, sT, B, H, L, BLK, _ptr(center), _ptr(out), _stream())
+    return out
+
+
+def smooth_k_center(k4: torch.Tensor, blk: int) -> torch.Tensor:
+    """Smooth-K centre ``k.mean(dim=-2)`` of ``k [B, H, L, D]`` -> ``[B, H, D]``."""
+    _require_cuda(k4)
+    B, H, L, D = k4.shape
+    NB = (L + blk - 1) // blk
+    ws = torch.empty(B, NB, H * D, device=k4.device, dtype=torch.float32)
+    c = torch.empty(B, H, D, device=k4.device, dtype=BF16)
+    sB, sH, sT, _ = k4.stride()
+    _lib.call("rola_b200_smooth_k_center", _ptr(k4), sB, sH, sT, B, H, L, blk, _ptr(ws), _ptr(c), _stream())
+    return c
+
+
+def block_select(pooled_q: torch.Tensor, pooled_k: torch.Tensor, topk: int) -> torch.Tensor:
+    """fp32 pooled scores + top-k (ties toward the lower index), int32 ascending
+    ``[B*H, NBq, topk]``."""
+    _require_cuda(pooled_q, pooled_k)
+    B, H, NBq, D = pooled_q.shape
+    NBk = pooled_k.shape[2]
+    pq, pk = pooled_q.contiguous(), pooled_k.contiguous()
+    scores = torch.empty(B * H, NBq, NBk, device=pq.device, dtype=torch.float32)
+    lut = torch.empty(B * H, NBq, topk, device=pq.device, dtype=torch.int32)
+    _lib.call("rola_b200_block_select", _ptr(pq), _ptr(pk), B * H, NBq, NBk, topk, _ptr(scores), _ptr(lut),
+              _stream())
+    return lut
+
+
+def fused_sparse_attn(q, k, v, topk_ratio: float = 0.1, blkq: int = 64, blkk: int = 64, num_heads=None,
+                      force_local_sink: bool = False):
+    """Block-sparse attention over ``q, k, v [B*H, L, D]`` (already normed and
+    roped) -> ``[B, H, L, D]`` (sparkdiffusion/ops/fused_kernel/fused_sparse_attn.py:151-215).
+
+    Selection uses the build's contract (fp32 scores, lower-index ties, LUT
+    ascending).  ``force_local_sink`` is not supported (off in the reference)."""
+    BH, L, D = q.shape
+    if num_heads is None or BH % num_heads != 0:
+        raise ValueError(f"invalid num_heads={num_heads} for leading dimension {BH}")
+    if force_local_sink:
+        raise ValueError("force_local_sink is not supported by the B200 path")
+    if blkq != blkk or blkq != 128:
+        raise ValueError("the B200 attention kernel supports blkq == blkk == 128")
+    _require_cuda(q, k, v)
+    H = num_heads
+    B = BH // H
+    q4, k4, v4 = (t.view(B, H, L, D).contiguous() for t in (q, k, v))
+    NB = (L + blkq - 1) // blkq
+    topk = topk_count(topk_ratio, NB)
+    pq = mean_pool(q4, blkq)
+    pk = mean_pool(k4, blkk, center=smooth_k_center(k4, blkk))
+    lut = block_select(pq, pk, topk)
+    o = torch.empty_like(v4)
+    s = q4.stride()
+    vs = v4.stride()
+    _lib.call("rola_b200_sparse_attn", _ptr(q4), _ptr(k4), s[0], s[1], s[2], _ptr(v4), vs[0], vs[1], vs[2],
+              _ptr(lut), B, L, H, blkq, topk, None, None, None, 0.0, None, _ptr(o), s[0], s[1], s[2], _stream())
+    return o
+
+
+def fused_qkv_gemm_rope(x, q_proj, k_proj, v_proj, freqs, norm_q_weight, norm_k_weight, num_heads, head_dim,
+                        eps: float = 1e-6, return_normed: bool = False, fp8_weights=None, cos_sin=None):
+    """QKV projection + full-width qk-RMSNorm + interleaved RoPE
+    (sparkdiffusion/ops/fused_kernel/fused_qkv_rope.py:228-333).  Returns q, k,
+    v as ``[B*H, L, D]`` (and q/k normed ``[B, L, H, D]``), the reference's layouts."""
+    if fp8_weights is not None:
+        raise ValueError("fp8 QKV weights are not supported by the B200 path yet")
+    if head_dim != HEAD_DIM:
+        raise ValueError("head_dim must be 128")
+    B, L, dim = x.shape
+    H = num_heads
+    w = torch.cat([q_proj.weight, k_proj.weight, v_proj.weight], 0).to(BF16)
+    bias = None
+    if q_proj.bias is not None:
+        bias = torch.cat([q_proj.bias, k_proj.bias, v_proj.bias], 0).to(BF16)
+    qkv = qkv_gemm(x.reshape(B * L, dim), w, bias).view(B, L, 3 * dim)
+    if cos_sin is None:
+        cos_sin = prepare_cos_sin(freqs, L, head_dim)
+    e = lambda: torch.empty(B, L, dim, device=x.device, dtype=BF16)  # noqa: E731
+    q_rope, k_rope, q_n, k_n = e(), e(), e(), e()
+    has_norm = norm_q_weight is not None and norm_k_weight is not None
+    nwq = _bf16_vec(norm_q_weight, dim, "norm_q_weight") if has_norm else None
+    nwk = _bf16_vec(norm_k_weight, dim, "norm_k_weight") if has_norm else None
+    _lib.call("rola_b200_qk_norm_rope", _ptr(qkv), _ptr(qkv[..., dim:]), 3 * dim, None, _ptr(nwq), _ptr(nwk),
+              _ptr(cos_sin.to(torch.float32).contiguous()), None, None, B, L, H, 128, eps, _ptr(q_rope),
+              _ptr(k_rope), _ptr(q_n), _ptr(k_n), None, None, None, _stream())
+
+    def bhld(t):
+        return t.view(B, L, H, head_dim).permute(0, 2, 1, 3).reshape(B * H, L, head_dim)
+
+    outs = (bhld(q_rope), bhld(k_rope), bhld(qkv[..., 2 * dim:]))
+    if return_normed:
+        return (*outs, q_n.view(B, L, H, head_dim), k_n.view(B, L, H, head_dim))
+    return outs
