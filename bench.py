@@ -1,0 +1,399 @@
+#!/usr/bin/env python
+"""Benchmark: RoLa attention forward (ms/layer and effective TFLOP/s over the
+selected blocks), Wan2.1-14B 720P at 0.97 sparsity (configuration C4), on 1-8 B200.
+
+One step = one RoLa attention layer forward without the output projection
+(QKV GEMM + qk-RMSNorm + RoPE, block selection, low-rank branch, block-sparse
+attention with the fused epilogue) over one batch of synthetic inputs.  At N
+GPUs the same layer is split Ulysses-style (sequence shards for the prologue,
+head shards for attention, NCCL all-to-alls in between), so the total work is
+fixed (strong scaling).
+
+``value`` = selected-block attention FLOPs of the whole layer (4*D*sum rows*cols
+over valid tokens, from the actual LUT) / (max over ranks of the device time
+per step).  ``e2e`` is the same metric through the single C-ABI call (1 GPU) or
+the Ulysses entry (N GPUs) with the hidden states copied in from pinned host
+memory and the output copied back each step.
+
+``--impl reference`` times the reference algorithm on the host CPU cores (the
+CPU oracle port, see ``oracle/``) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "RoLa attn ms/layer & effective TFLOP/s (selected blocks), Wan14B 720P, 1/2/4/8 B200"
+UNIT = "TFLOP/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (read + write) per launch from one ncu capture (profiles/); None until captured
+NCU_TRAFFIC_BYTES = {"gemm": None, "attn": None}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="C4")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except Exception:
+        return FALLBACK_PEAKS, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=5)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1].split()[0]))
+                smax.append(float(parts[2].split()[0]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference algorithm (CPU oracle port) on a bounded sample
+# ---------------------------------------------------------------------------
+PRO_SAMPLE_TOKENS = 1024
+
+
+def cpu_sample_seconds(wl) -> tuple[float, str, int]:
+    """Seconds of one extrapolated layer on the host cores, the sample text and the thread count."""
+    from oracle import rola_oracle as orc
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    dim, H, L, D, R = wl.dim, wl.H, wl.L, 128, wl.rank
+    bf = torch.bfloat16
+    freqs = orc.wan_rope_freqs(*wl.grid)
+    cos_sin = orc.prepare_cos_sin(freqs, L, D)
+    lr_cos, lr_sin, rope_dim = orc.prepare_lowrank_cos_sin(freqs, L, R, bf)
+    ones = torch.ones(dim, dtype=bf)
+    # (1) prologue on a token sample, all heads (the norm couples heads)
+    n = PRO_SAMPLE_TOKENS
+    x = torch.randn(1, n, dim, generator=g).to(bf)
+    w = (torch.randn(3 * dim, dim, generator=g) * 0.02).to(bf)
+    t0 = time.perf_counter()
+    q_raw = orc.qkv_linear(x, w[:dim])
+    k_raw = orc.qkv_linear(x, w[dim:2 * dim])
+    v_raw = orc.qkv_linear(x, w[2 * dim:])
+    orc.qkv_epilogue(q_raw, k_raw, v_raw, cos_sin[:n], ones, ones, H)
+    gate = orc.gate_values(x, torch.full((D,), 0.01, dtype=bf), torch.full((H,), -1.946), H)
+    t_pro = time.perf_counter() - t0
+    # (2) one head over the whole sequence: selection, sparse attention, low-rank, gate
+    q = torch.randn(1, 1, L, D, generator=g).to(bf)
+    k = torch.randn(1, 1, L, D, generator=g).to(bf)
+    v = torch.randn(1, 1, L, D, generator=g).to(bf)
+    pq = (torch.randn(R, D, generator=g) / D ** 0.5).to(bf)
+    t0 = time.perf_counter()
+    lut, *_ = orc.block_select(q, k, wl.blk, wl.blk, wl.topk)
+    o_sparse = orc.sparse_attn_lut(q, k, v, lut, wl.blk, wl.blk)
+    o_lr, *_ = orc.fused_lowrank(q.transpose(1, 2), k.transpose(1, 2), v.reshape(1, L, D), pq, pq, lr_cos, lr_sin,
+                                 rope_dim)
+    orc.fused_gate(o_lr, o_sparse, None, None, None, gate=torch.full((1, L, 1), 0.125, dtype=bf))
+    t_head = time.perf_counter() - t0
+    del gate
+    total = t_pro * (wl.B * L / n) + t_head * wl.B * H
+    sample = (f"CPU oracle port (torch, fp32 math with the reference's bf16 rounding points): prologue on "
+              f"{n} of {wl.B * L} tokens (x{wl.B * L / n:.1f}) + selection/sparse attention/low-rank/gate for 1 of "
+              f"{wl.B * H} (batch, head) pairs over all {L} tokens (x{wl.B * H})")
+    return total, sample, threads
+
+
+def run_reference(args, wl, rank):
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_sample_seconds(wl)
+    secs = []
+    sample = ""
+    threads = 0
+    for _ in range(args.steps):
+        s, sample, threads = cpu_sample_seconds(wl)
+        secs.append(s)
+    t = statistics.median(secs)
+    flops = wl.attn_flops()
+    value = flops / t / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "ms_per_layer": t * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random hidden states and weights)",
+        "config": {"workload": workload_desc(wl), "global_batch": wl.B, "seq_len": wl.L},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "flops_per_layer": flops,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def workload_desc(wl) -> str:
+    return (f"{wl.name}: B={wl.B} H={wl.H} D=128 latent grid {wl.grid[0]}x{wl.grid[1]}x{wl.grid[2]} L={wl.L}, "
+            f"block {wl.blk} ({wl.NB} blocks), top-{wl.topk}, low-rank {wl.rank}, fused QKV from hidden states")
+
+
+def gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            return int(vis.split(",")[local_rank])
+        except (ValueError, IndexError):
+            return local_rank
+    return local_rank
+
+
+def main():
+    args = parse_args()
+    from sparkdiffusion_b200 import _lib, ops
+    from sparkdiffusion_b200.rope import prepare_cos_sin, prepare_lowrank_cos_sin, wan_rope_freqs
+    from sparkdiffusion_b200.workloads import ALL, attn_flops_lut, make_inputs
+
+    wl = ALL[args.workload]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if args.impl == "reference":
+        run_reference(args, wl, rank)
+        return
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=180),
+                                device_id=dev)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    _lib.load_library()
+    peaks, peak_kind = load_peaks()
+    inp = make_inputs(wl, device=dev)
+    freqs = wan_rope_freqs(*wl.grid, device=dev)
+    cos_sin = prepare_cos_sin(freqs, wl.L, 128)
+    lr_cos, lr_sin, rope_dim = prepare_lowrank_cos_sin(freqs, wl.L, wl.rank, torch.bfloat16)
+    B, L, H, dim = wl.B, wl.L, wl.H, wl.dim
+    Ls = L // world
+    x = inp["x"][:, rank * Ls:(rank + 1) * Ls].contiguous()
+    w_qkv = inp["w_qkv"]
+    common = (cos_sin, lr_cos, lr_sin, rope_dim, inp["norm_wq"], inp["norm_wk"], inp["proj_q"], inp["proj_k"],
+              inp["gate_w"], inp["gate_b"])
+
+    if world == 1:
+        def step(xin, events=None):
+            return ops.rola_attention_core(xin, w_qkv, None, *common, H, 128, wl.topk, events=events)
+    else:
+        from sparkdiffusion_b200.ulysses import ulysses_rola_attention_params
+
+        def step(xin, events=None):
+            return ulysses_rola_attention_params(xin, w_qkv, None, *common, H, wl.topk, group, events=events)
+
+    # exact selected-block FLOPs from this layer's LUT.  Every rank runs the
+    # 1-GPU pipeline once on the full hidden states (selection is bit-exact and
+    # identical to the head-sharded one), so no collective is needed here.
+    _, ex = ops.rola_attention_core(inp["x"], w_qkv, None, *common, H, 128, wl.topk, keep=True)
+    flops_total = attn_flops_lut(ex["lut"], L, wl.blk)
+    del ex
+    torch.cuda.synchronize()
+    if _lib.device_status() != 0:
+        raise SystemExit("device-side error flag set during the LUT pass")
+    torch.cuda.empty_cache()
+
+    for _ in range(args.warmup):
+        step(x)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    K = args.steps
+    ev = {"gemm": [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)],
+          "attn": [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]}
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(gpu_index(local_rank))
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start.record()
+    for i in range(K):
+        step(x, events={"gemm": ev["gemm"][i], "attn": ev["attn"][i]})
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = start.elapsed_time(end) / K
+    t_gemm = sum(a.elapsed_time(b) for a, b in ev["gemm"]) / K
+    t_attn = sum(a.elapsed_time(b) for a, b in ev["attn"]) / K
+    stats = torch.tensor([ms, t_gemm, t_attn], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    ms, t_gemm, t_attn = (float(v) for v in stats.tolist())
+    status = _lib.device_status()
+
+    # end to end: pinned host -> device, forward, device -> pinned host, every step
+    e2e = None
+    if not args.no_e2e:
+        x_host = x.cpu().pin_memory()
+        x_dev = torch.empty_like(x)
+        out_host = torch.empty(B, Ls, dim, dtype=torch.bfloat16).pin_memory()
+        if world == 1:
+            ws_bytes = _lib.lib().rola_b200_forward_workspace_bytes(B, L, H, 128, wl.rank,
+                                                                     ops.default_splits(B, H, L))
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+            out_dev = torch.empty(B, L, dim, dtype=torch.bfloat16, device=dev)
+
+            def e2e_step():
+                x_dev.copy_(x_host, non_blocking=True)
+                ops.rola_forward_capi(x_dev, w_qkv, None, *common, H, wl.topk, workspace=ws, out=out_dev)
+                out_host.copy_(out_dev, non_blocking=True)
+        else:
+            def e2e_step():
+                x_dev.copy_(x_host, non_blocking=True)
+                o = step(x_dev)
+                out_host.copy_(o, non_blocking=True)
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(K):
+            e2e_step()
+        e2.record()
+        torch.cuda.synchronize()
+        t_e2e = torch.tensor([s2.elapsed_time(e2) / K], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
+        t_e2e = float(t_e2e.item())
+        e2e = {"value": flops_total / (t_e2e * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": t_e2e,
+               "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+               "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
+               "api": "rola_b200_rola_forward (C ABI)" if world == 1 else "ulysses_rola_attention_params"}
+
+    cpu_base = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        runs = [cpu_sample_seconds(wl) for _ in range(3)]
+        secs = statistics.median(r[0] for r in runs)
+        sample, threads = runs[0][1] + " (median of 3)", runs[0][2]
+        cpu_base = {"value": flops_total / secs / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+                    "sample": sample, "ms_per_layer": secs * 1e3}
+
+    peak_sust = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+    gemm_flops_local = 6.0 * B * Ls * dim * dim
+    gemm_ach = gemm_flops_local / (t_gemm * 1e-3) / 1e12
+    attn_ach = (flops_total / world) / (t_attn * 1e-3) / 1e12
+    dominant = "gemm" if t_gemm >= t_attn else "attn"
+
+    def roof(name, ach):
+        tr = NCU_TRAFFIC_BYTES.get(name)
+        return {"kernel": {"gemm": "gemm_bf16_tcgen05", "attn": "sparse_attn_tcgen05"}[name], "bound": "tensor",
+                "achieved": ach, "peak": peak_sust, "unit": "TFLOP/s", "frac": ach / peak_sust,
+                "peak_kind": f"{peak_kind} bf16 sustained", "traffic": tr,
+                "ms_per_launch": t_gemm if name == "gemm" else t_attn}
+
+    launches_per_step = 10 if world == 1 else 11
+    line = {
+        "metric": METRIC, "value": flops_total / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": ms, "ms_per_layer": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) hidden states, N(0,0.02) QKV weights, random low-rank/gate factors)",
+        "config": {"workload": workload_desc(wl), "global_batch": B, "seq_len": L,
+                   "parallelism": f"ulysses{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (hidden states 774 MB, QKV 2.3 GB per layer); no flush"},
+        "flops_per_layer": flops_total,
+        "roofline": roof(dominant, gemm_ach if dominant == "gemm" else attn_ach),
+        "roofline_attention": roof("attn", attn_ach),
+        "roofline_gemm": roof("gemm", gemm_ach),
+        "e2e": e2e,
+        "cpu_baseline": cpu_base,
+        "clocks": clk,
+        "gpu_launches": launches_per_step * K,
+        "device_status": status,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

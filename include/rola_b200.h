@@ -73,10 +73,11 @@ int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw,
                            void* k_normed, void* gate_out, void* pooled_q, float* ksum, rola_stream_t stream);
 
 /* Sequence-parallel half of the prologue epilogue (before the Ulysses
- * all-to-all): qk-RMSNorm and gate on a sequence shard, writing q_normed,
- * k_normed and v into send buffers laid out [H/heads_per_chunk][B*L][heads_per_chunk*D]
- * (one contiguous chunk per destination rank).  Same reference interface as
- * rola_b200_qk_norm_rope. */
+ * all-to-all): qk-RMSNorm and gate on a sequence shard of L tokens, writing
+ * q_normed, k_normed and v into send buffers laid out
+ * [B][H/heads_per_chunk][L][heads_per_chunk*D] and the gate as
+ * [B][H/heads_per_chunk][L][heads_per_chunk] (per batch, one contiguous block
+ * per destination rank).  Same reference interface as rola_b200_qk_norm_rope. */
 int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_raw, int64_t ld_raw, const void* x,
                            const void* norm_wq, const void* norm_wk, const void* gate_w, const void* gate_b, int B,
                            int L, int H, int heads_per_chunk, float eps, void* q_send, void* k_send, void* v_send,

@@ -401,13 +401,14 @@ def gate_values(x, gate_w, gate_b, num_heads: int) -> torch.Tensor:
     return _r(1.0 / (1.0 + torch.exp(-logit)), dt)
 
 
-def fused_gate(o_lr, o_sparse, x, gate_w, gate_b, out_dtype=None) -> torch.Tensor:
+def fused_gate(o_lr, o_sparse, x, gate_w, gate_b, out_dtype=None, gate=None) -> torch.Tensor:
     """Restates ``_gate_fusion_kernel`` (fused_gate.py:27-127).
 
     o_lr_n = dtype(o_lr * rsqrt(mean(o_lr^2) + eps_lr)), eps_lr =
     finfo(dtype).eps (:72-77,220); os_rms through the dtype chain
     pow -> mean -> +1e-5 -> sqrt (:84-95); out = (os/os_rms + gate*o_lr_n) *
-    os_rms in fp32 (:120-121), stored ``[B, L, H*D]`` (:123-127).
+    os_rms in fp32 (:120-121), stored ``[B, L, H*D]`` (:123-127).  ``gate``
+    (``[B, L, H]`` from ``gate_values``) may replace x, gate_w and gate_b.
     """
     dt = o_lr.dtype
     B, H, L, D = o_lr.shape
@@ -420,7 +421,9 @@ def fused_gate(o_lr, o_sparse, x, gate_w, gate_b, out_dtype=None) -> torch.Tenso
     os_mean = _r(os_sq.sum(-1, keepdim=True) / D, dt)
     os_mean_eps = _r(os_mean + 1e-5, dt)
     os_rms = _r(torch.sqrt(os_mean_eps), dt)
-    gate = gate_values(x, gate_w, gate_b, H).permute(0, 2, 1)[..., None]
+    if gate is None:
+        gate = gate_values(x, gate_w, gate_b, H)
+    gate = gate.to(F32).permute(0, 2, 1)[..., None]
     out = (os_ / os_rms + gate * olr_n) * os_rms
     return out.to(out_dtype or dt).permute(0, 2, 1, 3).reshape(B, L, H * D).contiguous()
 

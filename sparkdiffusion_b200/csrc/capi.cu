@@ -179,7 +179,6 @@ int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw,
   p.blk = blk;
   p.NB = (L + blk - 1) / blk;
   p.heads_per_chunk = H;
-  p.chunk_stride = 0;
   p.eps = eps;
   const bool norm = norm_wq != nullptr;
   const bool pool = pooled_q != nullptr;
@@ -221,7 +220,6 @@ int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_r
   p.blk = 128;
   p.NB = (L + 127) / 128;
   p.heads_per_chunk = heads_per_chunk;
-  p.chunk_stride = (int64_t)B * L * heads_per_chunk * 128;
   p.eps = eps;
   return cuda_status(launch_norm_rope_pool(p, true, false, false, S(stream)), "qk_norm_pack");
 }

@@ -24,15 +24,14 @@ struct NormRopeParams {
   // outputs (any may be nullptr)
   __nv_bfloat16* q_rope;  // [B*L, dim]
   __nv_bfloat16* k_rope;
-  __nv_bfloat16* q_normed;  // chunked layout, see out_offset()
+  __nv_bfloat16* q_normed;  // [B][H/heads_per_chunk][L][heads_per_chunk*D] (see out_offset)
   __nv_bfloat16* k_normed;
   __nv_bfloat16* v_out;
-  __nv_bfloat16* gate_out;  // [B*L, H]
+  __nv_bfloat16* gate_out;  // [B][H/heads_per_chunk][L][heads_per_chunk]
   __nv_bfloat16* pooled_q;  // [B, H, NB, D]
   float* ksum;              // [B, NB, dim]
   int B, L, H, blk, NB;
-  int heads_per_chunk;     // chunked output layout for the all-to-all send buffers
-  int64_t chunk_stride;    // elements between chunks
+  int heads_per_chunk;     // chunked output layout for the all-to-all send buffers (H: plain layout)
   float eps;
 };
 int launch_norm_rope_pool(const NormRopeParams& p, bool norm, bool rope, bool pool, cudaStream_t s);

@@ -19,13 +19,21 @@ namespace rola {
 
 
 
-// Output offset of (row = b*L + t, column c) in the chunked layout
-// [H/heads_per_chunk][B*L][heads_per_chunk*D].  With heads_per_chunk == H this
-// is the plain token-major [B*L, dim] layout.
-__device__ __forceinline__ int64_t out_offset(const NormRopeParams& p, int64_t row, int col) {
+// Output offset of (batch b, token t, hidden column c) in the chunked layout
+// [B][H / heads_per_chunk][L][heads_per_chunk * D]: one contiguous block per
+// destination rank of the sequence->head all-to-all.  With heads_per_chunk == H
+// this is the plain token-major [B, L, H*D] layout.
+__device__ __forceinline__ int64_t out_offset(const NormRopeParams& p, int b, int t, int col) {
   const int chunk_cols = p.heads_per_chunk * 128;
   const int chunk = col / chunk_cols;
-  return chunk * p.chunk_stride + row * chunk_cols + (col - chunk * chunk_cols);
+  return (int64_t)b * p.L * (p.H * 128) + (int64_t)chunk * p.L * chunk_cols + (int64_t)t * chunk_cols +
+         (col - chunk * chunk_cols);
+}
+// same layout for the per-(token, head) gate: [B][H / heads_per_chunk][L][heads_per_chunk]
+__device__ __forceinline__ int64_t gate_offset(const NormRopeParams& p, int b, int t, int h) {
+  const int chunk = h / p.heads_per_chunk;
+  return (int64_t)b * p.L * p.H + (int64_t)chunk * p.L * p.heads_per_chunk + (int64_t)t * p.heads_per_chunk +
+         (h - chunk * p.heads_per_chunk);
 }
 
 __device__ __forceinline__ void load8(const __nv_bfloat16* src, float (&v)[8]) {
@@ -108,7 +116,7 @@ __global__ void __launch_bounds__(768) norm_rope_pool_kernel(NormRopeParams p) {
     if (p.v_out != nullptr && active) {
       float v[8];
       load8(p.v_in + row * p.ld_in + col, v);
-      store8(p.v_out + out_offset(p, row, col), v);
+      store8(p.v_out + out_offset(p, b, t, col), v);
     }
     if (NORM) {
       float ss[2] = {0.f, 0.f};
@@ -125,8 +133,8 @@ __global__ void __launch_bounds__(768) norm_rope_pool_kernel(NormRopeParams p) {
         q[i] = rbf(rbf(q[i] * rq) * wq[i]);  // unit in bf16, then x weight in bf16
         k[i] = rbf(rbf(k[i] * rk) * wk[i]);
       }
-      if (p.q_normed && active) store8(p.q_normed + out_offset(p, row, col), q);
-      if (p.k_normed && active) store8(p.k_normed + out_offset(p, row, col), k);
+      if (p.q_normed && active) store8(p.q_normed + out_offset(p, b, t, col), q);
+      if (p.k_normed && active) store8(p.k_normed + out_offset(p, b, t, col), k);
     }
     if (ROPE) {
       const float4* cs = reinterpret_cast<const float4*>(p.cos_sin + (int64_t)t * 128 + d0);
@@ -165,7 +173,7 @@ __global__ void __launch_bounds__(768) norm_rope_pool_kernel(NormRopeParams p) {
       if ((j & 15) == 0 && active) {
         const float lin = rbf(g);
         const float logit = rbf(lin + gbias);
-        p.gate_out[row * p.H + h] = f2bf(1.0f / (1.0f + expf(-logit)));
+        p.gate_out[gate_offset(p, b, t, h)] = f2bf(1.0f / (1.0f + expf(-logit)));
       }
     }
   }

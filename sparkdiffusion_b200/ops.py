@@ -84,9 +84,70 @@ def qkv_gemm(x2d: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = Non
     return out
 
 
+def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, ksum, lr_cos, lr_sin, rope_dim,
+                         proj_q, proj_k, num_heads: int, blk: int, topk: int, splits: int | None = None,
+                         keep: bool = False, lut=None, events: dict | None = None):
+    """Selection, low-rank branch and fused attention for ``num_heads`` heads
+    over the full sequence.  q_rope/k_rope/q_normed/k_normed/v are token-major
+    ``[B, L, H*D]`` (unit column stride; q/k tensors contiguous), gate
+    ``[B, L, H]``, pooled_q ``[B, H, NB, D]`` and ksum ``[B, NB, H*D]`` come from
+    the prologue pass.  Returns the gated output ``[B, L, H*D]``."""
+    B, L, dim = q_rope.shape
+    H = num_heads
+    dev = q_rope.device
+    NB = (L + blk - 1) // blk
+    R = proj_q.shape[0]
+    splits = splits or default_splits(B, H, L)
+    st = _stream()
+    e = lambda *s, dt=BF16: torch.empty(*s, device=dev, dtype=dt)  # noqa: E731
+    center = e(B, H, HEAD_DIM)
+    pooled_k = e(B, H, NB, HEAD_DIM)
+    q_lr = e(B, L, H * R)
+    c_part = e(splits, B * H, R, HEAD_DIM, dt=torch.float32)
+    C = e(B * H, R, HEAD_DIM) if keep else None
+    Ct = e(B * H, HEAD_DIM, R)
+    out = e(B, L, dim)
+    o_sparse = e(B, L, dim) if keep else None
+    scores = None
+    _lib.call("rola_b200_center_from_sums", _ptr(ksum), B, NB, dim, L, _ptr(center), st)
+    _lib.call("rola_b200_mean_pool", _ptr(k_rope), L * dim, HEAD_DIM, dim, B, H, L, blk, _ptr(center),
+              _ptr(pooled_k), st)
+    if lut is None:
+        scores = e(B * H, NB, NB, dt=torch.float32)
+        lut = e(B * H, NB, topk, dt=torch.int32)
+        _lib.call("rola_b200_block_select", _ptr(pooled_q), _ptr(pooled_k), B * H, NB, NB, topk, _ptr(scores),
+                  _ptr(lut), st)
+    else:
+        lut = lut.to(device=dev, dtype=torch.int32).reshape(B * H, NB, -1).contiguous()
+        topk = lut.shape[-1]
+    pq_, pk_ = proj_q.to(BF16).contiguous(), proj_k.to(BF16).contiguous()
+    lc = None if lr_cos is None else lr_cos.to(BF16).contiguous()
+    ls = None if lr_sin is None else lr_sin.to(BF16).contiguous()
+    vs = v.stride()
+    ks = k_normed.stride()
+    qs = q_normed.stride()
+    _lib.call("rola_b200_lowrank_kv", _ptr(k_normed), ks[0], HEAD_DIM, ks[1], _ptr(v), vs[0], HEAD_DIM, vs[1],
+              _ptr(pk_), _ptr(lc), _ptr(ls), rope_dim, B, L, H, R, splits, _ptr(c_part), _ptr(C), _ptr(Ct), st)
+    _lib.call("rola_b200_lowrank_q", _ptr(q_normed), qs[0], HEAD_DIM, qs[1], _ptr(pq_), _ptr(lc), _ptr(ls),
+              rope_dim, B, L, H, R, _ptr(q_lr), st)
+    eps_lr = float(torch.finfo(BF16).eps)
+    if events is not None:
+        events["attn"][0].record()
+    _lib.call("rola_b200_sparse_attn", _ptr(q_rope), _ptr(k_rope), L * dim, HEAD_DIM, dim, _ptr(v), vs[0],
+              HEAD_DIM, vs[1], _ptr(lut), B, L, H, blk, topk, _ptr(q_lr), _ptr(Ct), _ptr(gate), eps_lr, _ptr(out),
+              _ptr(o_sparse), L * dim, HEAD_DIM, dim, st)
+    if events is not None:
+        events["attn"][1].record()
+    if not keep:
+        return out
+    return out, dict(pooled_k=pooled_k, center=center, scores=scores, lut=lut, q_lr=q_lr, C=C, Ct=Ct,
+                     o_sparse=o_sparse)
+
+
 def rola_attention_from_qkv(q_raw, k_raw, v_raw, x, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk,
                             proj_q, proj_k, gate_w, gate_b, num_heads: int, blk: int = 128, topk: int = 1,
-                            eps: float = 1e-6, splits: int | None = None, keep: bool = False, lut=None):
+                            eps: float = 1e-6, splits: int | None = None, keep: bool = False, lut=None,
+                            events: dict | None = None):
     """RoLa forward from projected q/k/v (token-major ``[B, L, H*D]`` views
     with unit column stride; q and k share a row stride) to the gated output
     ``[B, L, H*D]``.  ``keep`` returns the intermediates too.  ``lut`` (int32
@@ -108,73 +169,48 @@ def rola_attention_from_qkv(q_raw, k_raw, v_raw, x, cos_sin, lr_cos, lr_sin, rop
     NB = (L + blk - 1) // blk
     if not 1 <= topk <= NB:
         raise ValueError(f"topk must be in [1, {NB}]")
-    R = proj_q.shape[0]
-    splits = splits or default_splits(B, H, L)
     st = _stream()
     e = lambda *s, dt=BF16: torch.empty(*s, device=dev, dtype=dt)  # noqa: E731
     q_rope, k_rope = e(B, L, dim), e(B, L, dim)
     q_normed, k_normed = e(B, L, dim), e(B, L, dim)
     gate = e(B, L, H)
-    pooled_q, pooled_k = e(B, H, NB, HEAD_DIM), e(B, H, NB, HEAD_DIM)
+    pooled_q = e(B, H, NB, HEAD_DIM)
     ksum = e(B, NB, dim, dt=torch.float32)
-    center = e(B, H, HEAD_DIM)
-    scores = e(B * H, NB, NB, dt=torch.float32)
-    q_lr = e(B, L, H * R)
-    c_part = e(splits, B * H, R, HEAD_DIM, dt=torch.float32)
-    C = e(B * H, R, HEAD_DIM) if keep else None
-    Ct = e(B * H, HEAD_DIM, R)
-    out = e(B, L, dim)
-    o_sparse = e(B, L, dim) if keep else None
     gw = _bf16_vec(gate_w, HEAD_DIM, "gate_w")
     gb = _bf16_vec(gate_b, H, "gate_b")
     nwq = None if norm_wq is None else _bf16_vec(norm_wq, dim, "norm_wq")
     nwk = None if norm_wk is None else _bf16_vec(norm_wk, dim, "norm_wk")
     cos_sin = cos_sin.to(torch.float32).contiguous()
-    ld_qk = q_raw.stride(1)
-    _lib.call("rola_b200_qk_norm_rope", _ptr(q_raw), _ptr(k_raw), ld_qk, _ptr(x.contiguous()), _ptr(nwq),
+    xc = x.contiguous()
+    _lib.call("rola_b200_qk_norm_rope", _ptr(q_raw), _ptr(k_raw), q_raw.stride(1), _ptr(xc), _ptr(nwq),
               _ptr(nwk), _ptr(cos_sin), _ptr(gw), _ptr(gb), B, L, H, blk, eps, _ptr(q_rope), _ptr(k_rope),
               _ptr(q_normed), _ptr(k_normed), _ptr(gate), _ptr(pooled_q), _ptr(ksum), st)
-    _lib.call("rola_b200_center_from_sums", _ptr(ksum), B, NB, dim, L, _ptr(center), st)
-    _lib.call("rola_b200_mean_pool", _ptr(k_rope), L * dim, HEAD_DIM, dim, B, H, L, blk, _ptr(center),
-              _ptr(pooled_k), st)
-    if lut is None:
-        lut = e(B * H, NB, topk, dt=torch.int32)
-        _lib.call("rola_b200_block_select", _ptr(pooled_q), _ptr(pooled_k), B * H, NB, NB, topk, _ptr(scores),
-                  _ptr(lut), st)
-    else:
-        lut = lut.to(device=dev, dtype=torch.int32).reshape(B * H, NB, -1).contiguous()
-        topk = lut.shape[-1]
-    pq_, pk_ = proj_q.to(BF16).contiguous(), proj_k.to(BF16).contiguous()
-    lc = None if lr_cos is None else lr_cos.to(BF16).contiguous()
-    ls = None if lr_sin is None else lr_sin.to(BF16).contiguous()
-    vs = v_raw.stride()
-    _lib.call("rola_b200_lowrank_kv", _ptr(k_normed), L * dim, HEAD_DIM, dim, _ptr(v_raw), vs[0], HEAD_DIM, vs[1],
-              _ptr(pk_), _ptr(lc), _ptr(ls), rope_dim, B, L, H, R, splits, _ptr(c_part), _ptr(C), _ptr(Ct), st)
-    _lib.call("rola_b200_lowrank_q", _ptr(q_normed), L * dim, HEAD_DIM, dim, _ptr(pq_), _ptr(lc), _ptr(ls),
-              rope_dim, B, L, H, R, _ptr(q_lr), st)
-    eps_lr = float(torch.finfo(BF16).eps)
-    _lib.call("rola_b200_sparse_attn", _ptr(q_rope), _ptr(k_rope), L * dim, HEAD_DIM, dim, _ptr(v_raw), vs[0],
-              HEAD_DIM, vs[1], _ptr(lut), B, L, H, blk, topk, _ptr(q_lr), _ptr(Ct), _ptr(gate), eps_lr, _ptr(out),
-              _ptr(o_sparse), L * dim, HEAD_DIM, dim, st)
+    res = head_local_attention(q_rope, k_rope, q_normed, k_normed, v_raw, gate, pooled_q, ksum, lr_cos, lr_sin,
+                               rope_dim, proj_q, proj_k, H, blk, topk, splits, keep, lut, events)
     if not keep:
-        return out
-    return out, dict(q_rope=q_rope, k_rope=k_rope, q_normed=q_normed, k_normed=k_normed, gate=gate,
-                     pooled_q=pooled_q, pooled_k=pooled_k, ksum=ksum, center=center, scores=scores, lut=lut,
-                     q_lr=q_lr, C=C, Ct=Ct, o_sparse=o_sparse, v=v_raw)
+        return res
+    out, extra = res
+    extra.update(q_rope=q_rope, k_rope=k_rope, q_normed=q_normed, k_normed=k_normed, gate=gate,
+                 pooled_q=pooled_q, ksum=ksum, v=v_raw)
+    return out, extra
 
 
 def rola_attention_core(x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk, proj_q, proj_k,
                         gate_w, gate_b, num_heads: int, blk: int = 128, topk: int = 1, eps: float = 1e-6,
-                        splits: int | None = None, keep: bool = False):
+                        splits: int | None = None, keep: bool = False, events: dict | None = None):
     """RoLa forward from hidden states ``x [B, L, H*D]`` up to (excluding) the
     output projection: ``WanSelfAttentionRoLa.fused_forward`` minus ``self.o``
     (sparkdiffusion/networks/wan_rola_attention.py:414-446).  ``w_qkv`` is the
     concatenated ``[Wq; Wk; Wv]`` of shape ``[3*dim, dim]``."""
     B, L, dim = x.shape
+    if events is not None:
+        events["gemm"][0].record()
     qkv = qkv_gemm(x.reshape(B * L, dim), w_qkv, b_qkv).view(B, L, 3 * dim)
+    if events is not None:
+        events["gemm"][1].record()
     res = rola_attention_from_qkv(qkv[..., :dim], qkv[..., dim:2 * dim], qkv[..., 2 * dim:], x, cos_sin, lr_cos,
                                   lr_sin, rope_dim, norm_wq, norm_wk, proj_q, proj_k, gate_w, gate_b, num_heads,
-                                  blk, topk, eps, splits, keep)
+                                  blk, topk, eps, splits, keep, events=events)
     if keep:
         out, extra = res
         extra["qkv"] = qkv

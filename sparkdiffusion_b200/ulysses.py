@@ -1,0 +1,135 @@
+"""Ulysses sequence<->head parallel RoLa attention across GPUs (NCCL).
+
+The layer's input arrives sequence-sharded: rank r holds tokens
+[r*Ls, (r+1)*Ls) of every head (Ls = L / p).  The qk-RMSNorm couples all heads
+of a token (sparkdiffusion/ops/fused_kernel/fused_qkv_rope.py:146-149), so
+
+1. the QKV GEMM, the qk-RMSNorm and the gate run on the sequence shard, the
+   norm pass writing q_normed, k_normed, v and the gate straight into
+   per-destination send blocks ``[B][p][Ls][Hl*D]`` (Hl = H / p);
+2. one all-to-all per tensor (per batch element) moves them to head shards:
+   rank r now holds heads [r*Hl, (r+1)*Hl) of the whole sequence;
+3. RoPE (global positions), pooling, selection, the low-rank branch and the
+   fused block-sparse attention run head-local over the full sequence;
+4. an all-to-all sends each rank's output rows back to their sequence owner,
+   which interleaves the head groups into ``[B, Ls, H*D]``.
+
+This follows the reference's DistributedAttention pattern
+(sparkdiffusion/utils/a2a_cp.py:146-186) but applies it to RoLa, so the
+multi-GPU result equals the single-GPU one (the reference's own context
+parallel RoLa attends only within each rank's shard).
+
+``seq_to_head`` / ``head_to_seq`` are device-agnostic (they also run on gloo
+CPU ranks in the tests); ``ulysses_rola_attention`` runs the CUDA kernels.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _lib, ops
+from .ops import BF16, HEAD_DIM, _bf16_vec, _ptr, _stream
+
+
+def seq_to_head(send: torch.Tensor, group=None, async_op: bool = False):
+    """``send [B, p, Ls, X]`` (block j goes to rank j) -> ``recv [B, p, Ls, X]``
+    whose block i came from rank i, i.e. ``[B, L, X]`` in global token order."""
+    recv = torch.empty_like(send)
+    works = [dist.all_to_all_single(recv[b], send[b], group=group, async_op=async_op) for b in range(send.shape[0])]
+    return recv, works
+
+
+def head_to_seq(out_heads: torch.Tensor, p: int, group=None) -> torch.Tensor:
+    """``out_heads [B, L, X]`` (this rank's head group, all tokens) ->
+    ``[B, Ls, p*X]``: this rank's tokens with the p head groups side by side."""
+    B, L, X = out_heads.shape
+    Ls = L // p
+    send = out_heads.contiguous().view(B, p, Ls, X)
+    recv = torch.empty_like(send)
+    for b in range(B):
+        dist.all_to_all_single(recv[b], send[b], group=group)
+    return recv.permute(0, 2, 1, 3).reshape(B, Ls, p * X)
+
+
+def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk,
+                                  proj_q, proj_k, gate_w, gate_b, num_heads: int, topk: int, group=None,
+                                  eps: float = 1e-6, splits: int | None = None, events: dict | None = None):
+    """Sequence-sharded RoLa forward: ``x_local [B, Ls, H*D]`` on this rank ->
+    ``[B, Ls, H*D]`` (excluding the output projection).  ``cos_sin`` and the
+    low-rank tables cover the whole sequence (global positions)."""
+    p = dist.get_world_size(group)
+    B, Ls, dim = x_local.shape
+    H = num_heads
+    if H % p != 0:
+        raise ValueError(f"num_heads={H} must be divisible by the sequence-parallel size {p}")
+    Hl = H // p
+    L = Ls * p
+    if cos_sin.shape[0] < L:
+        raise ValueError("cos_sin must cover the full (global) sequence")
+    dev = x_local.device
+    st = _stream()
+    if events is not None:
+        events["gemm"][0].record()
+    qkv = ops.qkv_gemm(x_local.reshape(B * Ls, dim), w_qkv, b_qkv)
+    if events is not None:
+        events["gemm"][1].record()
+    q_send = torch.empty(B, p, Ls, Hl * HEAD_DIM, device=dev, dtype=BF16)
+    k_send = torch.empty_like(q_send)
+    v_send = torch.empty_like(q_send)
+    g_send = torch.empty(B, p, Ls, Hl, device=dev, dtype=BF16)
+    gw = _bf16_vec(gate_w, HEAD_DIM, "gate_w")
+    gb = _bf16_vec(gate_b, H, "gate_b")
+    xc = x_local.contiguous()
+    _lib.call("rola_b200_qk_norm_pack", _ptr(qkv), _ptr(qkv[:, dim:]), _ptr(qkv[:, 2 * dim:]), 3 * dim, _ptr(xc),
+              _ptr(_bf16_vec(norm_wq, dim, "norm_wq")), _ptr(_bf16_vec(norm_wk, dim, "norm_wk")), _ptr(gw),
+              _ptr(gb), B, Ls, H, Hl, eps, _ptr(q_send), _ptr(k_send), _ptr(v_send), _ptr(g_send), st)
+    q_n, w1 = seq_to_head(q_send, group, async_op=True)
+    k_n, w2 = seq_to_head(k_send, group, async_op=True)
+    v, w3 = seq_to_head(v_send, group, async_op=True)
+    gate, w4 = seq_to_head(g_send, group, async_op=True)
+    for w in (*w1, *w2, *w3, *w4):
+        w.wait()
+    q_n = q_n.view(B, L, Hl * HEAD_DIM)
+    k_n = k_n.view(B, L, Hl * HEAD_DIM)
+    v = v.view(B, L, Hl * HEAD_DIM)
+    gate = gate.view(B, L, Hl)
+    blk = 128
+    NB = (L + blk - 1) // blk
+    q_rope = torch.empty_like(q_n)
+    k_rope = torch.empty_like(k_n)
+    pooled_q = torch.empty(B, Hl, NB, HEAD_DIM, device=dev, dtype=BF16)
+    ksum = torch.empty(B, NB, Hl * HEAD_DIM, device=dev, dtype=torch.float32)
+    cs = cos_sin.to(torch.float32).contiguous()
+    _lib.call("rola_b200_rope_pool", _ptr(q_n), _ptr(k_n), Hl * HEAD_DIM, _ptr(cs), B, L, Hl, blk, _ptr(q_rope),
+              _ptr(k_rope), _ptr(pooled_q), _ptr(ksum), st)
+    out_heads = ops.head_local_attention(q_rope, k_rope, q_n, k_n, v, gate, pooled_q, ksum, lr_cos, lr_sin,
+                                         rope_dim, proj_q, proj_k, Hl, blk, topk, splits, events=events)
+    return head_to_seq(out_heads, p, group)
+
+
+def ulysses_rola_attention(layer, x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, nwq, nwk):
+    """Entry used by WanSelfAttentionRoLaB200 when a sequence-parallel group is set.
+
+    The model passes RoPE tables of the local shard (wan2pt1.py:825-826); the
+    head-local stages need the whole sequence, so the tables are all-gathered."""
+    group = layer._pg
+    p = dist.get_world_size(group)
+    B, Ls, dim = x_local.shape
+    L = Ls * p
+    if cos_sin.shape[0] == Ls and p > 1:
+        cos_sin = _all_gather_rows(cos_sin, group)
+        lr_cos = _all_gather_rows(lr_cos, group)
+        lr_sin = _all_gather_rows(lr_sin, group)
+    NB = (L + 127) // 128
+    topk = ops.topk_count(layer.rola_topk_ratio, NB)
+    return ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, nwq, nwk,
+                                         layer.proj_q.weight, layer.proj_k.weight, layer.gate_proj.weight,
+                                         layer.gate_bias, layer.num_heads, topk, group, layer.eps)
+
+
+def _all_gather_rows(t: torch.Tensor, group) -> torch.Tensor:
+    p = dist.get_world_size(group)
+    parts = [torch.empty_like(t) for _ in range(p)]
+    dist.all_gather(parts, t.contiguous(), group=group)
+    return torch.cat(parts, 0)
