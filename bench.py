@@ -252,8 +252,9 @@ def main():
     Ls = L // world
     x = inp["x"][:, rank * Ls:(rank + 1) * Ls].contiguous()
     w_qkv = inp["w_qkv"]
+    # parameters in their kernel dtype once (no per-step conversion kernels)
     common = (cos_sin, lr_cos, lr_sin, rope_dim, inp["norm_wq"], inp["norm_wk"], inp["proj_q"], inp["proj_k"],
-              inp["gate_w"], inp["gate_b"])
+              inp["gate_w"].reshape(-1).contiguous(), inp["gate_b"].reshape(-1).to(torch.bfloat16))
 
     if world == 1:
         def step(xin, events=None):
