@@ -144,6 +144,25 @@ int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t q
                           int topk, const void* q_lr, const void* Ct, const void* gate, float eps_lr, void* out,
                           void* o_sparse, int64_t o_sB, int64_t o_sH, int64_t o_sT, rola_stream_t stream);
 
+/* Allocation-free variant of rola_b200_lowrank_kv.  No counterpart in the
+ * reference: SparkDiffusion lets PyTorch allocate every temporary.
+ * For callers that cannot provide or allocate device memory for the fp32
+ * partial sums: a host framework that owns a fixed device-memory pool and
+ * forbids allocations outside it, a latency-critical loop where cudaMalloc /
+ * cudaFree (which may synchronise the device) is not acceptable, or a binding
+ * with no CUDA allocator at hand.  The partials live in a fixed 16 MiB
+ * (4 Mi fp32) array compiled into the library, held by every GPU that loads
+ * the library until the process exits; splits*B*H*R*D must not exceed 4 Mi
+ * (larger requests return ROLA_ERR_INVALID; C4 fits with splits <= 12).  The
+ * first call on a device looks up the array's device address (issue it before
+ * any stream capture on that device).  All calls share the array, so calls that
+ * overlap on the GPU race; the array needs no clearing (every partial is
+ * overwritten before it is read).  Arguments and outputs as rola_b200_lowrank_kv. */
+int rola_b200_lowrank_kv_noalloc(const void* k_normed, int64_t k_sB, int64_t k_sH, int64_t k_sT, const void* v,
+                                 int64_t v_sB, int64_t v_sH, int64_t v_sT, const void* proj_k, const void* lr_cos,
+                                 const void* lr_sin, int rope_dim, int B, int L, int H, int R, int splits, void* C,
+                                 void* Ct, rola_stream_t stream);
+
 /* Workspace bytes needed by rola_b200_rola_forward for these sizes. */
 size_t rola_b200_forward_workspace_bytes(int B, int L, int H, int blk, int R, int splits);
 

@@ -54,6 +54,8 @@ SIGNATURES = {
                              _P, _P, _P, _P],
     "rola_b200_sparse_attn": [_P, _P, _L, _L, _L, _P, _L, _L, _L, _P, _I, _I, _I, _I, _I, _P, _P, _P,
                               _F, _P, _P, _L, _L, _L, _P],
+    "rola_b200_lowrank_kv_noalloc": [_P, _L, _L, _L, _P, _L, _L, _L, _P, _P, _P, _I, _I, _I, _I, _I, _I,
+                                     _P, _P, _P],
     "rola_b200_forward_workspace_bytes": [_I, _I, _I, _I, _I, _I],
     "rola_b200_rola_forward": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I,
                                _I, _I, _F, _P, _Z, _P, _P, _P],

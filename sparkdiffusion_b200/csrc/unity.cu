@@ -7,3 +7,4 @@
 #include "gemm.cu"
 #include "attn.cu"
 #include "capi.cu"
+#include "noalloc.cu"
