@@ -50,15 +50,20 @@ const char* rola_b200_last_error(void);
 int rola_b200_device_status(int clear);
 
 /* (a4) QKV projection: out[M, N] (row stride N) = x[M, K] . w[N, K]^T + bias[N].
- * bias may be NULL.  N % 256 == 0, K % 64 == 0.
+ * bias may be NULL.  N % 256 == 0, K % 64 == 0.  ssq (NULL to skip): fp32
+ * [M, N/256], the sum of squares of each row's bf16 outputs per 256-column
+ * tile, consumed by the qk-RMSNorm pass.
  * Replaces the three F.linear calls of fused_qkv_gemm_rope
  * (sparkdiffusion/ops/fused_kernel/fused_qkv_rope.py:287-289) with one GEMM over
  * the concatenated weight [Wq; Wk; Wv]. */
-int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out, int64_t M, int64_t N, int64_t K,
-                       rola_stream_t stream);
+int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out, float* ssq, int64_t M, int64_t N,
+                       int64_t K, rola_stream_t stream);
 
 /* (a4 epilogue, a5 q-pool, a6 block sums, a10 gate) in one pass over the rows.
- * q_raw/k_raw: token-major, row stride ld_raw.  x: token-major [B*L, dim] (gate
+ * q_raw/k_raw: token-major, row stride ld_raw.  ssq (optional): the
+ * [B*L, ssq_ld] sums of squares written by rola_b200_qkv_gemm over the q|k|v
+ * row (q tiles first, then k), which replace the in-kernel row reduction (H even,
+ * blk <= 256); NULL computes the row norms in the kernel.  x: token-major [B*L, dim] (gate
  * input; NULL skips the gate).  norm_wq/norm_wk: [dim] (both NULL = no norm).
  * cos_sin: [L, D] fp32 interleaved (cos0, sin0, cos1, ...).  gate_w: [D],
  * gate_b: [H] bf16.  Outputs (any may be NULL): q_rope, k_rope, q_normed,
@@ -67,10 +72,11 @@ int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out
  * Replaces _epilogue_kernel (fused_qkv_rope.py:53-225, layout [B*H, L, D] there),
  * mean_pool(q) (utils.py:272-297 via fused_sparse_attn.py:179) and the gate
  * logits of _gate_fusion_kernel (fused_gate.py:97-114). */
-int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw, const void* x, const void* norm_wq,
-                           const void* norm_wk, const float* cos_sin, const void* gate_w, const void* gate_b, int B,
-                           int L, int H, int blk, float eps, void* q_rope, void* k_rope, void* q_normed,
-                           void* k_normed, void* gate_out, void* pooled_q, float* ksum, rola_stream_t stream);
+int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw, const float* ssq, int ssq_ld,
+                           const void* x, const void* norm_wq, const void* norm_wk, const float* cos_sin,
+                           const void* gate_w, const void* gate_b, int B, int L, int H, int blk, float eps,
+                           void* q_rope, void* k_rope, void* q_normed, void* k_normed, void* gate_out, void* pooled_q,
+                           float* ksum, rola_stream_t stream);
 
 /* Sequence-parallel half of the prologue epilogue (before the Ulysses
  * all-to-all): qk-RMSNorm and gate on a sequence shard of L tokens, writing
@@ -78,10 +84,10 @@ int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw,
  * [B][H/heads_per_chunk][L][heads_per_chunk*D] and the gate as
  * [B][H/heads_per_chunk][L][heads_per_chunk] (per batch, one contiguous block
  * per destination rank).  Same reference interface as rola_b200_qk_norm_rope. */
-int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_raw, int64_t ld_raw, const void* x,
-                           const void* norm_wq, const void* norm_wk, const void* gate_w, const void* gate_b, int B,
-                           int L, int H, int heads_per_chunk, float eps, void* q_send, void* k_send, void* v_send,
-                           void* gate_out, rola_stream_t stream);
+int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_raw, int64_t ld_raw, const float* ssq,
+                           int ssq_ld, const void* x, const void* norm_wq, const void* norm_wk, const void* gate_w,
+                           const void* gate_b, int B, int L, int H, int heads_per_chunk, float eps, void* q_send,
+                           void* k_send, void* v_send, void* gate_out, rola_stream_t stream);
 
 /* Head-parallel half (after the all-to-all): RoPE, q-pool and k block sums from
  * the normed q/k (token-major, row stride ld).  Same reference interface as
@@ -107,7 +113,8 @@ int rola_b200_center_from_sums(const float* ksum, int B, int NB, int dim, int L,
 
 /* (a7) pooled scores (fp32) and top-k selection: pooled_q [BH, NBq, D],
  * pooled_k [BH, NBk, D] bf16 -> lut [BH, NBq, topk] int32 ascending, ties toward
- * the lower block index.  scores_ws: fp32 scratch of BH*NBq*NBk floats.
+ * the lower block index.  scores_ws: fp32 scratch of BH*NBq*NBk floats, used
+ * only when NBk > 832 (below that the scores stay on chip; NULL is allowed).
  * Replaces `pooled_q @ pooled_k^T` + torch.topk (fused_sparse_attn.py:181-198). */
 int rola_b200_block_select(const void* pooled_q, const void* pooled_k, int BH, int NBq, int NBk, int topk,
                            float* scores_ws, int32_t* lut, rola_stream_t stream);

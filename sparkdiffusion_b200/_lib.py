@@ -39,10 +39,10 @@ SIGNATURES = {
     "rola_b200_abi_version": [],
     "rola_b200_last_error": [],
     "rola_b200_device_status": [_I],
-    "rola_b200_qkv_gemm": [_P, _P, _P, _P, _L, _L, _L, _P],
-    "rola_b200_qk_norm_rope": [_P, _P, _L, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F,
+    "rola_b200_qkv_gemm": [_P, _P, _P, _P, _P, _L, _L, _L, _P],
+    "rola_b200_qk_norm_rope": [_P, _P, _L, _P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F,
                                _P, _P, _P, _P, _P, _P, _P, _P],
-    "rola_b200_qk_norm_pack": [_P, _P, _P, _L, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F,
+    "rola_b200_qk_norm_pack": [_P, _P, _P, _L, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F,
                                _P, _P, _P, _P, _P],
     "rola_b200_rope_pool": [_P, _P, _L, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P],
     "rola_b200_mean_pool": [_P, _L, _L, _L, _I, _I, _I, _I, _P, _P, _P],

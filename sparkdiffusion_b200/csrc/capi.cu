@@ -121,8 +121,8 @@ int rola_b200_device_status(int clear) {
   return v;
 }
 
-int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out, int64_t M, int64_t N, int64_t K,
-                       rola_stream_t stream) {
+int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out, float* ssq, int64_t M, int64_t N,
+                       int64_t K, rola_stream_t stream) {
   ROLA_CHECK(x && w && out, "qkv_gemm: null pointer");
   ROLA_CHECK(M > 0 && M < (1ll << 31), "qkv_gemm: M out of range");
   ROLA_CHECK(N > 0 && N % 256 == 0 && N <= 65536, "qkv_gemm: N must be a positive multiple of 256");
@@ -141,21 +141,26 @@ int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out
     const uint32_t box[2] = {64, 256};
     ROLA_TRY(make_map(&tb, w, 2, dims, strides, box, "qkv_gemm: w"));
   }
-  return cuda_status(launch_gemm_bf16(ta, tb, BF(bias), BFm(out), N, (int)M, (int)N, (int)K, S(stream)),
+  return cuda_status(launch_gemm_bf16(ta, tb, BF(bias), BFm(out), N, ssq, (int)M, (int)N, (int)K, S(stream)),
                      "qkv_gemm");
 }
 
-int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw, const void* x, const void* norm_wq,
-                           const void* norm_wk, const float* cos_sin, const void* gate_w, const void* gate_b, int B,
-                           int L, int H, int blk, float eps, void* q_rope, void* k_rope, void* q_normed,
-                           void* k_normed, void* gate_out, void* pooled_q, float* ksum, rola_stream_t stream) {
+int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw, const float* ssq, int ssq_ld,
+                           const void* x, const void* norm_wq, const void* norm_wk, const float* cos_sin,
+                           const void* gate_w, const void* gate_b, int B, int L, int H, int blk, float eps,
+                           void* q_rope, void* k_rope, void* q_normed, void* k_normed, void* gate_out, void* pooled_q,
+                           float* ksum, rola_stream_t stream) {
   ROLA_CHECK(q_raw && k_raw && cos_sin, "qk_norm_rope: null input");
-  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 48 && blk > 0, "qk_norm_rope: bad sizes (H <= 48)");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 40 && blk > 0, "qk_norm_rope: bad sizes (H <= 40)");
   ROLA_CHECK((norm_wq == nullptr) == (norm_wk == nullptr), "qk_norm_rope: give both norm weights or neither");
   ROLA_CHECK(ld_raw % 8 == 0 && aligned16(q_raw) && aligned16(k_raw), "qk_norm_rope: 16-byte aligned rows required");
   ROLA_CHECK((pooled_q == nullptr) == (ksum == nullptr), "qk_norm_rope: pooled_q and ksum go together");
   ROLA_CHECK(x == nullptr || (gate_w && gate_b && gate_out), "qk_norm_rope: the gate needs gate_w, gate_b, gate_out");
+  ROLA_CHECK(ssq == nullptr || (H % 2 == 0 && blk <= 256 && ssq_ld >= H),
+             "qk_norm_rope: sums of squares need an even head count, blk <= 256 and ssq_ld >= H");
   NormRopeParams p{};
+  p.ssq = ssq;
+  p.ssq_ld = ssq_ld;
   p.q_in = BF(q_raw);
   p.k_in = BF(k_raw);
   p.ld_in = ld_raw;
@@ -189,17 +194,20 @@ int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw,
   return cuda_status(launch_norm_rope_pool(p, norm, true, pool, S(stream)), "qk_norm_rope");
 }
 
-int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_raw, int64_t ld_raw, const void* x,
-                           const void* norm_wq, const void* norm_wk, const void* gate_w, const void* gate_b, int B,
-                           int L, int H, int heads_per_chunk, float eps, void* q_send, void* k_send, void* v_send,
-                           void* gate_out, rola_stream_t stream) {
+int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_raw, int64_t ld_raw, const float* ssq,
+                           int ssq_ld, const void* x, const void* norm_wq, const void* norm_wk, const void* gate_w,
+                           const void* gate_b, int B, int L, int H, int heads_per_chunk, float eps, void* q_send,
+                           void* k_send, void* v_send, void* gate_out, rola_stream_t stream) {
   ROLA_CHECK(q_raw && k_raw && v_raw && norm_wq && norm_wk && q_send && k_send && v_send,
              "qk_norm_pack: null pointer");
-  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 48 && heads_per_chunk > 0 && H % heads_per_chunk == 0,
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 40 && heads_per_chunk > 0 && H % heads_per_chunk == 0,
              "qk_norm_pack: bad sizes");
   ROLA_CHECK(ld_raw % 8 == 0, "qk_norm_pack: 16-byte aligned rows required");
   ROLA_CHECK(x == nullptr || (gate_w && gate_b && gate_out), "qk_norm_pack: the gate needs gate_w, gate_b, gate_out");
+  ROLA_CHECK(ssq == nullptr || (H % 2 == 0 && ssq_ld >= H), "qk_norm_pack: sums of squares need an even head count");
   NormRopeParams p{};
+  p.ssq = ssq;
+  p.ssq_ld = ssq_ld;
   p.q_in = BF(q_raw);
   p.k_in = BF(k_raw);
   p.v_in = BF(v_raw);
@@ -228,7 +236,7 @@ int rola_b200_rope_pool(const void* q_normed, const void* k_normed, int64_t ld, 
                         int H, int blk, void* q_rope, void* k_rope, void* pooled_q, float* ksum,
                         rola_stream_t stream) {
   ROLA_CHECK(q_normed && k_normed && cos_sin && q_rope && k_rope, "rope_pool: null pointer");
-  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 48 && blk > 0, "rope_pool: bad sizes");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 40 && blk > 0, "rope_pool: bad sizes");
   ROLA_CHECK((pooled_q == nullptr) == (ksum == nullptr), "rope_pool: pooled_q and ksum go together");
   ROLA_CHECK(ld % 8 == 0, "rope_pool: 16-byte aligned rows required");
   NormRopeParams p{};
@@ -279,9 +287,14 @@ int rola_b200_center_from_sums(const float* ksum, int B, int NB, int dim, int L,
 
 int rola_b200_block_select(const void* pooled_q, const void* pooled_k, int BH, int NBq, int NBk, int topk,
                            float* scores_ws, int32_t* lut, rola_stream_t stream) {
-  ROLA_CHECK(pooled_q && pooled_k && scores_ws && lut, "block_select: null pointer");
+  ROLA_CHECK(pooled_q && pooled_k && lut && (scores_ws || NBk <= 832), "block_select: null pointer");
   ROLA_CHECK(BH > 0 && NBq > 0 && NBk > 0 && NBk <= 2048, "block_select: bad sizes (NBk <= 2048)");
   ROLA_CHECK(topk >= 1 && topk <= NBk, "block_select: topk must be in [1, NBk]");
+  if (NBk <= 832) {
+    // fused: the scores stay in registers (scores_ws is not written)
+    return cuda_status(launch_select_fused(BF(pooled_q), BF(pooled_k), BH, NBq, NBk, topk, lut, S(stream)),
+                       "block_select");
+  }
   ROLA_TRY(cuda_status(launch_scores(BF(pooled_q), BF(pooled_k), BH, NBq, NBk, scores_ws, S(stream)),
                        "block_select/scores"));
   return cuda_status(launch_topk(scores_ws, BH * NBq, NBk, topk, lut, S(stream)), "block_select/topk");
@@ -408,7 +421,7 @@ int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t q
 // whole layer
 // ---------------------------------------------------------------------------
 struct FwdLayout {
-  size_t qkv, q_rope, k_rope, q_normed, k_normed, gate, pooled_q, pooled_k, ksum, center, scores, lut, q_lr,
+  size_t qkv, ssq, q_rope, k_rope, q_normed, k_normed, gate, pooled_q, pooled_k, ksum, center, scores, lut, q_lr,
       c_partial, ct, total;
 };
 
@@ -422,6 +435,7 @@ static FwdLayout fwd_layout(int B, int L, int H, int blk, int R, int splits, int
     return o;
   };
   f.qkv = take(BL * 3 * dim * 2);
+  f.ssq = take(BL * (3 * dim / 256) * 4);
   f.q_rope = take(BL * dim * 2);
   f.k_rope = take(BL * dim * 2);
   f.q_normed = take(BL * dim * 2);
@@ -454,7 +468,8 @@ int rola_b200_rola_forward(const void* x, const void* w_qkv, const void* b_qkv, 
                            rola_stream_t stream) {
   ROLA_CHECK(x && w_qkv && norm_wq && norm_wk && cos_sin && proj_q && proj_k && gate_w && gate_b && workspace && out,
              "rola_forward: null pointer");
-  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 48 && blk == 128 && R == 64 && splits > 0, "rola_forward: bad sizes");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 40 && H % 2 == 0 && blk == 128 && R == 64 && splits > 0,
+             "rola_forward: bad sizes (even H <= 40, blk 128, R 64)");
   const int NB = (L + blk - 1) / blk;
   ROLA_CHECK(topk >= 1 && topk <= NB, "rola_forward: topk must be in [1, NB]");
   const FwdLayout f = fwd_layout(B, L, H, blk, R, splits, NB);
@@ -465,9 +480,11 @@ int rola_b200_rola_forward(const void* x, const void* w_qkv, const void* b_qkv, 
   const int64_t M = (int64_t)B * L;
   __nv_bfloat16* qkv = reinterpret_cast<__nv_bfloat16*>(ws + f.qkv);
   int32_t* lut = lut_out ? lut_out : reinterpret_cast<int32_t*>(ws + f.lut);
-  ROLA_TRY(rola_b200_qkv_gemm(x, w_qkv, b_qkv, qkv, M, 3 * dim, dim, stream));
-  ROLA_TRY(rola_b200_qk_norm_rope(qkv, qkv + dim, 3 * dim, x, norm_wq, norm_wk, cos_sin, gate_w, gate_b, B, L, H,
-                                  blk, eps, ws + f.q_rope, ws + f.k_rope, ws + f.q_normed, ws + f.k_normed,
+  float* ssq = reinterpret_cast<float*>(ws + f.ssq);
+  const int ssq_ld = (int)(3 * dim / 256);
+  ROLA_TRY(rola_b200_qkv_gemm(x, w_qkv, b_qkv, qkv, ssq, M, 3 * dim, dim, stream));
+  ROLA_TRY(rola_b200_qk_norm_rope(qkv, qkv + dim, 3 * dim, ssq, ssq_ld, x, norm_wq, norm_wk, cos_sin, gate_w, gate_b,
+                                  B, L, H, blk, eps, ws + f.q_rope, ws + f.k_rope, ws + f.q_normed, ws + f.k_normed,
                                   ws + f.gate, ws + f.pooled_q, reinterpret_cast<float*>(ws + f.ksum), stream));
   ROLA_TRY(rola_b200_center_from_sums(reinterpret_cast<float*>(ws + f.ksum), B, NB, (int)dim, L, ws + f.center,
                                       stream));

@@ -9,7 +9,8 @@
 // Warp roles: warp 0 issues TMA loads, warp 1 owns TMEM and issues the MMAs
 // from one elected thread (tcgen05.mma M=128 N=256 K=16), warps 2..5 drain the
 // accumulator from TMEM (each warp reads the 32 TMEM lanes its warp id allows)
-// and write bf16 rows.  Tiles are rasterised in groups of 16 M-tiles so the
+// and write bf16 rows (optionally also each row's sum of squares of its bf16
+// outputs per 256-column tile, which the qk-RMSNorm pass consumes).  Tiles are rasterised in groups of 16 M-tiles so the
 // CTAs resident at one time share A and W tiles through L2.
 #include "common.cuh"
 #include "kernels.h"
@@ -28,8 +29,8 @@ constexpr int GROUP_M = 16;
 
 __global__ void __launch_bounds__(gemm::THREADS, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                      const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out, int64_t ldo, int M,
-                      int N, int K) {
+                      const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out, int64_t ldo,
+                      float* __restrict__ ssq, int M, int N, int K) {
   using namespace gemm;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -122,6 +123,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     tc_fence_after();
     if (ok) {
       const int gm_row = m0 + row;
+      float ss = 0.f;  // sum of squares of this row's bf16 outputs in this tile
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
@@ -146,8 +148,16 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
             u.w = pack_bf2(f[8 * i + 6], f[8 * i + 7]);
             dst[i] = u;
           }
+          if (ssq) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float r = rbf(f[i]);
+              ss = fmaf(r, r, ss);
+            }
+          }
         }
       }
+      if (ssq && gm_row < M) ssq[(int64_t)gm_row * (N / BN) + n_tile] = ss;
     }
   }
   tc_fence_before();
@@ -160,12 +170,12 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
 }
 
 int launch_gemm_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const __nv_bfloat16* bias, __nv_bfloat16* out,
-                     int64_t ldo, int M, int N, int K, cudaStream_t s) {
+                     int64_t ldo, float* ssq, int M, int N, int K, cudaStream_t s) {
   using namespace gemm;
   if (N % BN != 0 || K % BK != 0 || M <= 0) return -1;
   cudaFuncSetAttribute(gemm_bf16_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   const int num_m = (M + BM - 1) / BM, num_n = N / BN;
-  gemm_bf16_tcgen05<<<num_m * num_n, THREADS, SMEM_BYTES, s>>>(ta, tb, bias, out, ldo, M, N, K);
+  gemm_bf16_tcgen05<<<num_m * num_n, THREADS, SMEM_BYTES, s>>>(ta, tb, bias, out, ldo, ssq, M, N, K);
   return (int)cudaGetLastError();
 }
 

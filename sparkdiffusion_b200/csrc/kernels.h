@@ -30,6 +30,8 @@ struct NormRopeParams {
   __nv_bfloat16* gate_out;  // [B][H/heads_per_chunk][L][heads_per_chunk]
   __nv_bfloat16* pooled_q;  // [B, H, NB, D]
   float* ksum;              // [B, NB, dim]
+  const float* ssq;         // optional [B*L, ssq_ld] per-256-column sums of squares (q tiles, then k tiles)
+  int ssq_ld;
   int B, L, H, blk, NB;
   int heads_per_chunk;     // chunked output layout for the all-to-all send buffers (H: plain layout)
   float eps;
@@ -50,6 +52,9 @@ int launch_scores(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH, int 
                   cudaStream_t s);
 // lut[bh, m, :] = top-k of scores[bh, m, :] (ties -> lower index), ascending int32
 int launch_topk(const float* scores, int rows, int NBk, int k, int32_t* lut, cudaStream_t s);
+// scores + top-k in one kernel (NBk <= 832; same results as launch_scores + launch_topk)
+int launch_select_fused(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH, int NBq, int NBk, int k,
+                        int32_t* lut, cudaStream_t s);
 
 // lowrank.cu --------------------------------------------------------------
 struct LowrankParams {
@@ -71,9 +76,10 @@ int launch_lowrank_reduce(const float* c_partial, int splits, int BH, int R, __n
                           cudaStream_t s);
 
 // gemm.cu -----------------------------------------------------------------
-// out[M, N] (row stride ldo) = A[M, K] * W[N, K]^T (+ bias[N]), bf16 in/out, fp32 accumulate
+// out[M, N] (row stride ldo) = A[M, K] * W[N, K]^T (+ bias[N]), bf16 in/out, fp32 accumulate;
+// ssq (optional) [M, N/256]: per-row sum of squares of the bf16 outputs of each 256-column tile
 int launch_gemm_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const __nv_bfloat16* bias, __nv_bfloat16* out,
-                     int64_t ldo, int M, int N, int K, cudaStream_t s);
+                     int64_t ldo, float* ssq, int M, int N, int K, cudaStream_t s);
 
 // attn.cu -----------------------------------------------------------------
 struct AttnParams {

@@ -135,13 +135,44 @@ __global__ void __launch_bounds__(128) lowrank_q_kernel(LowrankParams p) {
     }
 }
 
+// ---------------------------------------------------------------------------
 // partial C = sum over this CTA's token tiles of k_lr^T v (fp32)
-__global__ void __launch_bounds__(128) lowrank_kv_kernel(LowrankParams p) {
+//
+// 64-token tiles, 8 warps, k_normed/v tiles double-buffered with cp.async so
+// the HBM stream of the next tile overlaps the two MMA phases of this one:
+//   projection  k_lr[64 t][64 r]  : warp w -> tokens 16*(w%4), ranks 32*(w/4)
+//   accumulation C[64 r][128 d]   : warp w -> ranks 16*(w%4), dims 64*(w/4)
+// ---------------------------------------------------------------------------
+constexpr int kKvT = 64;                       // tokens per tile
+constexpr int kKvTile = kKvT * kPadX;          // elements of one padded [64 x 128] tile
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  const int n = valid ? 16 : 0;  // zero-fill rows past L
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void kv_issue_tile(__nv_bfloat16* sXb, __nv_bfloat16* sVb, const LowrankParams& p, int b,
+                                              int h, int t0) {
+  const __nv_bfloat16* xb = p.x + (int64_t)b * p.x_sB + (int64_t)h * p.x_sH;
+  const __nv_bfloat16* vb = p.v + (int64_t)b * p.v_sB + (int64_t)h * p.v_sH;
+  for (int i = threadIdx.x; i < kKvT * 16; i += blockDim.x) {
+    const int r = i >> 4, c = (i & 15) * 8;
+    const bool ok = t0 + r < p.L;
+    const int t = ok ? t0 + r : 0;
+    cp_async16(smem_u32(sXb + r * kPadX + c), xb + (int64_t)t * p.x_sT + c, ok);
+    cp_async16(smem_u32(sVb + r * kPadX + c), vb + (int64_t)t * p.v_sT + c, ok);
+  }
+}
+
+__global__ void __launch_bounds__(256, 2) lowrank_kv_kernel(LowrankParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  __nv_bfloat16* sX = reinterpret_cast<__nv_bfloat16*>(smem_raw);
-  __nv_bfloat16* sV = sX + kLrT * kPadX;
-  __nv_bfloat16* sP = sV + kLrT * kPadX;
-  __nv_bfloat16* sK = sP + 64 * kPadX;  // k_lr [128 t][64 r] (padded)
+  __nv_bfloat16* sX = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [2][64][136]
+  __nv_bfloat16* sV = sX + 2 * kKvTile;                             // [2][64][136]
+  __nv_bfloat16* sP = sV + 2 * kKvTile;                             // [64][136]
+  __nv_bfloat16* sK = sP + 64 * kPadX;                              // k_lr [64 t][72]
   const int split = blockIdx.x;
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -150,63 +181,95 @@ __global__ void __launch_bounds__(128) lowrank_kv_kernel(LowrankParams p) {
     const int r = i >> 4, c = (i & 15) * 8;
     *reinterpret_cast<uint4*>(sP + r * kPadX + c) = *reinterpret_cast<const uint4*>(p.proj + r * 128 + c);
   }
-  float cacc[16][4];
+  float cacc[8][4];
 #pragma unroll
-  for (int nt = 0; nt < 16; ++nt)
+  for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) cacc[nt][e] = 0.f;
 
-  const int ntiles = (p.L + kLrT - 1) / kLrT;
-  for (int tile = split; tile < ntiles; tile += p.splits) {
-    const int t0 = tile * kLrT;
-    __syncthreads();  // previous tile fully consumed
-    load_tile(sX, p.x, p.x_sB, p.x_sH, p.x_sT, b, t0, p.L, h);
-    load_tile(sV, p.v, p.v_sB, p.v_sH, p.v_sT, b, t0, p.L, h);
+  const int ntiles = (p.L + kKvT - 1) / kKvT;
+  int tile = split;
+  int buf = 0;
+  if (tile < ntiles) kv_issue_tile(sX, sV, p, b, h, tile * kKvT);
+  cp_async_commit();
+  const int pm = warp & 3, pn = warp >> 2;  // projection: m-tile, rank half
+  for (; tile < ntiles; tile += p.splits, buf ^= 1) {
+    const int next = tile + p.splits;
+    if (next < ntiles) kv_issue_tile(sX + (buf ^ 1) * kKvTile, sV + (buf ^ 1) * kKvTile, p, b, h, next * kKvT);
+    cp_async_commit();
+    cp_async_wait_1();  // this tile has landed (the next may still be in flight)
     __syncthreads();
-    float acc[2][8][4];
-    project_warp(sX, sP, acc);
+    const __nv_bfloat16* cX = sX + buf * kKvTile;
+    const __nv_bfloat16* cV = sV + buf * kKvTile;
+    // projection: 16 tokens x 32 ranks per warp, K = 128
+    float acc[4][4];
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int tl = warp * 32 + mt * 16 + g + half * 8;
-        const int t = t0 + tl;
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-          const int r = nt * 8 + tig * 2;
-          uint32_t v = 0u;
-          if (t < p.L) v = silu_rope_pair(acc[mt][nt][half * 2], acc[mt][nt][half * 2 + 1], t, r >> 1, p);
-          *reinterpret_cast<uint32_t*>(sK + tl * kPadR + r) = v;
-        }
-      }
-    __syncthreads();
-    // C[r, d] += sum_t k_lr[t, r] v[t, d]; warp w owns r in [16w, 16w + 16)
+      for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
       uint32_t a0, a1, a2, a3;
       {
         const int mi = lane >> 3;
+        const int row = pm * 16 + (lane & 7) + (mi & 1) * 8;
+        const int col = ks * 16 + (mi >> 1) * 8;
+        ldsm_x4(smem_u32(cX + row * kPadX + col), a0, a1, a2, a3);
+      }
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        const int mi = lane >> 3;
+        const int n = pn * 32 + np * 16 + (lane & 7) + (mi >> 1) * 8;
+        const int k = ks * 16 + (mi & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(smem_u32(sP + n * kPadX + k), b0, b1, b2, b3);
+        mma16816(acc[2 * np], a0, a1, a2, a3, b0, b1);
+        mma16816(acc[2 * np + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    const int t0 = tile * kKvT;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int tl = pm * 16 + g + half * 8;
+      const int t = t0 + tl;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int r = pn * 32 + nt * 8 + tig * 2;
+        uint32_t v = 0u;
+        if (t < p.L) v = silu_rope_pair(acc[nt][half * 2], acc[nt][half * 2 + 1], t, r >> 1, p);
+        *reinterpret_cast<uint32_t*>(sK + tl * kPadR + r) = v;
+      }
+    }
+    __syncthreads();
+    // C[r, d] += sum_t k_lr[t, r] v[t, d]; warp w: r in [16*(w%4), +16), d in [64*(w/4), +64)
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      uint32_t a0, a1, a2, a3;
+      {
+        const int mi = lane >> 3;
         const int t = ks * 16 + (lane & 7) + (mi >> 1) * 8;
-        const int r = warp * 16 + (mi & 1) * 8;
+        const int r = pm * 16 + (mi & 1) * 8;
         ldsm_x4_t(smem_u32(sK + t * kPadR + r), a0, a1, a2, a3);
       }
 #pragma unroll
-      for (int np = 0; np < 8; ++np) {
+      for (int np = 0; np < 4; ++np) {
         const int mi = lane >> 3;
         const int t = ks * 16 + (lane & 7) + (mi & 1) * 8;
-        const int d = np * 16 + (mi >> 1) * 8;
+        const int d = pn * 64 + np * 16 + (mi >> 1) * 8;
         uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(smem_u32(sV + t * kPadX + d), b0, b1, b2, b3);
+        ldsm_x4_t(smem_u32(cV + t * kPadX + d), b0, b1, b2, b3);
         mma16816(cacc[2 * np], a0, a1, a2, a3, b0, b1);
         mma16816(cacc[2 * np + 1], a0, a1, a2, a3, b2, b3);
       }
     }
+    __syncthreads();  // both tiles of this buffer consumed before it is refilled
   }
+  cp_async_wait_0();
   float* dst = p.c_partial + (((int64_t)split * p.B * p.H + bh) * 64) * 128;
 #pragma unroll
-  for (int nt = 0; nt < 16; ++nt) {
-    const int d = nt * 8 + tig * 2;
-    const int r0 = warp * 16 + g;
+  for (int nt = 0; nt < 8; ++nt) {
+    const int d = pn * 64 + nt * 8 + tig * 2;
+    const int r0 = pm * 16 + g;
     *reinterpret_cast<float2*>(dst + r0 * 128 + d) = make_float2(cacc[nt][0], cacc[nt][1]);
     *reinterpret_cast<float2*>(dst + (r0 + 8) * 128 + d) = make_float2(cacc[nt][2], cacc[nt][3]);
   }
@@ -235,10 +298,10 @@ int launch_lowrank_q(const LowrankParams& p, cudaStream_t s) {
 }
 
 int launch_lowrank_kv(const LowrankParams& p, cudaStream_t s) {
-  const int smem = (2 * kLrT * kPadX + 64 * kPadX + kLrT * kPadR) * 2;
+  const int smem = (4 * kKvTile + 64 * kPadX + kKvT * kPadR) * 2;
   cudaFuncSetAttribute(lowrank_kv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   dim3 grid(p.splits, p.B * p.H);
-  lowrank_kv_kernel<<<grid, 128, smem, s>>>(p);
+  lowrank_kv_kernel<<<grid, 256, smem, s>>>(p);
   return (int)cudaGetLastError();
 }
 

@@ -76,8 +76,9 @@ __device__ __forceinline__ void block_sum(float (&v)[NV], float* red, int parity
 }
 
 template <bool NORM, bool ROPE, bool POOL>
-__global__ void __launch_bounds__(768) norm_rope_pool_kernel(NormRopeParams p) {
+__global__ void __launch_bounds__(640) norm_rope_pool_kernel(NormRopeParams p) {
   __shared__ float red[2 * 2 * 32];
+  __shared__ float s_rstd[2][256];
   const int m = blockIdx.x, b = blockIdx.y;
   const int dim = p.H * 128;
   // the block is rounded up to whole warps; threads past H*16 only join the reductions
@@ -88,6 +89,20 @@ __global__ void __launch_bounds__(768) norm_rope_pool_kernel(NormRopeParams p) {
   const int t0 = m * p.blk;
   const int t1 = min(p.L, t0 + p.blk);
   const float inv_dim = 1.0f / (float)dim;
+  // With the GEMM's per-tile sums of squares the norm needs no block reduction:
+  // the rstd of every token of the block is computed up front.
+  const bool use_ssq = NORM && p.ssq != nullptr;
+  if (use_ssq) {
+    const int nt = dim / 256, n = t1 - t0;
+    for (int i = threadIdx.x; i < 2 * n; i += blockDim.x) {
+      const int which = i / n, tl = i - which * n;
+      const float* src = p.ssq + ((int64_t)b * p.L + t0 + tl) * p.ssq_ld + which * nt;
+      float s = 0.f;
+      for (int k = 0; k < nt; ++k) s += src[k];
+      s_rstd[which][tl] = rsqrtf(s * inv_dim + p.eps);
+    }
+    __syncthreads();
+  }
 
   float wq[8], wk[8];
   if (NORM) {
@@ -97,18 +112,27 @@ __global__ void __launch_bounds__(768) norm_rope_pool_kernel(NormRopeParams p) {
   float gw[8];
   const bool gate = p.x != nullptr && p.gate_out != nullptr;
   if (gate) load8(p.gate_w + d0, gw);
-  float gbias = gate ? bf2f(p.gate_b[h]) : 0.f;
+  const float gbias = gate ? bf2f(p.gate_b[h]) : 0.f;
 
   float qs[8], ks[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) qs[i] = ks[i] = 0.f;
 
+  // one token ahead in registers so its loads overlap this token's work
+  float q[8], k[8], xv[8];
+  auto load_tok = [&](int t, float (&qq)[8], float (&kk)[8], float (&xx)[8]) {
+    const int64_t row = (int64_t)b * p.L + t;
+    load8(p.q_in + row * p.ld_in + col, qq);
+    load8(p.k_in + row * p.ld_in + col, kk);
+    if (gate) load8(p.x + row * p.ld_x + col, xx);
+  };
+  if (t0 < t1) load_tok(t0, q, k, xv);
   int parity = 0;
+#pragma unroll 1
   for (int t = t0; t < t1; ++t, parity ^= 1) {
     const int64_t row = (int64_t)b * p.L + t;
-    float q[8], k[8];
-    load8(p.q_in + row * p.ld_in + col, q);
-    load8(p.k_in + row * p.ld_in + col, k);
+    float qn[8], kn[8], xn[8];
+    if (t + 1 < t1) load_tok(t + 1, qn, kn, xn);
     if (!active) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) q[i] = k[i] = 0.f;
@@ -119,15 +143,21 @@ __global__ void __launch_bounds__(768) norm_rope_pool_kernel(NormRopeParams p) {
       store8(p.v_out + out_offset(p, b, t, col), v);
     }
     if (NORM) {
-      float ss[2] = {0.f, 0.f};
+      float rq, rk;
+      if (use_ssq) {
+        rq = s_rstd[0][t - t0];
+        rk = s_rstd[1][t - t0];
+      } else {
+        float ss[2] = {0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        ss[0] = fmaf(q[i], q[i], ss[0]);
-        ss[1] = fmaf(k[i], k[i], ss[1]);
+        for (int i = 0; i < 8; ++i) {
+          ss[0] = fmaf(q[i], q[i], ss[0]);
+          ss[1] = fmaf(k[i], k[i], ss[1]);
+        }
+        block_sum<2>(ss, red, parity);
+        rq = rsqrtf(ss[0] * inv_dim + p.eps);
+        rk = rsqrtf(ss[1] * inv_dim + p.eps);
       }
-      block_sum<2>(ss, red, parity);
-      const float rq = rsqrtf(ss[0] * inv_dim + p.eps);
-      const float rk = rsqrtf(ss[1] * inv_dim + p.eps);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         q[i] = rbf(rbf(q[i] * rq) * wq[i]);  // unit in bf16, then x weight in bf16
@@ -163,8 +193,6 @@ __global__ void __launch_bounds__(768) norm_rope_pool_kernel(NormRopeParams p) {
       }
     }
     if (gate) {
-      float xv[8];
-      load8(p.x + row * p.ld_x + col, xv);
       float g = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) g = fmaf(xv[i], gw[i], g);
@@ -175,6 +203,12 @@ __global__ void __launch_bounds__(768) norm_rope_pool_kernel(NormRopeParams p) {
         const float logit = rbf(lin + gbias);
         p.gate_out[gate_offset(p, b, t, h)] = f2bf(1.0f / (1.0f + expf(-logit)));
       }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      q[i] = qn[i];
+      k[i] = kn[i];
+      xv[i] = xn[i];
     }
   }
   if (POOL && active) {

@@ -25,6 +25,7 @@ from .rope import prepare_cos_sin
 
 BF16 = torch.bfloat16
 HEAD_DIM = 128
+FUSED_SELECT_MAX_NB = 832  # up to this many key blocks the scores stay on chip (no scores buffer)
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -58,17 +59,21 @@ def topk_count(topk_ratio: float, nb: int) -> int:
 
 
 def default_splits(B: int, H: int, L: int) -> int:
-    """Sequence splits of the low-rank C reduction: about two CTAs per SM."""
-    tiles = (L + 127) // 128
+    """Sequence splits of the low-rank C reduction: about two waves of two
+    CTAs per SM (64-token tiles)."""
+    tiles = (L + 63) // 64
     sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    return max(1, min(tiles, (2 * sms + B * H - 1) // (B * H)))
+    return max(1, min(tiles, round(4 * sms / (B * H))))
 
 
 # ---------------------------------------------------------------------------
 # fused B200 path
 # ---------------------------------------------------------------------------
-def qkv_gemm(x2d: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
-    """out[M, N] = x[M, K] w[N, K]^T (+ bias) on tcgen05 (bf16 in/out, fp32 accumulate)."""
+def qkv_gemm(x2d: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+             ssq: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M, N] = x[M, K] w[N, K]^T (+ bias) on tcgen05 (bf16 in/out, fp32 accumulate).
+    ``ssq`` (fp32 ``[M, N/256]``) receives each row's sum of squares of its bf16
+    outputs per 256-column tile."""
     _require_cuda(x2d, w, bias)
     if x2d.dtype != BF16 or w.dtype != BF16:
         raise ValueError("qkv_gemm: bf16 operands required")
@@ -80,7 +85,9 @@ def qkv_gemm(x2d: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = Non
         raise ValueError(f"qkv_gemm: weight {tuple(w.shape)} does not match x {tuple(x2d.shape)}")
     out = torch.empty(M, N, device=x2d.device, dtype=BF16)
     b = None if bias is None else bias.to(BF16).contiguous()
-    _lib.call("rola_b200_qkv_gemm", _ptr(x2d), _ptr(w), _ptr(b), _ptr(out), M, N, K, _stream())
+    if ssq is not None and (ssq.dtype != torch.float32 or ssq.shape != (M, N // 256) or not ssq.is_contiguous()):
+        raise ValueError("qkv_gemm: ssq must be a contiguous fp32 [M, N/256] tensor")
+    _lib.call("rola_b200_qkv_gemm", _ptr(x2d), _ptr(w), _ptr(b), _ptr(out), _ptr(ssq), M, N, K, _stream())
     return out
 
 
@@ -113,7 +120,7 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
     _lib.call("rola_b200_mean_pool", _ptr(k_rope), L * dim, HEAD_DIM, dim, B, H, L, blk, _ptr(center),
               _ptr(pooled_k), st)
     if lut is None:
-        scores = e(B * H, NB, NB, dt=torch.float32)
+        scores = e(B * H, NB, NB, dt=torch.float32) if NB > FUSED_SELECT_MAX_NB else None
         lut = e(B * H, NB, topk, dt=torch.int32)
         _lib.call("rola_b200_block_select", _ptr(pooled_q), _ptr(pooled_k), B * H, NB, NB, topk, _ptr(scores),
                   _ptr(lut), st)
@@ -147,11 +154,13 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
 def rola_attention_from_qkv(q_raw, k_raw, v_raw, x, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk,
                             proj_q, proj_k, gate_w, gate_b, num_heads: int, blk: int = 128, topk: int = 1,
                             eps: float = 1e-6, splits: int | None = None, keep: bool = False, lut=None,
-                            events: dict | None = None):
+                            events: dict | None = None, ssq: torch.Tensor | None = None):
     """RoLa forward from projected q/k/v (token-major ``[B, L, H*D]`` views
     with unit column stride; q and k share a row stride) to the gated output
     ``[B, L, H*D]``.  ``keep`` returns the intermediates too.  ``lut`` (int32
-    ``[B*H, NB, k]``) replaces the kernel's own selection.
+    ``[B*H, NB, k]``) replaces the kernel's own selection.  ``ssq`` are the QKV
+    GEMM's per-tile sums of squares (``qkv_gemm``), which make the norm pass a
+    pure stream.
     """
     _require_cuda(q_raw, k_raw, v_raw, x)
     B, L, dim = q_raw.shape
@@ -182,9 +191,10 @@ def rola_attention_from_qkv(q_raw, k_raw, v_raw, x, cos_sin, lr_cos, lr_sin, rop
     nwk = None if norm_wk is None else _bf16_vec(norm_wk, dim, "norm_wk")
     cos_sin = cos_sin.to(torch.float32).contiguous()
     xc = x.contiguous()
-    _lib.call("rola_b200_qk_norm_rope", _ptr(q_raw), _ptr(k_raw), q_raw.stride(1), _ptr(xc), _ptr(nwq),
-              _ptr(nwk), _ptr(cos_sin), _ptr(gw), _ptr(gb), B, L, H, blk, eps, _ptr(q_rope), _ptr(k_rope),
-              _ptr(q_normed), _ptr(k_normed), _ptr(gate), _ptr(pooled_q), _ptr(ksum), st)
+    ssq_ld = 0 if ssq is None else ssq.shape[-1]
+    _lib.call("rola_b200_qk_norm_rope", _ptr(q_raw), _ptr(k_raw), q_raw.stride(1), _ptr(ssq), ssq_ld, _ptr(xc),
+              _ptr(nwq), _ptr(nwk), _ptr(cos_sin), _ptr(gw), _ptr(gb), B, L, H, blk, eps, _ptr(q_rope),
+              _ptr(k_rope), _ptr(q_normed), _ptr(k_normed), _ptr(gate), _ptr(pooled_q), _ptr(ksum), st)
     res = head_local_attention(q_rope, k_rope, q_normed, k_normed, v_raw, gate, pooled_q, ksum, lr_cos, lr_sin,
                                rope_dim, proj_q, proj_k, H, blk, topk, splits, keep, lut, events)
     if not keep:
@@ -203,14 +213,15 @@ def rola_attention_core(x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm
     (sparkdiffusion/networks/wan_rola_attention.py:414-446).  ``w_qkv`` is the
     concatenated ``[Wq; Wk; Wv]`` of shape ``[3*dim, dim]``."""
     B, L, dim = x.shape
+    ssq = torch.empty(B * L, 3 * dim // 256, device=x.device, dtype=torch.float32)
     if events is not None:
         events["gemm"][0].record()
-    qkv = qkv_gemm(x.reshape(B * L, dim), w_qkv, b_qkv).view(B, L, 3 * dim)
+    qkv = qkv_gemm(x.reshape(B * L, dim), w_qkv, b_qkv, ssq).view(B, L, 3 * dim)
     if events is not None:
         events["gemm"][1].record()
     res = rola_attention_from_qkv(qkv[..., :dim], qkv[..., dim:2 * dim], qkv[..., 2 * dim:], x, cos_sin, lr_cos,
                                   lr_sin, rope_dim, norm_wq, norm_wk, proj_q, proj_k, gate_w, gate_b, num_heads,
-                                  blk, topk, eps, splits, keep, events=events)
+                                  blk, topk, eps, splits, keep, events=events, ssq=ssq)
     if keep:
         out, extra = res
         extra["qkv"] = qkv
@@ -285,7 +296,8 @@ def block_select(pooled_q: torch.Tensor, pooled_k: torch.Tensor, topk: int) -> t
     B, H, NBq, D = pooled_q.shape
     NBk = pooled_k.shape[2]
     pq, pk = pooled_q.contiguous(), pooled_k.contiguous()
-    scores = torch.empty(B * H, NBq, NBk, device=pq.device, dtype=torch.float32)
+    scores = (torch.empty(B * H, NBq, NBk, device=pq.device, dtype=torch.float32)
+              if NBk > FUSED_SELECT_MAX_NB else None)
     lut = torch.empty(B * H, NBq, topk, device=pq.device, dtype=torch.int32)
     _lib.call("rola_b200_block_select", _ptr(pq), _ptr(pk), B * H, NBq, NBk, topk, _ptr(scores), _ptr(lut),
               _stream())
@@ -338,7 +350,8 @@ def fused_qkv_gemm_rope(x, q_proj, k_proj, v_proj, freqs, norm_q_weight, norm_k_
     bias = None
     if q_proj.bias is not None:
         bias = torch.cat([q_proj.bias, k_proj.bias, v_proj.bias], 0).to(BF16)
-    qkv = qkv_gemm(x.reshape(B * L, dim), w, bias).view(B, L, 3 * dim)
+    ssq = torch.empty(B * L, 3 * dim // 256, device=x.device, dtype=torch.float32) if H % 2 == 0 else None
+    qkv = qkv_gemm(x.reshape(B * L, dim), w, bias, ssq).view(B, L, 3 * dim)
     if cos_sin is None:
         cos_sin = prepare_cos_sin(freqs, L, head_dim)
     e = lambda: torch.empty(B, L, dim, device=x.device, dtype=BF16)  # noqa: E731
@@ -346,7 +359,8 @@ def fused_qkv_gemm_rope(x, q_proj, k_proj, v_proj, freqs, norm_q_weight, norm_k_
     has_norm = norm_q_weight is not None and norm_k_weight is not None
     nwq = _bf16_vec(norm_q_weight, dim, "norm_q_weight") if has_norm else None
     nwk = _bf16_vec(norm_k_weight, dim, "norm_k_weight") if has_norm else None
-    _lib.call("rola_b200_qk_norm_rope", _ptr(qkv), _ptr(qkv[..., dim:]), 3 * dim, None, _ptr(nwq), _ptr(nwk),
+    _lib.call("rola_b200_qk_norm_rope", _ptr(qkv), _ptr(qkv[..., dim:]), 3 * dim, _ptr(ssq if has_norm else None),
+              0 if ssq is None else ssq.shape[-1], None, _ptr(nwq), _ptr(nwk),
               _ptr(cos_sin.to(torch.float32).contiguous()), None, None, B, L, H, 128, eps, _ptr(q_rope),
               _ptr(k_rope), _ptr(q_n), _ptr(k_n), None, None, None, _stream())
 

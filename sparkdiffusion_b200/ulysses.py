@@ -69,9 +69,10 @@ def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin
         raise ValueError("cos_sin must cover the full (global) sequence")
     dev = x_local.device
     st = _stream()
+    ssq = torch.empty(B * Ls, 3 * dim // 256, device=dev, dtype=torch.float32)
     if events is not None:
         events["gemm"][0].record()
-    qkv = ops.qkv_gemm(x_local.reshape(B * Ls, dim), w_qkv, b_qkv)
+    qkv = ops.qkv_gemm(x_local.reshape(B * Ls, dim), w_qkv, b_qkv, ssq)
     if events is not None:
         events["gemm"][1].record()
     q_send = torch.empty(B, p, Ls, Hl * HEAD_DIM, device=dev, dtype=BF16)
@@ -81,7 +82,8 @@ def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin
     gw = _bf16_vec(gate_w, HEAD_DIM, "gate_w")
     gb = _bf16_vec(gate_b, H, "gate_b")
     xc = x_local.contiguous()
-    _lib.call("rola_b200_qk_norm_pack", _ptr(qkv), _ptr(qkv[:, dim:]), _ptr(qkv[:, 2 * dim:]), 3 * dim, _ptr(xc),
+    _lib.call("rola_b200_qk_norm_pack", _ptr(qkv), _ptr(qkv[:, dim:]), _ptr(qkv[:, 2 * dim:]), 3 * dim, _ptr(ssq),
+              ssq.shape[-1], _ptr(xc),
               _ptr(_bf16_vec(norm_wq, dim, "norm_wq")), _ptr(_bf16_vec(norm_wk, dim, "norm_wk")), _ptr(gw),
               _ptr(gb), B, Ls, H, Hl, eps, _ptr(q_send), _ptr(k_send), _ptr(v_send), _ptr(g_send), st)
     q_n, w1 = seq_to_head(q_send, group, async_op=True)

@@ -42,7 +42,7 @@ def test_abi_version_and_validation_without_gpu():
     assert lib.rola_b200_abi_version() == _lib.ABI_VERSION
     # argument validation runs on the host before any launch: a bad size is
     # rejected with ROLA_ERR_INVALID and a message, no GPU needed
-    rc = lib.rola_b200_qkv_gemm(None, None, None, None, 0, 0, 0, None)
+    rc = lib.rola_b200_qkv_gemm(None, None, None, None, None, 0, 0, 0, None)
     assert rc == _lib.ROLA_ERR_INVALID
     assert b"null pointer" in lib.rola_b200_last_error()
     rc = lib.rola_b200_block_select(ctypes.c_void_p(16), ctypes.c_void_p(16), 1, 4, 4, 9, ctypes.c_void_p(16),
