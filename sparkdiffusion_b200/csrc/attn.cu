@@ -7,43 +7,59 @@
 // columns past L masked to -inf for a partial block, base-2 online softmax,
 // P rounded to bf16 before P.V, o = acc / l.  The epilogue then restates
 // o_lr = q_lr . C (fused_lowrank.py:360-362) and `_gate_fusion_kernel`
-// (fused_gate.py:67-127), storing the gated output [B, L, H*D] directly.
+// (fused_gate.py:67-127), storing the gated output directly.
 //
-// One CTA per (query block, batch*head), 6 warps:
-//   warp 0      TMA producer: Q once, then K_j and V_j (two 64-column boxes
-//               each) into a 2-stage ring, gathered by LUT block index; the
-//               low-rank operands q_lr and C^T for the epilogue.
-//   warp 1      TMEM owner and MMA issuer (one elected thread):
-//               S_i = Q K_i^T into one of two TMEM S buffers, O += P_i V_i.
-//   warps 2..5  softmax: thread = query row = TMEM lane; reads S from TMEM,
-//               keeps the running max/sum, writes P (bf16, 128B-swizzled) to
-//               shared memory, rescales O in TMEM when the running max grows
-//               by more than `rescale_threshold` (log2 units; 0 = every growth,
-//               exactly the reference's recurrence; larger values keep a stale
-//               max, which leaves acc / l unchanged but moves the bf16
-//               rounding of P), and finally runs the epilogue.
-// TMEM columns: S0 [0,128), S1 [128,256), O [256,384); o_lr reuses S0.
+// One CTA per (pair of query blocks, batch*head): the two 128-row tiles A and
+// B have their own LUT rows and run ping-pong, so the tensor core executes one
+// tile's MMAs while the other tile's softmax runs.  Three warpgroups with
+// registers rebalanced by setmaxnreg (launch: 384 threads x 168):
+//   WG0 (56 regs)   warp 0 lane 0: TMA producer.  Q of both tiles once, then
+//                   the K and V blocks of both LUTs through one 5-slot ring in
+//                   exactly the order the MMAs consume them (K_A0 K_B0 | V_A0
+//                   K_A1 V_B0 K_B1 | ...), then the epilogue operands (q_lr
+//                   tiles and C^T).  No multicast.
+//                   warp 1: TMEM owner and MMA issuer (one elected thread):
+//                   S = Q K^T (smem x smem) and O += P V with P read from TMEM
+//                   (tcgen05.mma with the A operand in tensor memory).
+//   WG1, WG2 (224)  softmax of tile A / tile B: thread = query row = TMEM lane.
+//                   Per KV block the whole S row is loaded at once, the row max
+//                   taken, P = exp2(s*scale - m) written back over the S
+//                   columns as packed bf16, and O rescaled in TMEM when the
+//                   running max grew by more than `rescale_threshold` (0 = every
+//                   growth: the reference's recurrence exactly); then the
+//                   fused epilogue.
+// TMEM columns: S/P of tile t at [128 t, 128 t + 128), O of tile t at
+// [256 + 128 t, ...); the epilogue's o_lr reuses the S columns.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace rola {
 
 namespace attn {
-constexpr int THREADS = 192;
-constexpr int TILE = 16384;  // one [128 rows x 64 bf16] box, 128B swizzle
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = 2 * TILE;        // 2 stages x 2 boxes
-constexpr int OFF_V = OFF_K + 4 * TILE;
-constexpr int OFF_P = OFF_V + 4 * TILE;
-constexpr int OFF_E = OFF_P + 2 * TILE;  // q_lr box, C^T box
-constexpr int OFF_BAR = OFF_E + 2 * TILE;
+constexpr int THREADS = 384;
+constexpr int LAUNCH_REGS = 168;            // 65536 / 384, rounded down to 8
+constexpr int REGS_LOAD = 56, REGS_SOFTMAX = 224;
+static_assert(128 * REGS_LOAD + 2 * 128 * REGS_SOFTMAX <= THREADS * LAUNCH_REGS, "register split exceeds the pool");
+constexpr int TILE = 16384;                 // one [128 rows x 64 bf16] box, 128B swizzle
+constexpr int SLOT = 2 * TILE;              // one 128x128 K or V block
+constexpr int NSLOTS = 5;
+constexpr int OFF_Q = 0;                    // 2 tiles x 2 boxes
+constexpr int OFF_RING = 4 * TILE;          // 5 slots
+constexpr int OFF_BAR = OFF_RING + NSLOTS * SLOT;  // 224 KB
 constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 }  // namespace attn
 
 // barrier slots
 enum : int {
-  B_Q = 0, B_KF0, B_KF1, B_VF0, B_VF1, B_KVE0, B_KVE1, B_SF0, B_SF1, B_SFREE0, B_SFREE1,
-  B_PF, B_OF, B_EPI, B_LR, B_DRAIN, B_COUNT
+  B_Q = 0,
+  B_FULL0,                       // ring slot s full (TMA): B_FULL0 + s
+  B_EMPTY0 = B_FULL0 + 5,        // ring slot s consumed (MMA commit): B_EMPTY0 + s
+  B_SF0 = B_EMPTY0 + 5, B_SF1,   // S of tile t ready (MMA -> softmax)
+  B_PF0, B_PF1,                  // P of tile t in TMEM and O rescaled (softmax -> MMA), 4 arrivals
+  B_OF0, B_OF1,                  // last P V of tile t complete
+  B_LR0, B_LR1,                  // o_lr of tile t in TMEM
+  B_DRAIN,
+  B_COUNT
 };
 
 __device__ __forceinline__ int lut_block(const AttnParams& p, const int32_t* lut_row, int i) {
@@ -70,27 +86,24 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 8 * B_COUNT + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m = blockIdx.x, bh = blockIdx.y;
+  const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
+  const int m0 = 2 * blockIdx.x;
+  const int nt = (m0 + 1 < p.NBq) ? 2 : 1;  // active tiles
   const int topk = p.topk;
-  const int32_t* lut_row = p.lut + ((int64_t)bh * p.NBq + m) * topk;
 
   if (threadIdx.x == 0) {
     mbar_init(bar(B_Q), 1);
-    mbar_init(bar(B_KF0), 1);
-    mbar_init(bar(B_KF1), 1);
-    mbar_init(bar(B_VF0), 1);
-    mbar_init(bar(B_VF1), 1);
-    mbar_init(bar(B_KVE0), 1);
-    mbar_init(bar(B_KVE1), 1);
-    mbar_init(bar(B_SF0), 1);
-    mbar_init(bar(B_SF1), 1);
-    mbar_init(bar(B_SFREE0), 4);
-    mbar_init(bar(B_SFREE1), 4);
-    mbar_init(bar(B_PF), 4);
-    mbar_init(bar(B_OF), 1);
-    mbar_init(bar(B_EPI), 1);
-    mbar_init(bar(B_LR), 1);
+    for (int s = 0; s < NSLOTS; ++s) {
+      mbar_init(bar(B_FULL0 + s), 1);
+      mbar_init(bar(B_EMPTY0 + s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(B_SF0 + t), 1);
+      mbar_init(bar(B_PF0 + t), 4);
+      mbar_init(bar(B_OF0 + t), 1);
+      mbar_init(bar(B_LR0 + t), 1);
+    }
     mbar_init(bar(B_DRAIN), 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -110,42 +123,64 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS[2] = {tmem, tmem + 128};
-  const uint32_t tO = tmem + 256;
+  auto slot_addr = [&](int r) { return base + OFF_RING + (r % NSLOTS) * SLOT; };
 
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_LOAD));
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA
-    if (elect_one()) {
-      mbar_expect_tx(bar(B_Q), 2 * TILE);
-      tma_load_4d(base + OFF_Q, &tq, bar(B_Q), 0, m * 128, h, b);
-      tma_load_4d(base + OFF_Q + TILE, &tq, bar(B_Q), 64, m * 128, h, b);
-      if (p.has_lowrank) {
-        mbar_expect_tx(bar(B_EPI), 2 * TILE);
-        tma_load_4d(base + OFF_E, &tqlr, bar(B_EPI), 0, m * 128, h, b);
-        tma_load_3d(base + OFF_E + TILE, &tct, bar(B_EPI), 0, 0, bh);
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA
+      mbar_expect_tx(bar(B_Q), nt * 2 * TILE);
+      for (int t = 0; t < nt; ++t) {
+        tma_load_4d(base + OFF_Q + t * 2 * TILE, &tq, bar(B_Q), 0, (m0 + t) * 128, h, b);
+        tma_load_4d(base + OFF_Q + t * 2 * TILE + TILE, &tq, bar(B_Q), 64, (m0 + t) * 128, h, b);
       }
-      int issued = 0;
-      for (int i = 0; i < topk; ++i) {
-        const int s = i & 1;
-        if (!mbar_wait(bar(B_KVE0 + s), ((i >> 1) & 1) ^ 1, abort_flag, kDevTimeoutMma)) break;
-        const int j = lut_block(p, lut_row, i);
-        const uint32_t sk = base + OFF_K + s * 2 * TILE;
-        const uint32_t sv = base + OFF_V + s * 2 * TILE;
-        mbar_expect_tx(bar(B_KF0 + s), 2 * TILE);
-        tma_load_4d(sk, &tk, bar(B_KF0 + s), 0, j * 128, h, b);
-        tma_load_4d(sk + TILE, &tk, bar(B_KF0 + s), 64, j * 128, h, b);
-        mbar_expect_tx(bar(B_VF0 + s), 2 * TILE);
-        tma_load_4d(sv, &tv, bar(B_VF0 + s), 0, j * 128, h, b);
-        tma_load_4d(sv + TILE, &tv, bar(B_VF0 + s), 64, j * 128, h, b);
-        ++issued;
+      int r = 0;
+      bool ok = true;
+      // one ring entry: wait until its slot is free, then issue its loads
+      auto acquire = [&](int bytes) -> uint32_t {
+        const int s = r % NSLOTS;
+        if (!mbar_wait(bar(B_EMPTY0 + s), ((r / NSLOTS) & 1) ^ 1, abort_flag, kDevTimeoutMma)) {
+          ok = false;
+          return 0;
+        }
+        mbar_expect_tx(bar(B_FULL0 + s), bytes);
+        return slot_addr(r);
+      };
+      auto load_block = [&](const CUtensorMap* m, int t, int i) {
+        const uint32_t dst = acquire(SLOT);
+        if (!ok) return;
+        const int s = r % NSLOTS;
+        const int j = lut_block(p, p.lut + ((int64_t)bh * p.NBq + m0 + t) * topk, i);
+        tma_load_4d(dst, m, bar(B_FULL0 + s), 0, j * 128, h, b);
+        tma_load_4d(dst + TILE, m, bar(B_FULL0 + s), 64, j * 128, h, b);
+        ++r;
+      };
+      for (int t = 0; t < nt && ok; ++t) load_block(&tk, t, 0);
+      for (int i = 0; i < topk && ok; ++i) {
+        for (int t = 0; t < nt && ok; ++t) {
+          load_block(&tv, t, i);
+          if (ok && i + 1 < topk) load_block(&tk, t, i + 1);
+        }
+      }
+      if (ok && p.has_lowrank) {
+        // epilogue operands: q_lr of each tile in one slot, C^T in the next
+        uint32_t dst = acquire(nt * TILE);
+        if (ok) {
+          const int s = r % NSLOTS;
+          for (int t = 0; t < nt; ++t) tma_load_4d(dst + t * TILE, &tqlr, bar(B_FULL0 + s), 0, (m0 + t) * 128, h, b);
+          ++r;
+        }
+        if (ok) dst = acquire(TILE);
+        if (ok) {
+          tma_load_3d(dst, &tct, bar(B_FULL0 + r % NSLOTS), 0, 0, bh);
+          ++r;
+        }
       }
       // drain: no TMA may still target shared memory when the CTA exits
       mbar_wait(bar(B_Q), 0, abort_flag, kDevTimeoutLoad);
-      if (p.has_lowrank) mbar_wait(bar(B_EPI), 0, abort_flag, kDevTimeoutLoad);
-      for (int i = max(0, issued - 2); i < issued; ++i) {
-        mbar_wait(bar(B_KF0 + (i & 1)), (i >> 1) & 1, abort_flag, kDevTimeoutLoad);
-        mbar_wait(bar(B_VF0 + (i & 1)), (i >> 1) & 1, abort_flag, kDevTimeoutLoad);
-      }
+      for (int n = max(0, r - NSLOTS); n < r; ++n)
+        mbar_wait(bar(B_FULL0 + n % NSLOTS), (n / NSLOTS) & 1, abort_flag, kDevTimeoutLoad);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA
@@ -153,220 +188,222 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       const uint32_t id_qk = idesc_bf16_f32(128, 128, false, false);
       const uint32_t id_pv = idesc_bf16_f32(128, 128, false, true);
       bool ok = mbar_wait(bar(B_Q), 0, abort_flag, kDevTimeoutLoad);
-      auto issue_pv = [&](int i) -> bool {
-        const int s = i & 1;
-        if (!mbar_wait(bar(B_PF), i & 1, abort_flag, kDevTimeoutSoftmax)) return false;
-        if (!mbar_wait(bar(B_VF0 + s), (i >> 1) & 1, abort_flag, kDevTimeoutLoad)) return false;
-        tc_fence_after();
-        const uint32_t sv = base + OFF_V + s * 2 * TILE;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t da = sdesc_sw128(base + OFF_P + (kk >> 2) * TILE + (kk & 3) * 32, 16, 1024);
-          const uint64_t db = sdesc_sw128(sv + kk * 2048, TILE, 1024);
-          mma_bf16_ss(tO, da, db, id_pv, (i > 0 || kk > 0) ? 1u : 0u);
+      int r = 0;
+      // next ring entry (consumption order = load order)
+      auto pop = [&]() -> int {
+        const int s = r % NSLOTS;
+        if (!mbar_wait(bar(B_FULL0 + s), (r / NSLOTS) & 1, abort_flag, kDevTimeoutLoad)) {
+          ok = false;
+          return -1;
         }
-        mma_commit(bar(B_KVE0 + s));
-        mma_commit(bar(B_OF));
-        return true;
-      };
-      for (int i = 0; i < topk && ok; ++i) {
-        const int s = i & 1;
-        ok = mbar_wait(bar(B_KF0 + s), (i >> 1) & 1, abort_flag, kDevTimeoutLoad) &&
-             mbar_wait(bar(B_SFREE0 + s), ((i >> 1) & 1) ^ 1, abort_flag, kDevTimeoutSoftmax);
-        if (!ok) break;
         tc_fence_after();
-        const uint32_t sk = base + OFF_K + s * 2 * TILE;
+        return r++;
+      };
+      auto issue_s = [&](int t) {
+        const int e = pop();
+        if (e < 0) return;
+        const uint32_t sq = base + OFF_Q + t * 2 * TILE;
+        const uint32_t sk = slot_addr(e);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * TILE + (kk & 3) * 32;
-          mma_bf16_ss(tS[s], sdesc_sw128(base + OFF_Q + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), id_qk,
+          mma_bf16_ss(tmem + 128 * t, sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), id_qk,
                       kk > 0 ? 1u : 0u);
         }
-        mma_commit(bar(B_SF0 + s));
-        if (i >= 1) ok = issue_pv(i - 1);
-      }
-      if (ok) ok = issue_pv(topk - 1);
-      if (ok && p.has_lowrank) {
-        // o_lr = q_lr . C into S0 once the softmax released the last S0 use
-        const int last0 = ((topk - 1) & 1) == 0 ? topk - 1 : topk - 2;
-        ok = mbar_wait(bar(B_EPI), 0, abort_flag, kDevTimeoutLoad) &&
-             mbar_wait(bar(B_SFREE0), (last0 >> 1) & 1, abort_flag, kDevTimeoutSoftmax);
-        if (ok) {
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            mma_bf16_ss(tS[0], sdesc_sw128(base + OFF_E + kk * 32, 16, 1024),
-                        sdesc_sw128(base + OFF_E + TILE + kk * 32, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
+        mma_commit(bar(B_EMPTY0 + e % NSLOTS));
+        mma_commit(bar(B_SF0 + t));
+      };
+      for (int t = 0; t < nt && ok; ++t) issue_s(t);
+      for (int i = 0; i < topk && ok; ++i) {
+        for (int t = 0; t < nt && ok; ++t) {
+          if (!mbar_wait(bar(B_PF0 + t), i & 1, abort_flag, kDevTimeoutSoftmax)) {
+            ok = false;
+            break;
           }
-          mma_commit(bar(B_LR));
+          const int e = pop();
+          if (e < 0) break;
+          const uint32_t sv = slot_addr(e);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            // A = P from TMEM (16 bf16 of K = 8 packed columns per step), B = V (MN-major)
+            mma_bf16_ts(tmem + 256 + 128 * t, tmem + 128 * t + kk * 8, sdesc_sw128(sv + kk * 2048, TILE, 1024),
+                        id_pv, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(bar(B_EMPTY0 + e % NSLOTS));
+          if (i + 1 < topk) {
+            issue_s(t);  // overwrites P_t(i) in TMEM after P_t(i) V_t(i) in issue order
+          } else {
+            mma_commit(bar(B_OF0 + t));
+          }
+        }
+      }
+      if (ok && p.has_lowrank) {
+        const int e0 = pop();
+        const int e1 = ok ? pop() : -1;
+        if (ok) {
+          for (int t = 0; t < nt; ++t) {
+            // o_lr = q_lr . C into the (now free) S columns of tile t
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              mma_bf16_ss(tmem + 128 * t, sdesc_sw128(slot_addr(e0) + t * TILE + kk * 32, 16, 1024),
+                          sdesc_sw128(slot_addr(e1) + kk * 32, 16, 1024), id_qk, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(bar(B_LR0 + t));
+          }
         }
       }
       mma_commit(bar(B_DRAIN));
       mbar_wait(bar(B_DRAIN), 0, abort_flag, kDevTimeoutMma);
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_SOFTMAX));
     // -------------------------------------------------------------- softmax
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    const float scale = p.qk_scale;
-    float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
-    uint8_t* sP = gbase + OFF_P;
-    for (int i = 0; i < topk; ++i) {
-      const int s = i & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(B_SF0 + s), (i >> 1) & 1, abort_flag, kDevTimeoutMma))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t sv[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS[s] + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_SFREE0 + s));
-
-      const int j = lut_block(p, lut_row, i);
-      const int valid = p.L - j * 128;
-      float mx = -INFINITY;
-      if (valid < 128) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          if (c >= valid) sv[c] = __float_as_uint(-INFINITY);
-        }
-      }
-#pragma unroll
-      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sv[c]));
-      const float m_new = fmaxf(m_run, mx * scale);
-      float m_use = m_run, alpha = 1.f;
-      bool rescale = false;
-      if (i == 0) {
-        m_use = m_new;
-      } else if (m_new - m_run > p.rescale_threshold) {
-        m_use = m_new;
-        alpha = ex2_approx(m_run - m_new);
-        rescale = true;
-      }
-      float rs = 0.f;
-      uint32_t pk[64];
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * c]), scale, -m_use));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * c + 1]), scale, -m_use));
-        rs += p0 + p1;
-        pk[c] = pack_bf2(p0, p1);
-      }
-      l_run = l_run * alpha + rs;
-      m_run = m_use;
-
-      if (i >= 1) {
-        // P buffer and O are in use by P_{i-1} V_{i-1} until it completes
-        if (!__all_sync(0xffffffffu, mbar_wait(bar(B_OF), (i - 1) & 1, abort_flag, kDevTimeoutMma))) {
+    const int t = (warp - 4) >> 2;  // tile of this warpgroup
+    const int q = warp & 3;         // TMEM lane quadrant of this warp
+    if (t < nt) {
+      const int row = q * 32 + lane;
+      const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+      const uint32_t tS = tmem + 128 * t + lane_off;
+      const uint32_t tO = tmem + 256 + 128 * t + lane_off;
+      const int32_t* lut_row = p.lut + ((int64_t)bh * p.NBq + m0 + t) * topk;
+      const float scale = p.qk_scale;
+      float m_run = -INFINITY, l_run = 0.f;
+      bool ok = true;
+      for (int i = 0; i < topk; ++i) {
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(B_SF0 + t), i & 1, abort_flag, kDevTimeoutMma))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
+        const int j = lut_block(p, lut_row, i);
+        const int valid = p.L - j * 128;
+        // the whole S row: four 32-column loads, one wait
+        uint32_t v[128];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t ov[32];
-            tmem_ld32(tO + lane_off + c * 32, ov);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-            tmem_st32(tO + lane_off + c * 32, ov);
-          }
-          tmem_st_wait();
-        }
-      }
-      // P row -> shared memory, 128B-swizzled K-major layout (two 64-column boxes)
-#pragma unroll
-      for (int c16 = 0; c16 < 16; ++c16) {
-        const int box = c16 >> 3, chunk = c16 & 7;
-        uint4 u = make_uint4(pk[4 * c16], pk[4 * c16 + 1], pk[4 * c16 + 2], pk[4 * c16 + 3]);
-        *reinterpret_cast<uint4*>(sP + box * TILE + row * 128 + ((chunk ^ (row & 7)) << 4)) = u;
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(B_PF));
-    }
-
-    // ------------------------------------------------------------ epilogue
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_OF), (topk - 1) & 1, abort_flag, kDevTimeoutMma));
-    tc_fence_after();
-    bool lowrank = false;
-    if (ok && p.has_lowrank)
-      lowrank = __all_sync(0xffffffffu, mbar_wait(bar(B_LR), 0, abort_flag, kDevTimeoutMma));
-    ok = ok && (lowrank || !p.has_lowrank);
-    if (ok) {
-      tc_fence_after();
-      const int t = m * 128 + row;
-      const float inv_l = 1.0f / l_run;
-      // pass 1: row statistics of o_sparse (bf16 chain) and of o_lr
-      float ss_os = 0.f, ss_lr = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t ov[32];
-        tmem_ld32(tO + lane_off + c * 32, ov);
-        uint32_t lv[32];
-        if (lowrank) tmem_ld32(tS[0] + lane_off + c * 32, lv);
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
         tmem_ld_wait();
+        if (valid < 128) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float os = rbf(__uint_as_float(ov[e]) * inv_l);
-          ss_os += rbf(os * os);
-          if (lowrank) {
-            const float lr = rbf(__uint_as_float(lv[e]));
-            ss_lr = fmaf(lr, lr, ss_lr);
+          for (int c = 0; c < 128; ++c)
+            if (c >= valid) v[c] = __float_as_uint(-INFINITY);
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(v[c]));
+        const float m_new = fmaxf(m_run, mx * scale);
+        float m_use = m_run, alpha = 1.f;
+        bool rescale = false;
+        if (i == 0) {
+          m_use = m_new;
+        } else if (m_new - m_run > p.rescale_threshold) {
+          m_use = m_new;
+          alpha = ex2_approx(m_run - m_new);
+          rescale = true;
+        }
+        // P = exp2(s*scale - m), packed bf16 over the S columns (already in registers)
+        float rs = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t w[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = ex2_approx(fmaf(__uint_as_float(v[32 * c + 2 * e]), scale, -m_use));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(v[32 * c + 2 * e + 1]), scale, -m_use));
+            rs += p0 + p1;
+            w[e] = pack_bf2(p0, p1);
+          }
+          tmem_st16(tS + c * 16, w);
+        }
+        // O of this tile is stable: its last P V completed before this S (in-order MMAs)
+        if (__any_sync(0xffffffffu, rescale)) {
+          uint32_t ov[128];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tmem_ld32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[c * 32]));
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 128; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tmem_st32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[c * 32]));
+        }
+        tmem_st_wait();
+        l_run = l_run * alpha + rs;
+        m_run = m_use;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_PF0 + t));
+      }
+
+      // ---------------------------------------------------------- epilogue
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_OF0 + t), 0, abort_flag, kDevTimeoutMma));
+      bool lowrank = false;
+      if (ok && p.has_lowrank)
+        lowrank = __all_sync(0xffffffffu, mbar_wait(bar(B_LR0 + t), 0, abort_flag, kDevTimeoutMma));
+      ok = ok && (lowrank || !p.has_lowrank);
+      tc_fence_after();
+      if (ok) {
+        const int tok = (m0 + t) * 128 + row;
+        const float inv_l = 1.0f / l_run;
+        // pass 1: row statistics of o_sparse (bf16 chain) and of o_lr (16-column chunks)
+        float ss_os = 0.f, ss_lr = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          uint32_t ov[16];
+          tmem_ld16(tO + c * 16, ov);
+          uint32_t lv[16];
+          if (lowrank) tmem_ld16(tS + c * 16, lv);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float os = rbf(__uint_as_float(ov[e]) * inv_l);
+            ss_os += rbf(os * os);
+            if (lowrank) {
+              const float lr = rbf(__uint_as_float(lv[e]));
+              ss_lr = fmaf(lr, lr, ss_lr);
+            }
           }
         }
-      }
-      float os_rms = 1.f, lr_scale = 0.f, gate = 0.f;
-      if (lowrank) {
-        const float os_mean = rbf(ss_os * (1.0f / 128.0f));
-        const float os_mean_eps = rbf(os_mean + 1e-5f);
-        os_rms = rbf(sqrtf(os_mean_eps));
-        lr_scale = rsqrtf(ss_lr * (1.0f / 128.0f) + p.eps_lr);
-        gate = (p.gate != nullptr && t < p.L) ? bf2f(p.gate[((int64_t)b * p.L + t) * p.H + h]) : 0.f;
-      }
-      // pass 2: fuse and store (TMEM loads by the whole warp, stores only for rows < L)
-      const bool store = t < p.L;
-      {
-        const int64_t orow = (int64_t)b * p.o_sB + (int64_t)h * p.o_sH + (int64_t)t * p.o_sT;
+        float os_rms = 1.f, lr_scale = 0.f, gate = 0.f;
+        if (lowrank) {
+          const float os_mean = rbf(ss_os * (1.0f / 128.0f));
+          const float os_mean_eps = rbf(os_mean + 1e-5f);
+          os_rms = rbf(sqrtf(os_mean_eps));
+          lr_scale = rsqrtf(ss_lr * (1.0f / 128.0f) + p.eps_lr);
+          gate = (p.gate != nullptr && tok < p.L) ? bf2f(p.gate[((int64_t)b * p.L + tok) * p.H + h]) : 0.f;
+        }
+        // pass 2: fuse and store (TMEM loads by the whole warp, stores only for rows < L)
+        const bool store = tok < p.L;
+        const int64_t orow = (int64_t)b * p.o_sB + (int64_t)h * p.o_sH + (int64_t)tok * p.o_sT;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ov[32];
-          tmem_ld32(tO + lane_off + c * 32, ov);
-          uint32_t lv[32];
-          if (lowrank) tmem_ld32(tS[0] + lane_off + c * 32, lv);
+        for (int c = 0; c < 8; ++c) {
+          uint32_t ov[16];
+          tmem_ld16(tO + c * 16, ov);
+          uint32_t lv[16];
+          if (lowrank) tmem_ld16(tS + c * 16, lv);
           tmem_ld_wait();
-          float os[32], fo[32];
+          uint32_t wo[8], ws[8];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            os[e] = rbf(__uint_as_float(ov[e]) * inv_l);
+          for (int e = 0; e < 8; ++e) {
+            float os0 = rbf(__uint_as_float(ov[2 * e]) * inv_l);
+            float os1 = rbf(__uint_as_float(ov[2 * e + 1]) * inv_l);
+            ws[e] = pack_bf2(os0, os1);
             if (lowrank) {
-              const float lrn = rbf(rbf(__uint_as_float(lv[e])) * lr_scale);
-              fo[e] = (os[e] / os_rms + gate * lrn) * os_rms;
+              const float l0 = rbf(rbf(__uint_as_float(lv[2 * e])) * lr_scale);
+              const float l1 = rbf(rbf(__uint_as_float(lv[2 * e + 1])) * lr_scale);
+              wo[e] = pack_bf2((os0 / os_rms + gate * l0) * os_rms, (os1 / os_rms + gate * l1) * os_rms);
             } else {
-              fo[e] = os[e];
+              wo[e] = ws[e];
             }
           }
           if (p.out && store) {
-            uint4* dst = reinterpret_cast<uint4*>(p.out + orow + c * 32);
-#pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4)
-              dst[v4] = make_uint4(pack_bf2(fo[8 * v4], fo[8 * v4 + 1]), pack_bf2(fo[8 * v4 + 2], fo[8 * v4 + 3]),
-                                   pack_bf2(fo[8 * v4 + 4], fo[8 * v4 + 5]), pack_bf2(fo[8 * v4 + 6], fo[8 * v4 + 7]));
+            uint4* dst = reinterpret_cast<uint4*>(p.out + orow + c * 16);
+            dst[0] = make_uint4(wo[0], wo[1], wo[2], wo[3]);
+            dst[1] = make_uint4(wo[4], wo[5], wo[6], wo[7]);
           }
           if (p.o_sparse && store) {
-            uint4* dst = reinterpret_cast<uint4*>(p.o_sparse + orow + c * 32);
-#pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4)
-              dst[v4] = make_uint4(pack_bf2(os[8 * v4], os[8 * v4 + 1]), pack_bf2(os[8 * v4 + 2], os[8 * v4 + 3]),
-                                   pack_bf2(os[8 * v4 + 4], os[8 * v4 + 5]), pack_bf2(os[8 * v4 + 6], os[8 * v4 + 7]));
+            uint4* dst = reinterpret_cast<uint4*>(p.o_sparse + orow + c * 16);
+            dst[0] = make_uint4(ws[0], ws[1], ws[2], ws[3]);
+            dst[1] = make_uint4(ws[4], ws[5], ws[6], ws[7]);
           }
         }
       }
@@ -384,8 +421,17 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
 int launch_sparse_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tqlr,
                        const CUtensorMap& tct, const AttnParams& p, cudaStream_t s) {
   using namespace attn;
+  // setmaxnreg redistributes the block's launch registers; refuse to launch if
+  // the compiled kernel holds fewer than the split needs (the increase would wait)
+  static int launch_regs = -1;
+  if (launch_regs < 0) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, sparse_attn_tcgen05) != cudaSuccess) return (int)cudaGetLastError();
+    launch_regs = fa.numRegs;
+  }
+  if (launch_regs < LAUNCH_REGS) return -1;
   cudaFuncSetAttribute(sparse_attn_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  dim3 grid(p.NBq, p.B * p.H);
+  dim3 grid((p.NBq + 1) / 2, p.B * p.H);
   sparse_attn_tcgen05<<<grid, THREADS, SMEM_BYTES, s>>>(tq, tk, tv, tqlr, tct, p);
   return (int)cudaGetLastError();
 }
