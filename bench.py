@@ -238,8 +238,20 @@ def main():
     dev = torch.device("cuda", local_rank)
     group = None
     if world > 1:
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=180),
-                                device_id=dev)
+        # NCCL may print its banner on stdout while the communicator is created;
+        # keep stdout for the one JSON line by pointing fd 1 at stderr meanwhile
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=180),
+                                    device_id=dev)
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     _lib.load_library()
@@ -370,7 +382,8 @@ def main():
                 "peak_kind": f"{peak_kind} bf16 sustained", "traffic": tr,
                 "ms_per_launch": t_gemm if name == "gemm" else t_attn}
 
-    launches_per_step = 10 if world == 1 else 11
+    # gemm, norm(+pack), [rope_pool], centre, pooled k, select, lowrank_kv (+ reduce), lowrank_q, attention
+    launches_per_step = 9 if world == 1 else 10
     line = {
         "metric": METRIC, "value": flops_total / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": ms, "ms_per_layer": ms, "higher_is_better": True,

@@ -114,7 +114,7 @@ int rola_b200_center_from_sums(const float* ksum, int B, int NB, int dim, int L,
 /* (a7) pooled scores (fp32) and top-k selection: pooled_q [BH, NBq, D],
  * pooled_k [BH, NBk, D] bf16 -> lut [BH, NBq, topk] int32 ascending, ties toward
  * the lower block index.  scores_ws: fp32 scratch of BH*NBq*NBk floats, used
- * only when NBk > 832 (below that the scores stay on chip; NULL is allowed).
+ * only when NBk > 768 (below that the scores stay on chip; NULL is allowed).
  * Replaces `pooled_q @ pooled_k^T` + torch.topk (fused_sparse_attn.py:181-198). */
 int rola_b200_block_select(const void* pooled_q, const void* pooled_k, int BH, int NBq, int NBk, int topk,
                            float* scores_ws, int32_t* lut, rola_stream_t stream);
@@ -141,14 +141,18 @@ int rola_b200_lowrank_kv(const void* k_normed, int64_t k_sB, int64_t k_sH, int64
  * epilogue.  q and k share strides (qk_s*), v has its own (v_s*), out and
  * o_sparse share o_s*: element (b, h, t, d) at p + sB*b + sH*h + sT*t + d, all
  * strides multiples of 8 elements.  lut [B*H, NBq, topk] int32; q_lr [B*L, H*R]
- * and Ct [B*H, D, R] (both NULL: no low-rank branch and out = o_sparse);
- * gate [B*L, H] bf16 (NULL: gate 0).  out / o_sparse may be NULL (not both).
+ * and Ct [B*H, D, R] (both NULL: no low-rank branch and out = o_sparse).  The
+ * gate is either given as values, gate [B*L, H] bf16, or computed in the
+ * epilogue from the hidden states x (strided like q, x_s*) with gate_w [D] and
+ * gate_b [H] bf16 (give one of gate / x; neither: gate 0).  out / o_sparse may
+ * be NULL (not both).
  * blk == 128, R == 64.
  * Replaces _rola_fwd_kernel (fused_sparse_attn.py:55-144), the o_lr matmul
  * (fused_lowrank.py:360-362) and _gate_fusion_kernel (fused_gate.py:27-127). */
 int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT, const void* v,
                           int64_t v_sB, int64_t v_sH, int64_t v_sT, const int32_t* lut, int B, int L, int H, int blk,
-                          int topk, const void* q_lr, const void* Ct, const void* gate, float eps_lr, void* out,
+                          int topk, const void* q_lr, const void* Ct, const void* gate, const void* x, int64_t x_sB,
+                          int64_t x_sH, int64_t x_sT, const void* gate_w, const void* gate_b, float eps_lr, void* out,
                           void* o_sparse, int64_t o_sB, int64_t o_sH, int64_t o_sT, rola_stream_t stream);
 
 /* Allocation-free variant of rola_b200_lowrank_kv.  No counterpart in the

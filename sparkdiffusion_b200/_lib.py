@@ -53,7 +53,7 @@ SIGNATURES = {
     "rola_b200_lowrank_kv": [_P, _L, _L, _L, _P, _L, _L, _L, _P, _P, _P, _I, _I, _I, _I, _I, _I,
                              _P, _P, _P, _P],
     "rola_b200_sparse_attn": [_P, _P, _L, _L, _L, _P, _L, _L, _L, _P, _I, _I, _I, _I, _I, _P, _P, _P,
-                              _F, _P, _P, _L, _L, _L, _P],
+                              _P, _L, _L, _L, _P, _P, _F, _P, _P, _L, _L, _L, _P],
     "rola_b200_lowrank_kv_noalloc": [_P, _L, _L, _L, _P, _L, _L, _L, _P, _P, _P, _I, _I, _I, _I, _I, _I,
                                      _P, _P, _P],
     "rola_b200_forward_workspace_bytes": [_I, _I, _I, _I, _I, _I],

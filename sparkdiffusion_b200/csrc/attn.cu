@@ -17,7 +17,8 @@
 //                   the K and V blocks of both LUTs through one 5-slot ring in
 //                   exactly the order the MMAs consume them (K_A0 K_B0 | V_A0
 //                   K_A1 V_B0 K_B1 | ...), then the epilogue operands (q_lr
-//                   tiles and C^T).  No multicast.
+//                   tiles and C^T, and the hidden-state tiles from which the
+//                   epilogue computes the gate).  No multicast.
 //                   warp 1: TMEM owner and MMA issuer (one elected thread):
 //                   S = Q K^T (smem x smem) and O += P V with P read from TMEM
 //                   (tcgen05.mma with the A operand in tensor memory).
@@ -74,7 +75,8 @@ __device__ __forceinline__ int lut_block(const AttnParams& p, const int32_t* lut
 __global__ void __launch_bounds__(attn::THREADS, 1)
     sparse_attn_tcgen05(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tqlr,
-                        const __grid_constant__ CUtensorMap tct, const AttnParams p) {
+                        const __grid_constant__ CUtensorMap tct, const __grid_constant__ CUtensorMap tx,
+                        const AttnParams p) {
   using namespace attn;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -114,6 +116,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       prefetch_tmap(&tqlr);
       prefetch_tmap(&tct);
     }
+    if (p.has_x) prefetch_tmap(&tx);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), 512);
@@ -174,6 +177,17 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         if (ok) dst = acquire(TILE);
         if (ok) {
           tma_load_3d(dst, &tct, bar(B_FULL0 + r % NSLOTS), 0, 0, bh);
+          ++r;
+        }
+      }
+      if (p.has_x) {
+        // x tile of each query block (this head's 128 columns) for the gate
+        for (int t = 0; t < nt && ok; ++t) {
+          const uint32_t dst = acquire(SLOT);
+          if (!ok) break;
+          const int s = r % NSLOTS;
+          tma_load_4d(dst, &tx, bar(B_FULL0 + s), 0, (m0 + t) * 128, h, b);
+          tma_load_4d(dst + TILE, &tx, bar(B_FULL0 + s), 64, (m0 + t) * 128, h, b);
           ++r;
         }
       }
@@ -369,7 +383,36 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           const float os_mean_eps = rbf(os_mean + 1e-5f);
           os_rms = rbf(sqrtf(os_mean_eps));
           lr_scale = rsqrtf(ss_lr * (1.0f / 128.0f) + p.eps_lr);
-          gate = (p.gate != nullptr && tok < p.L) ? bf2f(p.gate[((int64_t)b * p.L + tok) * p.H + h]) : 0.f;
+          if (p.has_x) {
+            // gate = bf16(sigmoid(bf16(bf16(x_h . w_g) + b_h))) from this row of the x tile
+            // (fused_gate.py:97-114); the x tile is the last ring entry of this tile
+            const int r_x = nt * 2 * topk + 2 + t;
+            if (__all_sync(0xffffffffu, mbar_wait(bar(B_FULL0 + r_x % NSLOTS), (r_x / NSLOTS) & 1, abort_flag,
+                                                  kDevTimeoutLoad))) {
+              const uint8_t* xs = gbase + OFF_RING + (r_x % NSLOTS) * SLOT;
+              const uint4* wg4 = reinterpret_cast<const uint4*>(p.gate_w);
+              float acc = 0.f;
+#pragma unroll
+              for (int c16 = 0; c16 < 16; ++c16) {
+                const int box = c16 >> 3, chunk = c16 & 7;
+                const uint4 xv = *reinterpret_cast<const uint4*>(xs + box * TILE + row * 128 + ((chunk ^ (row & 7)) << 4));
+                const uint4 wv = __ldg(wg4 + c16);
+                const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  float x0, x1, w0, w1;
+                  unpack_bf2(xa[e], x0, x1);
+                  unpack_bf2(wa[e], w0, w1);
+                  acc = fmaf(x0, w0, acc);
+                  acc = fmaf(x1, w1, acc);
+                }
+              }
+              const float logit = rbf(rbf(acc) + bf2f(p.gate_b[h]));
+              gate = rbf(1.0f / (1.0f + expf(-logit)));
+            }
+          } else if (p.gate != nullptr && tok < p.L) {
+            gate = bf2f(p.gate[((int64_t)b * p.L + tok) * p.H + h]);
+          }
         }
         // pass 2: fuse and store (TMEM loads by the whole warp, stores only for rows < L)
         const bool store = tok < p.L;
@@ -419,7 +462,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
 }
 
 int launch_sparse_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tqlr,
-                       const CUtensorMap& tct, const AttnParams& p, cudaStream_t s) {
+                       const CUtensorMap& tct, const CUtensorMap& tx, const AttnParams& p, cudaStream_t s) {
   using namespace attn;
   // setmaxnreg redistributes the block's launch registers; refuse to launch if
   // the compiled kernel holds fewer than the split needs (the increase would wait)
@@ -432,7 +475,7 @@ int launch_sparse_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
   if (launch_regs < LAUNCH_REGS) return -1;
   cudaFuncSetAttribute(sparse_attn_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   dim3 grid((p.NBq + 1) / 2, p.B * p.H);
-  sparse_attn_tcgen05<<<grid, THREADS, SMEM_BYTES, s>>>(tq, tk, tv, tqlr, tct, p);
+  sparse_attn_tcgen05<<<grid, THREADS, SMEM_BYTES, s>>>(tq, tk, tv, tqlr, tct, tx, p);
   return (int)cudaGetLastError();
 }
 

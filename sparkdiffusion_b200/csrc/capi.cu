@@ -287,10 +287,11 @@ int rola_b200_center_from_sums(const float* ksum, int B, int NB, int dim, int L,
 
 int rola_b200_block_select(const void* pooled_q, const void* pooled_k, int BH, int NBq, int NBk, int topk,
                            float* scores_ws, int32_t* lut, rola_stream_t stream) {
-  ROLA_CHECK(pooled_q && pooled_k && lut && (scores_ws || NBk <= 832), "block_select: null pointer");
+  ROLA_CHECK(pooled_q && pooled_k && lut && (scores_ws || NBk <= 768), "block_select: null pointer");
+  ROLA_CHECK(aligned16(pooled_q) && aligned16(pooled_k), "block_select: pooled tensors must be 16-byte aligned");
   ROLA_CHECK(BH > 0 && NBq > 0 && NBk > 0 && NBk <= 2048, "block_select: bad sizes (NBk <= 2048)");
   ROLA_CHECK(topk >= 1 && topk <= NBk, "block_select: topk must be in [1, NBk]");
-  if (NBk <= 832) {
+  if (NBk <= 768) {
     // fused: the scores stay in registers (scores_ws is not written)
     return cuda_status(launch_select_fused(BF(pooled_q), BF(pooled_k), BH, NBq, NBk, topk, lut, S(stream)),
                        "block_select");
@@ -371,7 +372,8 @@ static int make_head_map(CUtensorMap* m, const void* ptr, int cols, int64_t sB, 
 
 int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT, const void* v,
                           int64_t v_sB, int64_t v_sH, int64_t v_sT, const int32_t* lut, int B, int L, int H, int blk,
-                          int topk, const void* q_lr, const void* Ct, const void* gate, float eps_lr, void* out,
+                          int topk, const void* q_lr, const void* Ct, const void* gate, const void* x, int64_t x_sB,
+                          int64_t x_sH, int64_t x_sT, const void* gate_w, const void* gate_b, float eps_lr, void* out,
                           void* o_sparse, int64_t o_sB, int64_t o_sH, int64_t o_sT, rola_stream_t stream) {
   ROLA_CHECK(q && k && v && lut, "sparse_attn: null pointer");
   ROLA_CHECK(out || o_sparse, "sparse_attn: no output requested");
@@ -380,12 +382,17 @@ int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t q
   const int NB = (L + blk - 1) / blk;
   ROLA_CHECK(topk >= 1 && topk <= NB, "sparse_attn: topk must be in [1, NB]");
   ROLA_CHECK((q_lr == nullptr) == (Ct == nullptr), "sparse_attn: q_lr and Ct go together");
+  ROLA_CHECK(x == nullptr || (gate_w && gate_b && q_lr), "sparse_attn: the gate from x needs gate_w, gate_b and q_lr");
+  ROLA_CHECK(x == nullptr || gate == nullptr, "sparse_attn: give gate values or x, not both");
+  ROLA_CHECK(gate_w == nullptr || aligned16(gate_w), "sparse_attn: gate_w must be 16-byte aligned");
   ROLA_CHECK(o_sB % 8 == 0 && o_sH % 8 == 0 && o_sT % 8 == 0 && (out == nullptr || aligned16(out)) &&
                  (o_sparse == nullptr || aligned16(o_sparse)),
              "sparse_attn: 16-byte aligned output rows required");
-  CUtensorMap tq, tk, tv, tqlr, tct;
+  CUtensorMap tq, tk, tv, tqlr, tct, tx;
   memset(&tqlr, 0, sizeof(tqlr));
   memset(&tct, 0, sizeof(tct));
+  memset(&tx, 0, sizeof(tx));
+  if (x) ROLA_TRY(make_head_map(&tx, x, 128, x_sB, x_sH, x_sT, L, H, B, "sparse_attn: x"));
   ROLA_TRY(make_head_map(&tq, q, 128, qk_sB, qk_sH, qk_sT, L, H, B, "sparse_attn: q"));
   ROLA_TRY(make_head_map(&tk, k, 128, qk_sB, qk_sH, qk_sT, L, H, B, "sparse_attn: k"));
   ROLA_TRY(make_head_map(&tv, v, 128, v_sB, v_sH, v_sT, L, H, B, "sparse_attn: v"));
@@ -399,6 +406,9 @@ int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t q
   AttnParams p{};
   p.lut = lut;
   p.gate = BF(gate);
+  p.gate_w = BF(gate_w);
+  p.gate_b = BF(gate_b);
+  p.has_x = x != nullptr;
   p.out = BFm(out);
   p.o_sB = o_sB;
   p.o_sH = o_sH;
@@ -414,7 +424,7 @@ int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t q
   p.qk_scale = (float)(0.08838834764831845 * 1.4426950408889634);  // 128^-0.5 * log2(e)
   p.eps_lr = eps_lr;
   p.rescale_threshold = 0.0f;
-  return cuda_status(launch_sparse_attn(tq, tk, tv, tqlr, tct, p, S(stream)), "sparse_attn");
+  return cuda_status(launch_sparse_attn(tq, tk, tv, tqlr, tct, tx, p, S(stream)), "sparse_attn");
 }
 
 // ---------------------------------------------------------------------------
@@ -483,9 +493,10 @@ int rola_b200_rola_forward(const void* x, const void* w_qkv, const void* b_qkv, 
   float* ssq = reinterpret_cast<float*>(ws + f.ssq);
   const int ssq_ld = (int)(3 * dim / 256);
   ROLA_TRY(rola_b200_qkv_gemm(x, w_qkv, b_qkv, qkv, ssq, M, 3 * dim, dim, stream));
-  ROLA_TRY(rola_b200_qk_norm_rope(qkv, qkv + dim, 3 * dim, ssq, ssq_ld, x, norm_wq, norm_wk, cos_sin, gate_w, gate_b,
-                                  B, L, H, blk, eps, ws + f.q_rope, ws + f.k_rope, ws + f.q_normed, ws + f.k_normed,
-                                  ws + f.gate, ws + f.pooled_q, reinterpret_cast<float*>(ws + f.ksum), stream));
+  ROLA_TRY(rola_b200_qk_norm_rope(qkv, qkv + dim, 3 * dim, ssq, ssq_ld, nullptr, norm_wq, norm_wk, cos_sin, nullptr,
+                                  nullptr, B, L, H, blk, eps, ws + f.q_rope, ws + f.k_rope, ws + f.q_normed,
+                                  ws + f.k_normed, nullptr, ws + f.pooled_q, reinterpret_cast<float*>(ws + f.ksum),
+                                  stream));
   ROLA_TRY(rola_b200_center_from_sums(reinterpret_cast<float*>(ws + f.ksum), B, NB, (int)dim, L, ws + f.center,
                                       stream));
   ROLA_TRY(rola_b200_mean_pool(ws + f.k_rope, (int64_t)L * dim, 128, dim, B, H, L, blk, ws + f.center,
@@ -499,8 +510,8 @@ int rola_b200_rola_forward(const void* x, const void* w_qkv, const void* b_qkv, 
   ROLA_TRY(rola_b200_lowrank_q(ws + f.q_normed, Ld, 128, dim, proj_q, lr_cos, lr_sin, rope_dim, B, L, H, R,
                                ws + f.q_lr, stream));
   return rola_b200_sparse_attn(ws + f.q_rope, ws + f.k_rope, Ld, 128, dim, qkv + 2 * dim, 3 * Ld, 128, 3 * dim, lut,
-                               B, L, H, blk, topk, ws + f.q_lr, ws + f.ct, ws + f.gate, 0.0078125f, out, nullptr, Ld,
-                               128, dim, stream);
+                               B, L, H, blk, topk, ws + f.q_lr, ws + f.ct, nullptr, x, Ld, 128, dim, gate_w, gate_b,
+                               0.0078125f, out, nullptr, Ld, 128, dim, stream);
 }
 
 }  // extern "C"

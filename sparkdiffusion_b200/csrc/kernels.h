@@ -52,7 +52,7 @@ int launch_scores(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH, int 
                   cudaStream_t s);
 // lut[bh, m, :] = top-k of scores[bh, m, :] (ties -> lower index), ascending int32
 int launch_topk(const float* scores, int rows, int NBk, int k, int32_t* lut, cudaStream_t s);
-// scores + top-k in one kernel (NBk <= 832; same results as launch_scores + launch_topk)
+// scores + top-k in one kernel (NBk <= 768; same results as launch_scores + launch_topk)
 int launch_select_fused(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH, int NBq, int NBk, int k,
                         int32_t* lut, cudaStream_t s);
 
@@ -84,7 +84,10 @@ int launch_gemm_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const __nv_bf
 // attn.cu -----------------------------------------------------------------
 struct AttnParams {
   const int32_t* lut;  // [B*H, NBq, topk]
-  const __nv_bfloat16* gate;  // [B*L, H] or nullptr
+  const __nv_bfloat16* gate;  // [B*L, H] precomputed gate values, or nullptr
+  const __nv_bfloat16* gate_w;  // [D] with has_x: the gate is computed from x tiles
+  const __nv_bfloat16* gate_b;  // [H]
+  int has_x;
   __nv_bfloat16* out;         // fused output, element (b,h,t,d) at out + b*o_sB + h*o_sH + t*o_sT + d (nullptr: skip)
   int64_t o_sB, o_sH, o_sT;
   __nv_bfloat16* o_sparse;    // optional, same layout as out
@@ -94,6 +97,6 @@ struct AttnParams {
   float rescale_threshold;  // log2 growth of the running max that triggers an O rescale (0 = always)
 };
 int launch_sparse_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tqlr,
-                       const CUtensorMap& tct, const AttnParams& p, cudaStream_t s);
+                       const CUtensorMap& tct, const CUtensorMap& tx, const AttnParams& p, cudaStream_t s);
 
 }  // namespace rola

@@ -88,14 +88,19 @@ __device__ __forceinline__ void project_warp(const __nv_bfloat16* sX, const __nv
   }
 }
 
-// SiLU + rank-RoPE on one (even, odd) rank pair of token t; returns packed bf16x2
-__device__ __forceinline__ uint32_t silu_rope_pair(float l0, float l1, int t, int pair, const LowrankParams& p) {
-  float e = rbf(l0), o = rbf(l1);                      // bf16 linear output (fused_lowrank.py:97)
-  e = rbf(e * (1.0f / (1.0f + expf(-e))));             // silu in fp32, then bf16 (:99-102)
-  o = rbf(o * (1.0f / (1.0f + expf(-o))));
-  if (pair < p.rope_dim) {                             // rotated pairs (:104-135)
-    const float c = bf2f(p.cos[(int64_t)t * p.rope_dim + pair]);
-    const float s = bf2f(p.sin[(int64_t)t * p.rope_dim + pair]);
+// cos/sin of one rank pair of token t (identity past rope_dim or past L)
+__device__ __forceinline__ float2 rope_cs(const LowrankParams& p, int t, int pair) {
+  if (pair >= p.rope_dim || t >= p.L) return make_float2(1.f, 0.f);
+  return make_float2(bf2f(p.cos[(int64_t)t * p.rope_dim + pair]), bf2f(p.sin[(int64_t)t * p.rope_dim + pair]));
+}
+
+// SiLU + rank-RoPE on one (even, odd) rank pair; returns packed bf16x2
+__device__ __forceinline__ uint32_t silu_rope_pair(float l0, float l1, float2 cs, bool rotate) {
+  float e = rbf(l0), o = rbf(l1);                       // bf16 linear output (fused_lowrank.py:97)
+  e = rbf(e * __fdividef(1.0f, 1.0f + __expf(-e)));     // silu in fp32, then bf16 (:99-102)
+  o = rbf(o * __fdividef(1.0f, 1.0f + __expf(-o)));
+  if (rotate) {                                         // rotated pairs (:104-135)
+    const float c = cs.x, s = cs.y;
     const float ec = rbf(e * c), os = rbf(o * s), es = rbf(e * s), oc = rbf(o * c);
     return pack_bf2(ec - os, es + oc);
   }
@@ -107,6 +112,7 @@ __global__ void __launch_bounds__(128) lowrank_q_kernel(LowrankParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __nv_bfloat16* sX = reinterpret_cast<__nv_bfloat16*>(smem_raw);
   __nv_bfloat16* sP = sX + kLrT * kPadX;
+  __nv_bfloat16* sO = sX;  // the q tile is dead after the projection: reuse it for q_lr [128 t][72]
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int t0 = blockIdx.x * kLrT;
   for (int i = threadIdx.x; i < 64 * 16; i += blockDim.x) {
@@ -114,25 +120,42 @@ __global__ void __launch_bounds__(128) lowrank_q_kernel(LowrankParams p) {
     *reinterpret_cast<uint4*>(sP + r * kPadX + c) = *reinterpret_cast<const uint4*>(p.proj + r * 128 + c);
   }
   load_tile(sX, p.x, p.x_sB, p.x_sH, p.x_sT, b, t0, p.L, h);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, tig = lane & 3;
+  // this thread's RoPE factors, fetched before the MMAs so their latency hides
+  float2 cs[2][2][8];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+        cs[mt][half][nt] = rope_cs(p, t0 + warp * 32 + mt * 16 + g + half * 8, nt * 4 + tig);
   __syncthreads();
   float acc[2][8][4];
   project_warp(sX, sP, acc);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int g = lane >> 2, tig = lane & 3;
+  __syncthreads();  // every warp is done reading sX before it is overwritten
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-      const int t = t0 + warp * 32 + mt * 16 + g + half * 8;
-      if (t >= p.L) continue;
-      __nv_bfloat16* dst = p.lr_out + ((int64_t)b * p.L + t) * p.H * 64 + h * 64;
+      const int tl = warp * 32 + mt * 16 + g + half * 8;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
         const int r = nt * 8 + tig * 2;
-        const uint32_t v = silu_rope_pair(acc[mt][nt][half * 2], acc[mt][nt][half * 2 + 1], t, r >> 1, p);
-        *reinterpret_cast<uint32_t*>(dst + r) = v;
+        *reinterpret_cast<uint32_t*>(sO + tl * kPadR + r) =
+            silu_rope_pair(acc[mt][nt][half * 2], acc[mt][nt][half * 2 + 1], cs[mt][half][nt], (r >> 1) < p.rope_dim);
       }
     }
+  __syncthreads();
+  // coalesced store: 8 threads per 128-byte token row
+  for (int i = threadIdx.x; i < kLrT * 8; i += blockDim.x) {
+    const int tl = i >> 3, c = (i & 7) * 8;
+    const int t = t0 + tl;
+    if (t < p.L)
+      *reinterpret_cast<uint4*>(p.lr_out + ((int64_t)b * p.L + t) * p.H * 64 + h * 64 + c) =
+          *reinterpret_cast<const uint4*>(sO + tl * kPadR + c);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -201,6 +224,12 @@ __global__ void __launch_bounds__(256, 2) lowrank_kv_kernel(LowrankParams p) {
     __syncthreads();
     const __nv_bfloat16* cX = sX + buf * kKvTile;
     const __nv_bfloat16* cV = sV + buf * kKvTile;
+    const int t0 = tile * kKvT;
+    float2 cs[2][4];  // this thread's RoPE factors, fetched before the MMAs
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) cs[half][nt] = rope_cs(p, t0 + pm * 16 + g + half * 8, pn * 16 + nt * 4 + tig);
     // projection: 16 tokens x 32 ranks per warp, K = 128
     float acc[4][4];
 #pragma unroll
@@ -227,7 +256,6 @@ __global__ void __launch_bounds__(256, 2) lowrank_kv_kernel(LowrankParams p) {
         mma16816(acc[2 * np + 1], a0, a1, a2, a3, b2, b3);
       }
     }
-    const int t0 = tile * kKvT;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int tl = pm * 16 + g + half * 8;
@@ -236,7 +264,7 @@ __global__ void __launch_bounds__(256, 2) lowrank_kv_kernel(LowrankParams p) {
       for (int nt = 0; nt < 4; ++nt) {
         const int r = pn * 32 + nt * 8 + tig * 2;
         uint32_t v = 0u;
-        if (t < p.L) v = silu_rope_pair(acc[nt][half * 2], acc[nt][half * 2 + 1], t, r >> 1, p);
+        if (t < p.L) v = silu_rope_pair(acc[nt][half * 2], acc[nt][half * 2 + 1], cs[half][nt], (r >> 1) < p.rope_dim);
         *reinterpret_cast<uint32_t*>(sK + tl * kPadR + r) = v;
       }
     }

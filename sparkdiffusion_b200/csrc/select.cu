@@ -238,92 +238,113 @@ int launch_topk(const float* scores, int rows, int NBk, int k, int32_t* lut, cud
 
 
 // ---------------------------------------------------------------------------
-// fused scores + top-k: one CTA per (32 query blocks, batch*head).  The head's
+// fused scores + top-k: one CTA per (64 query blocks, batch*head).  The head's
 // pooled K is staged in shared memory with a 65-word row stride (lane j reads
 // key block j: 32 different rows, 32 different banks); each lane keeps the
-// fp32 scores of its key blocks j = lane + 32 i in registers, accumulated over
-// d in order (the same FMA chain as scores_kernel), then the warp picks the
-// top-k exactly as topk_kernel does.
+// fp32 scores of its key blocks j = lane + 32 i for 4 query rows in registers,
+// every score accumulated over d in order (the same FMA chain as
+// scores_kernel), then the warp picks each row's top-k exactly as topk_kernel.
 // ---------------------------------------------------------------------------
-constexpr int kSelRows = 32;          // query blocks per CTA (4 per warp)
+constexpr int kSelRows = 64;          // query blocks per CTA (8 per warp, 4 at a time)
 constexpr int kSelWords = 65;         // smem row stride of pooled K, 32-bit words
-constexpr int kSelMaxNBk = 832;       // shared-memory bound of the fused kernel
+constexpr int kSelMaxNBk = 768;       // shared-memory bound of the fused kernel
+
+template <int PER>
+__device__ __forceinline__ void warp_topk_emit(const float (&acc)[PER], int per, int NBk, int k, int lane,
+                                               int32_t* __restrict__ dst) {
+  uint32_t key[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int j = lane + 32 * i;
+    key[i] = (i < per && j < NBk) ? orderable(acc[i]) : 0u;
+  }
+  uint64_t taken = 0;  // bit i: element lane + 32 i kept
+  for (int r = 0; r < k; ++r) {
+    uint64_t best = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int j = lane + 32 * i;
+      if (i < per && j < NBk && !((taken >> i) & 1ull)) {
+        const uint64_t cand = ((uint64_t)key[i] << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)j);
+        best = cand > best ? cand : best;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    const uint32_t jbest = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu);
+    if ((int)(jbest & 31) == lane) taken |= 1ull << (jbest >> 5);
+  }
+  int written = 0;
+  for (int i = 0; i < per; ++i) {
+    const bool kept = (taken >> i) & 1ull;
+    const uint32_t ballot = __ballot_sync(0xffffffffu, kept);
+    if (kept) dst[written + __popc(ballot & ((1u << lane) - 1u))] = lane + 32 * i;
+    written += __popc(ballot);
+  }
+}
 
 template <int PER>
 __global__ void __launch_bounds__(256) select_fused_kernel(const __nv_bfloat16* __restrict__ pq,
                                                            const __nv_bfloat16* __restrict__ pk, int NBq, int NBk,
                                                            int k, int32_t* __restrict__ lut) {
   extern __shared__ uint32_t sel_smem[];
-  uint32_t* sk = sel_smem;                                         // [NBk][65] words (bf16 pairs)
-  float* sq = reinterpret_cast<float*>(sel_smem + NBk * kSelWords);  // [32][128]
+  uint32_t* sk = sel_smem;                                    // [NBk][65] words (bf16 pairs)
+  uint32_t* sq = sel_smem + ((NBk * kSelWords + 3) & ~3);     // [64][64] words, 16-byte aligned
   const int bh = blockIdx.y;
   const int m0 = blockIdx.x * kSelRows;
-  const uint32_t* kb = reinterpret_cast<const uint32_t*>(pk + (int64_t)bh * NBk * 128);
-  for (int i = threadIdx.x; i < NBk * 64; i += blockDim.x) {
-    const int r = i >> 6, w = i & 63;
-    sk[r * kSelWords + w] = kb[i];
+  const uint4* kb = reinterpret_cast<const uint4*>(pk + (int64_t)bh * NBk * 128);
+  for (int i = threadIdx.x; i < NBk * 16; i += blockDim.x) {
+    const int r = i >> 4, w = (i & 15) * 4;
+    const uint4 u = kb[i];
+    uint32_t* d = sk + r * kSelWords + w;
+    d[0] = u.x;
+    d[1] = u.y;
+    d[2] = u.z;
+    d[3] = u.w;
   }
-  const __nv_bfloat16* qb = pq + (int64_t)bh * NBq * 128;
-  for (int i = threadIdx.x; i < kSelRows * 128; i += blockDim.x) {
-    const int r = i >> 7, d = i & 127;
-    sq[i] = (m0 + r < NBq) ? bf2f(qb[(int64_t)(m0 + r) * 128 + d]) : 0.f;
+  const uint4* qb = reinterpret_cast<const uint4*>(pq + (int64_t)bh * NBq * 128);
+  for (int i = threadIdx.x; i < kSelRows * 16; i += blockDim.x) {
+    const int r = i >> 4;
+    const uint4 u = (m0 + r < NBq) ? qb[(int64_t)m0 * 16 + i] : make_uint4(0, 0, 0, 0);
+    reinterpret_cast<uint4*>(sq)[i] = u;
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per = (NBk + 31) / 32;
-  for (int rr = warp; rr < kSelRows; rr += 8) {
-    const int m = m0 + rr;
-    if (m >= NBq) break;
-    const float* qrow = sq + rr * 128;
-    float acc[PER];
+  for (int g = 0; g < 2; ++g) {
+    const int rr0 = warp * 8 + g * 4;  // 4 query rows of this pass
+    if (m0 + rr0 >= NBq) break;
+    float acc[4][PER];
 #pragma unroll
-    for (int i = 0; i < PER; ++i) acc[i] = 0.f;
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int i = 0; i < PER; ++i) acc[a][i] = 0.f;
 #pragma unroll 2
     for (int w = 0; w < 64; ++w) {
-      const float q0 = qrow[2 * w], q1 = qrow[2 * w + 1];
+      float q0[4], q1[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) unpack_bf2(sq[(rr0 + a) * 64 + w], q0[a], q1[a]);
 #pragma unroll
       for (int i = 0; i < PER; ++i) {
         const int j = lane + 32 * i;
         if (i < per && j < NBk) {
           float k0, k1;
           unpack_bf2(sk[j * kSelWords + w], k0, k1);
-          acc[i] = __fmaf_rn(q0, k0, acc[i]);
-          acc[i] = __fmaf_rn(q1, k1, acc[i]);
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            acc[a][i] = __fmaf_rn(q0[a], k0, acc[a][i]);
+            acc[a][i] = __fmaf_rn(q1[a], k1, acc[a][i]);
+          }
         }
       }
     }
-    uint32_t key[PER];
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int j = lane + 32 * i;
-      key[i] = (i < per && j < NBk) ? orderable(acc[i]) : 0u;
-    }
-    uint64_t taken = 0;  // bit i: element lane + 32 i kept (PER <= 64)
-    for (int r = 0; r < k; ++r) {
-      uint64_t best = 0;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        const int j = lane + 32 * i;
-        if (i < per && j < NBk && !((taken >> i) & 1ull)) {
-          const uint64_t cand = ((uint64_t)key[i] << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)j);
-          best = cand > best ? cand : best;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const uint64_t other = __shfl_xor_sync(0xffffffffu, best, o);
-        best = other > best ? other : best;
-      }
-      const uint32_t jbest = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu);
-      if ((int)(jbest & 31) == lane) taken |= 1ull << (jbest >> 5);
-    }
-    int32_t* dst = lut + ((int64_t)bh * NBq + m) * k;
-    int written = 0;
-    for (int i = 0; i < per; ++i) {
-      const bool kept = (taken >> i) & 1ull;
-      const uint32_t ballot = __ballot_sync(0xffffffffu, kept);
-      if (kept) dst[written + __popc(ballot & ((1u << lane) - 1u))] = lane + 32 * i;
-      written += __popc(ballot);
+    for (int a = 0; a < 4; ++a) {
+      const int m = m0 + rr0 + a;
+      if (m < NBq) warp_topk_emit<PER>(acc[a], per, NBk, k, lane, lut + ((int64_t)bh * NBq + m) * k);
     }
   }
 }
@@ -331,18 +352,18 @@ __global__ void __launch_bounds__(256) select_fused_kernel(const __nv_bfloat16* 
 int launch_select_fused(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH, int NBq, int NBk, int k,
                         int32_t* lut, cudaStream_t s) {
   if (NBk > kSelMaxNBk || k < 1 || k > NBk) return -1;
-  const int smem = (NBk * kSelWords + kSelRows * 128) * 4;
+  const int smem = (((NBk * kSelWords + 3) & ~3) + kSelRows * 64) * 4;
   dim3 grid((NBq + kSelRows - 1) / kSelRows, BH);
   const int per = (NBk + 31) / 32;
-#define ROLA_SEL(P)                                                                              \
-  do {                                                                                           \
+#define ROLA_SEL(P)                                                                                  \
+  do {                                                                                               \
     cudaFuncSetAttribute(select_fused_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-    select_fused_kernel<P><<<grid, 256, smem, s>>>(pq, pk, NBq, NBk, k, lut);                    \
+    select_fused_kernel<P><<<grid, 256, smem, s>>>(pq, pk, NBq, NBk, k, lut);                        \
   } while (0)
   if (per <= 4) ROLA_SEL(4);
   else if (per <= 8) ROLA_SEL(8);
   else if (per <= 16) ROLA_SEL(16);
-  else ROLA_SEL(26);
+  else ROLA_SEL(24);
 #undef ROLA_SEL
   return (int)cudaGetLastError();
 }

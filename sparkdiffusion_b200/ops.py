@@ -25,7 +25,7 @@ from .rope import prepare_cos_sin
 
 BF16 = torch.bfloat16
 HEAD_DIM = 128
-FUSED_SELECT_MAX_NB = 832  # up to this many key blocks the scores stay on chip (no scores buffer)
+FUSED_SELECT_MAX_NB = 768  # up to this many key blocks the scores stay on chip (no scores buffer)
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -59,11 +59,11 @@ def topk_count(topk_ratio: float, nb: int) -> int:
 
 
 def default_splits(B: int, H: int, L: int) -> int:
-    """Sequence splits of the low-rank C reduction: about two waves of two
-    CTAs per SM (64-token tiles)."""
+    """Sequence splits of the low-rank C reduction: one wave of two CTAs per
+    SM (64-token tiles)."""
     tiles = (L + 63) // 64
     sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    return max(1, min(tiles, round(4 * sms / (B * H))))
+    return max(1, min(tiles, (2 * sms) // (B * H)))
 
 
 # ---------------------------------------------------------------------------
@@ -93,12 +93,15 @@ def qkv_gemm(x2d: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = Non
 
 def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, ksum, lr_cos, lr_sin, rope_dim,
                          proj_q, proj_k, num_heads: int, blk: int, topk: int, splits: int | None = None,
-                         keep: bool = False, lut=None, events: dict | None = None):
+                         keep: bool = False, lut=None, events: dict | None = None, x=None, gate_w=None,
+                         gate_b=None):
     """Selection, low-rank branch and fused attention for ``num_heads`` heads
     over the full sequence.  q_rope/k_rope/q_normed/k_normed/v are token-major
-    ``[B, L, H*D]`` (unit column stride; q/k tensors contiguous), gate
-    ``[B, L, H]``, pooled_q ``[B, H, NB, D]`` and ksum ``[B, NB, H*D]`` come from
-    the prologue pass.  Returns the gated output ``[B, L, H*D]``."""
+    ``[B, L, H*D]`` (unit column stride; q/k tensors contiguous), pooled_q
+    ``[B, H, NB, D]`` and ksum ``[B, NB, H*D]`` come from the prologue pass.  The
+    gate is either given (``gate [B, L, H]``) or computed inside the attention
+    epilogue from the hidden states ``x [B, L, H*D]`` with ``gate_w``/``gate_b``.
+    Returns the gated output ``[B, L, H*D]``."""
     B, L, dim = q_rope.shape
     H = num_heads
     dev = q_rope.device
@@ -140,9 +143,16 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
     eps_lr = float(torch.finfo(BF16).eps)
     if events is not None:
         events["attn"][0].record()
+    if x is not None:
+        xs = x.stride()
+        gw = _bf16_vec(gate_w, HEAD_DIM, "gate_w")
+        gb = _bf16_vec(gate_b, H, "gate_b")
+        gate = None
+    else:
+        xs, gw, gb = (0, 0, 0), None, None
     _lib.call("rola_b200_sparse_attn", _ptr(q_rope), _ptr(k_rope), L * dim, HEAD_DIM, dim, _ptr(v), vs[0],
-              HEAD_DIM, vs[1], _ptr(lut), B, L, H, blk, topk, _ptr(q_lr), _ptr(Ct), _ptr(gate), eps_lr, _ptr(out),
-              _ptr(o_sparse), L * dim, HEAD_DIM, dim, st)
+              HEAD_DIM, vs[1], _ptr(lut), B, L, H, blk, topk, _ptr(q_lr), _ptr(Ct), _ptr(gate), _ptr(x), xs[0],
+              HEAD_DIM, xs[1], _ptr(gw), _ptr(gb), eps_lr, _ptr(out), _ptr(o_sparse), L * dim, HEAD_DIM, dim, st)
     if events is not None:
         events["attn"][1].record()
     if not keep:
@@ -182,26 +192,24 @@ def rola_attention_from_qkv(q_raw, k_raw, v_raw, x, cos_sin, lr_cos, lr_sin, rop
     e = lambda *s, dt=BF16: torch.empty(*s, device=dev, dtype=dt)  # noqa: E731
     q_rope, k_rope = e(B, L, dim), e(B, L, dim)
     q_normed, k_normed = e(B, L, dim), e(B, L, dim)
-    gate = e(B, L, H)
     pooled_q = e(B, H, NB, HEAD_DIM)
     ksum = e(B, NB, dim, dt=torch.float32)
-    gw = _bf16_vec(gate_w, HEAD_DIM, "gate_w")
-    gb = _bf16_vec(gate_b, H, "gate_b")
     nwq = None if norm_wq is None else _bf16_vec(norm_wq, dim, "norm_wq")
     nwk = None if norm_wk is None else _bf16_vec(norm_wk, dim, "norm_wk")
     cos_sin = cos_sin.to(torch.float32).contiguous()
     xc = x.contiguous()
     ssq_ld = 0 if ssq is None else ssq.shape[-1]
-    _lib.call("rola_b200_qk_norm_rope", _ptr(q_raw), _ptr(k_raw), q_raw.stride(1), _ptr(ssq), ssq_ld, _ptr(xc),
-              _ptr(nwq), _ptr(nwk), _ptr(cos_sin), _ptr(gw), _ptr(gb), B, L, H, blk, eps, _ptr(q_rope),
-              _ptr(k_rope), _ptr(q_normed), _ptr(k_normed), _ptr(gate), _ptr(pooled_q), _ptr(ksum), st)
-    res = head_local_attention(q_rope, k_rope, q_normed, k_normed, v_raw, gate, pooled_q, ksum, lr_cos, lr_sin,
-                               rope_dim, proj_q, proj_k, H, blk, topk, splits, keep, lut, events)
+    _lib.call("rola_b200_qk_norm_rope", _ptr(q_raw), _ptr(k_raw), q_raw.stride(1), _ptr(ssq), ssq_ld, None,
+              _ptr(nwq), _ptr(nwk), _ptr(cos_sin), None, None, B, L, H, blk, eps, _ptr(q_rope),
+              _ptr(k_rope), _ptr(q_normed), _ptr(k_normed), None, _ptr(pooled_q), _ptr(ksum), st)
+    res = head_local_attention(q_rope, k_rope, q_normed, k_normed, v_raw, None, pooled_q, ksum, lr_cos, lr_sin,
+                               rope_dim, proj_q, proj_k, H, blk, topk, splits, keep, lut, events, x=xc,
+                               gate_w=gate_w, gate_b=gate_b)
     if not keep:
         return res
     out, extra = res
-    extra.update(q_rope=q_rope, k_rope=k_rope, q_normed=q_normed, k_normed=k_normed, gate=gate,
-                 pooled_q=pooled_q, ksum=ksum, v=v_raw)
+    extra.update(q_rope=q_rope, k_rope=k_rope, q_normed=q_normed, k_normed=k_normed, pooled_q=pooled_q, ksum=ksum,
+                 v=v_raw)
     return out, extra
 
 
@@ -331,7 +339,8 @@ def fused_sparse_attn(q, k, v, topk_ratio: float = 0.1, blkq: int = 64, blkk: in
     s = q4.stride()
     vs = v4.stride()
     _lib.call("rola_b200_sparse_attn", _ptr(q4), _ptr(k4), s[0], s[1], s[2], _ptr(v4), vs[0], vs[1], vs[2],
-              _ptr(lut), B, L, H, blkq, topk, None, None, None, 0.0, None, _ptr(o), s[0], s[1], s[2], _stream())
+              _ptr(lut), B, L, H, blkq, topk, None, None, None, None, 0, 0, 0, None, None, 0.0, None, _ptr(o), s[0],
+              s[1], s[2], _stream())
     return o
 
 

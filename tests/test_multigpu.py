@@ -1,0 +1,94 @@
+"""Ulysses sequence<->head parallel forward on 2 GPUs (NCCL) vs the 1-GPU forward.
+
+Skipped unless at least two CUDA devices are visible.  Each rank holds a
+sequence shard of the hidden states; the result gathered from both ranks must
+select exactly the same key blocks as the single-GPU forward and match its
+output within the bf16 tolerance (the gate is summed in a different order on
+the two paths, so outputs may differ by bf16 rounding).
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from conftest import assert_bf16_close
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _workload():
+    from sparkdiffusion_b200.workloads import C3
+
+    wl = C3.scaled(H=4, grid=(3, 10, 24), B=1)  # L = 720 (NB = 6, ragged tail)
+    return wl.__class__(**{**wl.__dict__, "topk": 3})
+
+
+def _inputs(wl, dev):
+    from sparkdiffusion_b200.rope import prepare_cos_sin, prepare_lowrank_cos_sin, wan_rope_freqs
+    from sparkdiffusion_b200.workloads import make_inputs
+
+    inp = make_inputs(wl, device="cpu")
+    inp = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
+    freqs = wan_rope_freqs(*wl.grid)
+    cos_sin = prepare_cos_sin(freqs, wl.L, 128).to(dev)
+    lr_cos, lr_sin, rope_dim = prepare_lowrank_cos_sin(freqs, wl.L, wl.rank, torch.bfloat16)
+    common = (cos_sin, lr_cos.to(dev), lr_sin.to(dev), rope_dim, inp["norm_wq"], inp["norm_wk"], inp["proj_q"],
+              inp["proj_k"], inp["gate_w"], inp["gate_b"])
+    return inp, common
+
+
+def _rank_main(rank, port, out_path):
+    import datetime
+
+    import torch.distributed as dist
+
+    from sparkdiffusion_b200 import _lib
+    from sparkdiffusion_b200.ulysses import ulysses_rola_attention_params
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    wl = _workload()
+    inp, common = _inputs(wl, dev)
+    Ls = wl.L // WORLD
+    x_local = inp["x"][:, rank * Ls:(rank + 1) * Ls].contiguous()
+    out = ulysses_rola_attention_params(x_local, inp["w_qkv"], None, *common, wl.H, wl.topk)
+    torch.cuda.synchronize()
+    status = _lib.device_status()
+    parts = [torch.empty_like(out) for _ in range(WORLD)]
+    dist.all_gather(parts, out)
+    if rank == 0:
+        torch.save({"out": torch.cat(parts, dim=1).cpu(), "status": status}, out_path)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_ulysses_two_gpus_match_single_gpu(tmp_path):
+    from sparkdiffusion_b200 import ops
+
+    out_path = str(tmp_path / "ulysses.pt")
+    mp.start_processes(_rank_main, args=(_free_port(), out_path), nprocs=WORLD, start_method="spawn")
+    got = torch.load(out_path)
+    assert got["status"] == 0
+    wl = _workload()
+    inp, common = _inputs(wl, "cuda:0")
+    ref = ops.rola_attention_core(inp["x"], inp["w_qkv"], None, *common, wl.H, 128, wl.topk)
+    torch.cuda.synchronize()
+    assert_bf16_close(got["out"], ref.cpu(), "ulysses vs single GPU")
