@@ -62,13 +62,13 @@ int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out
 /* (a4 epilogue, a5 q-pool, a6 block sums, a10 gate) in one pass over the rows.
  * q_raw/k_raw: token-major, row stride ld_raw.  ssq (optional): the
  * [B*L, ssq_ld] sums of squares written by rola_b200_qkv_gemm over the q|k|v
- * row (q tiles first, then k), which replace the in-kernel row reduction (H even,
- * blk <= 256); NULL computes the row norms in the kernel.  x: token-major [B*L, dim] (gate
+ * row (q tiles first, then k; H even); NULL computes the row statistics first in
+ * stream-ordered scratch (cudaMallocAsync).  x: token-major [B*L, dim] (gate
  * input; NULL skips the gate).  norm_wq/norm_wk: [dim] (both NULL = no norm).
  * cos_sin: [L, D] fp32 interleaved (cos0, sin0, cos1, ...).  gate_w: [D],
  * gate_b: [H] bf16.  Outputs (any may be NULL): q_rope, k_rope, q_normed,
  * k_normed token-major [B*L, dim]; gate_out [B*L, H]; pooled_q [B, H, NB, D]
- * bf16; ksum [B, NB, dim] fp32 block sums of k_rope.  H <= 64.
+ * bf16; ksum [B, NB, dim] fp32 block sums of k_rope.
  * Replaces _epilogue_kernel (fused_qkv_rope.py:53-225, layout [B*H, L, D] there),
  * mean_pool(q) (utils.py:272-297 via fused_sparse_attn.py:179) and the gate
  * logits of _gate_fusion_kernel (fused_gate.py:97-114). */

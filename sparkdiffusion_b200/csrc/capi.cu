@@ -145,22 +145,48 @@ int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out
                      "qkv_gemm");
 }
 
+// Runs the streaming norm pass.  ssq: the QKV GEMM's per-256-column sums of
+// squares (row stride ssq_ld), or nullptr, in which case the row statistics are
+// computed first into stream-ordered scratch.
+static int run_norm_pass(NormRopeParams& p, bool norm, bool rope, bool pool, const float* ssq, int ssq_ld,
+                         cudaStream_t s, const char* what) {
+  float* scratch = nullptr;
+  if (norm && ssq == nullptr) {
+    const int64_t rows = (int64_t)p.B * p.L;
+    ROLA_TRY(cuda_status(cudaMallocAsync(reinterpret_cast<void**>(&scratch), rows * 2 * p.H * sizeof(float), s), what));
+    const int rc = launch_row_ssq(p.q_in, p.k_in, p.ld_in, rows, p.H * 128, scratch, s);
+    if (rc != 0) {
+      cudaFreeAsync(scratch, s);
+      return cuda_status(rc, what);
+    }
+    p.ssq = scratch;
+    p.ssq_ld = 2 * p.H;
+    p.ssq_tile = 128;
+  } else {
+    p.ssq = ssq;
+    p.ssq_ld = ssq_ld;
+    p.ssq_tile = 256;
+  }
+  const int rc = launch_norm_rope_pool(p, norm, rope, pool, s);
+  if (scratch) cudaFreeAsync(scratch, s);
+  if (rc == -1) return fail(ROLA_ERR_INVALID, "%s: unsupported configuration", what);
+  return cuda_status(rc, what);
+}
+
 int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw, const float* ssq, int ssq_ld,
                            const void* x, const void* norm_wq, const void* norm_wk, const float* cos_sin,
                            const void* gate_w, const void* gate_b, int B, int L, int H, int blk, float eps,
                            void* q_rope, void* k_rope, void* q_normed, void* k_normed, void* gate_out, void* pooled_q,
                            float* ksum, rola_stream_t stream) {
   ROLA_CHECK(q_raw && k_raw && cos_sin, "qk_norm_rope: null input");
-  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 40 && blk > 0, "qk_norm_rope: bad sizes (H <= 40)");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && blk > 0 && blk <= 4096, "qk_norm_rope: bad sizes");
   ROLA_CHECK((norm_wq == nullptr) == (norm_wk == nullptr), "qk_norm_rope: give both norm weights or neither");
   ROLA_CHECK(ld_raw % 8 == 0 && aligned16(q_raw) && aligned16(k_raw), "qk_norm_rope: 16-byte aligned rows required");
   ROLA_CHECK((pooled_q == nullptr) == (ksum == nullptr), "qk_norm_rope: pooled_q and ksum go together");
   ROLA_CHECK(x == nullptr || (gate_w && gate_b && gate_out), "qk_norm_rope: the gate needs gate_w, gate_b, gate_out");
-  ROLA_CHECK(ssq == nullptr || (H % 2 == 0 && blk <= 256 && ssq_ld >= H),
-             "qk_norm_rope: sums of squares need an even head count, blk <= 256 and ssq_ld >= H");
+  ROLA_CHECK(ssq == nullptr || (H % 2 == 0 && ssq_ld >= H),
+             "qk_norm_rope: sums of squares need an even head count and ssq_ld >= H");
   NormRopeParams p{};
-  p.ssq = ssq;
-  p.ssq_ld = ssq_ld;
   p.q_in = BF(q_raw);
   p.k_in = BF(k_raw);
   p.ld_in = ld_raw;
@@ -185,13 +211,7 @@ int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw,
   p.NB = (L + blk - 1) / blk;
   p.heads_per_chunk = H;
   p.eps = eps;
-  const bool norm = norm_wq != nullptr;
-  const bool pool = pooled_q != nullptr;
-  if (!norm && !pool) {
-    // rope only
-    return cuda_status(launch_norm_rope_pool(p, false, true, false, S(stream)), "qk_norm_rope");
-  }
-  return cuda_status(launch_norm_rope_pool(p, norm, true, pool, S(stream)), "qk_norm_rope");
+  return run_norm_pass(p, norm_wq != nullptr, true, pooled_q != nullptr, ssq, ssq_ld, S(stream), "qk_norm_rope");
 }
 
 int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_raw, int64_t ld_raw, const float* ssq,
@@ -200,14 +220,12 @@ int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_r
                            void* k_send, void* v_send, void* gate_out, rola_stream_t stream) {
   ROLA_CHECK(q_raw && k_raw && v_raw && norm_wq && norm_wk && q_send && k_send && v_send,
              "qk_norm_pack: null pointer");
-  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 40 && heads_per_chunk > 0 && H % heads_per_chunk == 0,
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && heads_per_chunk > 0 && H % heads_per_chunk == 0,
              "qk_norm_pack: bad sizes");
   ROLA_CHECK(ld_raw % 8 == 0, "qk_norm_pack: 16-byte aligned rows required");
   ROLA_CHECK(x == nullptr || (gate_w && gate_b && gate_out), "qk_norm_pack: the gate needs gate_w, gate_b, gate_out");
   ROLA_CHECK(ssq == nullptr || (H % 2 == 0 && ssq_ld >= H), "qk_norm_pack: sums of squares need an even head count");
   NormRopeParams p{};
-  p.ssq = ssq;
-  p.ssq_ld = ssq_ld;
   p.q_in = BF(q_raw);
   p.k_in = BF(k_raw);
   p.v_in = BF(v_raw);
@@ -229,14 +247,14 @@ int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_r
   p.NB = (L + 127) / 128;
   p.heads_per_chunk = heads_per_chunk;
   p.eps = eps;
-  return cuda_status(launch_norm_rope_pool(p, true, false, false, S(stream)), "qk_norm_pack");
+  return run_norm_pass(p, true, false, false, ssq, ssq_ld, S(stream), "qk_norm_pack");
 }
 
 int rola_b200_rope_pool(const void* q_normed, const void* k_normed, int64_t ld, const float* cos_sin, int B, int L,
                         int H, int blk, void* q_rope, void* k_rope, void* pooled_q, float* ksum,
                         rola_stream_t stream) {
   ROLA_CHECK(q_normed && k_normed && cos_sin && q_rope && k_rope, "rope_pool: null pointer");
-  ROLA_CHECK(B > 0 && L > 0 && H > 0 && H <= 40 && blk > 0, "rope_pool: bad sizes");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && blk > 0 && blk <= 4096, "rope_pool: bad sizes");
   ROLA_CHECK((pooled_q == nullptr) == (ksum == nullptr), "rope_pool: pooled_q and ksum go together");
   ROLA_CHECK(ld % 8 == 0, "rope_pool: 16-byte aligned rows required");
   NormRopeParams p{};
@@ -254,7 +272,7 @@ int rola_b200_rope_pool(const void* q_normed, const void* k_normed, int64_t ld, 
   p.blk = blk;
   p.NB = (L + blk - 1) / blk;
   p.heads_per_chunk = H;
-  return cuda_status(launch_norm_rope_pool(p, false, true, pooled_q != nullptr, S(stream)), "rope_pool");
+  return run_norm_pass(p, false, true, pooled_q != nullptr, nullptr, 0, S(stream), "rope_pool");
 }
 
 int rola_b200_mean_pool(const void* x, int64_t sB, int64_t sH, int64_t sT, int B, int H, int L, int blk,

@@ -30,13 +30,17 @@ struct NormRopeParams {
   __nv_bfloat16* gate_out;  // [B][H/heads_per_chunk][L][heads_per_chunk]
   __nv_bfloat16* pooled_q;  // [B, H, NB, D]
   float* ksum;              // [B, NB, dim]
-  const float* ssq;         // optional [B*L, ssq_ld] per-256-column sums of squares (q tiles, then k tiles)
+  const float* ssq;         // [B*L, ssq_ld] per-tile sums of squares (q tiles, then k tiles); needed to normalise
   int ssq_ld;
+  int ssq_tile;             // columns per partial sum (256 from the QKV GEMM, 128 from row_ssq)
   int B, L, H, blk, NB;
   int heads_per_chunk;     // chunked output layout for the all-to-all send buffers (H: plain layout)
   float eps;
 };
 int launch_norm_rope_pool(const NormRopeParams& p, bool norm, bool rope, bool pool, cudaStream_t s);
+// ssq[row, :] = sums of squares of q[row] and k[row] over 128-column tiles (q tiles, then k tiles)
+int launch_row_ssq(const __nv_bfloat16* q, const __nv_bfloat16* k, int64_t ld, int64_t rows, int dim, float* ssq,
+                   cudaStream_t s);
 
 // select.cu ---------------------------------------------------------------
 // Generic strided block pooling: element (b, h, t, d) of x sits at

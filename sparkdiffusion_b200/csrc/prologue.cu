@@ -52,119 +52,114 @@ __device__ __forceinline__ void store8(__nv_bfloat16* dst, const float (&v)[8]) 
   *reinterpret_cast<uint4*>(dst) = u;
 }
 
-// block-wide sum of NV values per thread; `red` holds 2 * NV * 32 floats
-template <int NV>
-__device__ __forceinline__ void block_sum(float (&v)[NV], float* red, int parity) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v[i] += __shfl_xor_sync(0xffffffffu, v[i], o);
-  }
-  float* buf = red + parity * NV * 32;
-  if (lane == 0) {
-#pragma unroll
-    for (int i = 0; i < NV; ++i) buf[i * 32 + warp] = v[i];
-  }
-  __syncthreads();
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    float s = 0.f;
-    for (int w = 0; w < nwarps; ++w) s += buf[i * 32 + w];
-    v[i] = s;
-  }
+// ---------------------------------------------------------------------------
+// Streaming pass.  One CTA per (token block m, group of 8 heads, batch b):
+// thread j owns hidden columns [8 j, 8 j + 8) of the group (16 threads per
+// head) for every token of the block.  The token rows of q, k (and v / x when
+// needed) are streamed through an 8-token cp.async ring in shared memory;
+// each thread reads back exactly the 16-byte chunks it copied, so the loop
+// needs no block-wide barrier.  The full-width RMS statistics come from the
+// per-tile sums of squares (QKV GEMM epilogue or row_ssq_kernel).
+// ---------------------------------------------------------------------------
+constexpr int kNormHeads = 8;                   // heads per CTA
+constexpr int kNormThreads = kNormHeads * 16;   // 128
+constexpr int kNormRing = 8;                    // tokens in flight
+constexpr int kNormRow = kNormHeads * 128 * 2;  // bytes of one tensor row segment (2 KB)
+
+__device__ __forceinline__ void cp_async16_ca(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_grp() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_grp() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void unpack8(const uint4 u, float (&v)[8]) {
+  unpack_bf2(u.x, v[0], v[1]);
+  unpack_bf2(u.y, v[2], v[3]);
+  unpack_bf2(u.z, v[4], v[5]);
+  unpack_bf2(u.w, v[6], v[7]);
 }
 
 template <bool NORM, bool ROPE, bool POOL>
-__global__ void __launch_bounds__(640) norm_rope_pool_kernel(NormRopeParams p) {
-  __shared__ float red[2 * 2 * 32];
-  __shared__ float s_rstd[2][256];
-  const int m = blockIdx.x, b = blockIdx.y;
+__global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParams p) {
+  extern __shared__ __align__(16) uint8_t nsm[];
+  const int nslots = 2 + (p.v_out != nullptr) + (p.x != nullptr && p.gate_out != nullptr);
+  const int slot_bytes = nslots * kNormRow;
+  float* s_rstd = reinterpret_cast<float*>(nsm + kNormRing * slot_bytes);  // [2][blk]
+  const int m = blockIdx.x, grp = blockIdx.y, b = blockIdx.z;
   const int dim = p.H * 128;
-  // the block is rounded up to whole warps; threads past H*16 only join the reductions
-  const bool active = threadIdx.x < p.H * 16;
-  const int j = active ? threadIdx.x : 0;
-  const int col = j * 8;
-  const int h = col >> 7, d0 = col & 127;
+  const int j = threadIdx.x;
+  const int h = grp * kNormHeads + (j >> 4);
+  const bool active = h < p.H;
+  const int col = active ? h * 128 + (j & 15) * 8 : 0;
+  const int d0 = (j & 15) * 8;
   const int t0 = m * p.blk;
   const int t1 = min(p.L, t0 + p.blk);
-  const float inv_dim = 1.0f / (float)dim;
-  // With the GEMM's per-tile sums of squares the norm needs no block reduction:
-  // the rstd of every token of the block is computed up front.
-  const bool use_ssq = NORM && p.ssq != nullptr;
-  if (use_ssq) {
-    const int nt = dim / 256, n = t1 - t0;
+  const int n = t1 - t0;
+  const bool has_v = p.v_out != nullptr;
+  const bool gate = p.x != nullptr && p.gate_out != nullptr;
+  const uint32_t ring = smem_u32(nsm);
+  auto issue = [&](int tl) {
+    if (tl < n && active) {
+      const int64_t row = (int64_t)b * p.L + t0 + tl;
+      const uint32_t slot = ring + (tl % kNormRing) * slot_bytes + j * 16;
+      cp_async16_ca(slot, p.q_in + row * p.ld_in + col);
+      cp_async16_ca(slot + kNormRow, p.k_in + row * p.ld_in + col);
+      if (has_v) cp_async16_ca(slot + 2 * kNormRow, p.v_in + row * p.ld_in + col);
+      if (gate) cp_async16_ca(slot + (2 + has_v) * kNormRow, p.x + row * p.ld_x + col);
+    }
+    cp_async_commit_grp();  // one group per token, empty past the block
+  };
+#pragma unroll
+  for (int i = 0; i < kNormRing; ++i) issue(i);
+  if (NORM) {
+    // rstd of every token of the block from the per-tile sums of squares
+    const int per = dim / p.ssq_tile;
     for (int i = threadIdx.x; i < 2 * n; i += blockDim.x) {
       const int which = i / n, tl = i - which * n;
-      const float* src = p.ssq + ((int64_t)b * p.L + t0 + tl) * p.ssq_ld + which * nt;
+      const float* src = p.ssq + ((int64_t)b * p.L + t0 + tl) * p.ssq_ld + which * per;
       float s = 0.f;
-      for (int k = 0; k < nt; ++k) s += src[k];
-      s_rstd[which][tl] = rsqrtf(s * inv_dim + p.eps);
+      for (int k = 0; k < per; ++k) s += src[k];
+      s_rstd[which * p.blk + tl] = rsqrtf(s * (1.0f / (float)dim) + p.eps);
     }
     __syncthreads();
   }
-
   float wq[8], wk[8];
-  if (NORM) {
+  if (NORM && active) {
     load8(p.norm_wq + col, wq);
     load8(p.norm_wk + col, wk);
   }
   float gw[8];
-  const bool gate = p.x != nullptr && p.gate_out != nullptr;
-  if (gate) load8(p.gate_w + d0, gw);
-  const float gbias = gate ? bf2f(p.gate_b[h]) : 0.f;
-
+  if (gate && active) load8(p.gate_w + d0, gw);
+  const float gbias = (gate && active) ? bf2f(p.gate_b[h]) : 0.f;
   float qs[8], ks[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) qs[i] = ks[i] = 0.f;
 
-  // one token ahead in registers so its loads overlap this token's work
-  float q[8], k[8], xv[8];
-  auto load_tok = [&](int t, float (&qq)[8], float (&kk)[8], float (&xx)[8]) {
-    const int64_t row = (int64_t)b * p.L + t;
-    load8(p.q_in + row * p.ld_in + col, qq);
-    load8(p.k_in + row * p.ld_in + col, kk);
-    if (gate) load8(p.x + row * p.ld_x + col, xx);
-  };
-  if (t0 < t1) load_tok(t0, q, k, xv);
-  int parity = 0;
 #pragma unroll 1
-  for (int t = t0; t < t1; ++t, parity ^= 1) {
+  for (int tl = 0; tl < n; ++tl) {
+    cp_async_wait_grp<kNormRing - 1>();  // this token's chunks have landed
+    const int t = t0 + tl;
     const int64_t row = (int64_t)b * p.L + t;
-    float qn[8], kn[8], xn[8];
-    if (t + 1 < t1) load_tok(t + 1, qn, kn, xn);
-    if (!active) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) q[i] = k[i] = 0.f;
-    }
-    if (p.v_out != nullptr && active) {
-      float v[8];
-      load8(p.v_in + row * p.ld_in + col, v);
-      store8(p.v_out + out_offset(p, b, t, col), v);
-    }
+    const uint8_t* slot = nsm + (tl % kNormRing) * slot_bytes + j * 16;
+    float q[8], k[8], xv[8];
+    unpack8(*reinterpret_cast<const uint4*>(slot), q);
+    unpack8(*reinterpret_cast<const uint4*>(slot + kNormRow), k);
+    uint4 vraw = make_uint4(0, 0, 0, 0);
+    if (has_v) vraw = *reinterpret_cast<const uint4*>(slot + 2 * kNormRow);
+    if (gate) unpack8(*reinterpret_cast<const uint4*>(slot + (2 + has_v) * kNormRow), xv);
+    issue(tl + kNormRing);  // refill the slot just read (own chunks only)
+    if (!active) continue;
+    if (has_v) *reinterpret_cast<uint4*>(p.v_out + out_offset(p, b, t, col)) = vraw;
     if (NORM) {
-      float rq, rk;
-      if (use_ssq) {
-        rq = s_rstd[0][t - t0];
-        rk = s_rstd[1][t - t0];
-      } else {
-        float ss[2] = {0.f, 0.f};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          ss[0] = fmaf(q[i], q[i], ss[0]);
-          ss[1] = fmaf(k[i], k[i], ss[1]);
-        }
-        block_sum<2>(ss, red, parity);
-        rq = rsqrtf(ss[0] * inv_dim + p.eps);
-        rk = rsqrtf(ss[1] * inv_dim + p.eps);
-      }
+      const float rq = s_rstd[tl], rk = s_rstd[p.blk + tl];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         q[i] = rbf(rbf(q[i] * rq) * wq[i]);  // unit in bf16, then x weight in bf16
         k[i] = rbf(rbf(k[i] * rk) * wk[i]);
       }
-      if (p.q_normed && active) store8(p.q_normed + out_offset(p, b, t, col), q);
-      if (p.k_normed && active) store8(p.k_normed + out_offset(p, b, t, col), k);
+      if (p.q_normed) store8(p.q_normed + out_offset(p, b, t, col), q);
+      if (p.k_normed) store8(p.k_normed + out_offset(p, b, t, col), k);
     }
     if (ROPE) {
       const float4* cs = reinterpret_cast<const float4*>(p.cos_sin + (int64_t)t * 128 + d0);
@@ -182,8 +177,8 @@ __global__ void __launch_bounds__(640) norm_rope_pool_kernel(NormRopeParams p) {
         kr[e1] = rbf(k[e1] * c.z - k[e1 + 1] * c.w);
         kr[e1 + 1] = rbf(k[e1] * c.w + k[e1 + 1] * c.z);
       }
-      if (p.q_rope && active) store8(p.q_rope + row * dim + col, qr);
-      if (p.k_rope && active) store8(p.k_rope + row * dim + col, kr);
+      if (p.q_rope) store8(p.q_rope + row * dim + col, qr);
+      if (p.k_rope) store8(p.k_rope + row * dim + col, kr);
       if (POOL) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -196,23 +191,20 @@ __global__ void __launch_bounds__(640) norm_rope_pool_kernel(NormRopeParams p) {
       float g = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) g = fmaf(xv[i], gw[i], g);
+      // the 16 lanes of one head (the other half-warp may be an absent head)
+      const unsigned half = 0xffffu << (threadIdx.x & 16);
 #pragma unroll
-      for (int o = 8; o > 0; o >>= 1) g += __shfl_xor_sync(0xffffffffu, g, o);  // 16 lanes of one head
-      if ((j & 15) == 0 && active) {
+      for (int o = 8; o > 0; o >>= 1) g += __shfl_xor_sync(half, g, o);
+      if ((j & 15) == 0) {
         const float lin = rbf(g);
         const float logit = rbf(lin + gbias);
         p.gate_out[gate_offset(p, b, t, h)] = f2bf(1.0f / (1.0f + expf(-logit)));
       }
     }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      q[i] = qn[i];
-      k[i] = kn[i];
-      xv[i] = xn[i];
-    }
   }
+  cp_async_wait_grp<0>();
   if (POOL && active) {
-    const float nx = (float)(t1 - t0);
+    const float nx = (float)n;
     float pq[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) pq[i] = __fdiv_rn(qs[i], nx);
@@ -223,15 +215,52 @@ __global__ void __launch_bounds__(640) norm_rope_pool_kernel(NormRopeParams p) {
   }
 }
 
+// per-row sums of squares of q and k over tiles of 128 columns (q tiles, then k tiles)
+__global__ void row_ssq_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k, int64_t ld,
+                               int64_t rows, int dim, float* __restrict__ ssq) {
+  const int tiles = dim / 128;
+  const int64_t gid = (int64_t)blockIdx.x * (blockDim.x / 16) + (threadIdx.x >> 4);  // (row, which, tile)
+  const int sub = threadIdx.x & 15;
+  if (gid >= rows * 2 * tiles) return;
+  const int64_t row = gid / (2 * tiles);
+  const int which = (int)((gid / tiles) % 2), tile = (int)(gid % tiles);
+  const __nv_bfloat16* src = (which ? k : q) + row * ld + tile * 128 + sub * 8;
+  float v[8];
+  load8(src, v);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s = fmaf(v[i], v[i], s);
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (sub == 0) ssq[row * 2 * tiles + which * tiles + tile] = s;
+}
+
+int launch_row_ssq(const __nv_bfloat16* q, const __nv_bfloat16* k, int64_t ld, int64_t rows, int dim, float* ssq,
+                   cudaStream_t s) {
+  const int64_t items = rows * 2 * (dim / 128);
+  const int per_block = 256 / 16;
+  row_ssq_kernel<<<(unsigned)((items + per_block - 1) / per_block), 256, 0, s>>>(q, k, ld, rows, dim, ssq);
+  return (int)cudaGetLastError();
+}
+
 int launch_norm_rope_pool(const NormRopeParams& p, bool norm, bool rope, bool pool, cudaStream_t s) {
-  dim3 grid(p.NB, p.B);
-  dim3 block((p.H * 16 + 31) / 32 * 32);
-  if (norm && rope && pool) norm_rope_pool_kernel<true, true, true><<<grid, block, 0, s>>>(p);
-  else if (norm && rope) norm_rope_pool_kernel<true, true, false><<<grid, block, 0, s>>>(p);
-  else if (norm) norm_rope_pool_kernel<true, false, false><<<grid, block, 0, s>>>(p);
-  else if (rope && pool) norm_rope_pool_kernel<false, true, true><<<grid, block, 0, s>>>(p);
-  else if (rope) norm_rope_pool_kernel<false, true, false><<<grid, block, 0, s>>>(p);
+  if (norm && (p.ssq == nullptr || p.ssq_tile <= 0 || (p.H * 128) % p.ssq_tile != 0)) return -1;
+  const int nslots = 2 + (p.v_out != nullptr) + (p.x != nullptr && p.gate_out != nullptr);
+  const int smem = kNormRing * nslots * kNormRow + (norm ? 2 * p.blk * (int)sizeof(float) : 0);
+  if (smem > 227 * 1024) return -1;
+  dim3 grid(p.NB, (p.H + kNormHeads - 1) / kNormHeads, p.B);
+#define ROLA_NORM(N, R, P)                                                                              \
+  do {                                                                                                  \
+    cudaFuncSetAttribute(norm_stream_kernel<N, R, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+    norm_stream_kernel<N, R, P><<<grid, kNormThreads, smem, s>>>(p);                                    \
+  } while (0)
+  if (norm && rope && pool) ROLA_NORM(true, true, true);
+  else if (norm && rope) ROLA_NORM(true, true, false);
+  else if (norm) ROLA_NORM(true, false, false);
+  else if (rope && pool) ROLA_NORM(false, true, true);
+  else if (rope) ROLA_NORM(false, true, false);
   else return -1;
+#undef ROLA_NORM
   return (int)cudaGetLastError();
 }
 

@@ -245,7 +245,7 @@ int launch_topk(const float* scores, int rows, int NBk, int k, int32_t* lut, cud
 // every score accumulated over d in order (the same FMA chain as
 // scores_kernel), then the warp picks each row's top-k exactly as topk_kernel.
 // ---------------------------------------------------------------------------
-constexpr int kSelRows = 64;          // query blocks per CTA (8 per warp, 4 at a time)
+constexpr int kSelRows = 64;          // query blocks per CTA (16 warps x 4 rows)
 constexpr int kSelWords = 65;         // smem row stride of pooled K, 32-bit words
 constexpr int kSelMaxNBk = 768;       // shared-memory bound of the fused kernel
 
@@ -287,7 +287,7 @@ __device__ __forceinline__ void warp_topk_emit(const float (&acc)[PER], int per,
 }
 
 template <int PER>
-__global__ void __launch_bounds__(256) select_fused_kernel(const __nv_bfloat16* __restrict__ pq,
+__global__ void __launch_bounds__(512) select_fused_kernel(const __nv_bfloat16* __restrict__ pq,
                                                            const __nv_bfloat16* __restrict__ pk, int NBq, int NBk,
                                                            int k, int32_t* __restrict__ lut) {
   extern __shared__ uint32_t sel_smem[];
@@ -296,14 +296,25 @@ __global__ void __launch_bounds__(256) select_fused_kernel(const __nv_bfloat16* 
   const int bh = blockIdx.y;
   const int m0 = blockIdx.x * kSelRows;
   const uint4* kb = reinterpret_cast<const uint4*>(pk + (int64_t)bh * NBk * 128);
-  for (int i = threadIdx.x; i < NBk * 16; i += blockDim.x) {
-    const int r = i >> 4, w = (i & 15) * 4;
-    const uint4 u = kb[i];
-    uint32_t* d = sk + r * kSelWords + w;
-    d[0] = u.x;
-    d[1] = u.y;
-    d[2] = u.z;
-    d[3] = u.w;
+  // staging: eight 16-byte loads in flight per thread before their smem stores
+  for (int i0 = threadIdx.x; i0 < NBk * 16; i0 += 8 * blockDim.x) {
+    uint4 u[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int i = i0 + e * blockDim.x;
+      u[e] = i < NBk * 16 ? kb[i] : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int i = i0 + e * blockDim.x;
+      if (i < NBk * 16) {
+        uint32_t* d = sk + (i >> 4) * kSelWords + (i & 15) * 4;
+        d[0] = u[e].x;
+        d[1] = u[e].y;
+        d[2] = u[e].z;
+        d[3] = u[e].w;
+      }
+    }
   }
   const uint4* qb = reinterpret_cast<const uint4*>(pq + (int64_t)bh * NBq * 128);
   for (int i = threadIdx.x; i < kSelRows * 16; i += blockDim.x) {
@@ -314,9 +325,9 @@ __global__ void __launch_bounds__(256) select_fused_kernel(const __nv_bfloat16* 
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per = (NBk + 31) / 32;
-  for (int g = 0; g < 2; ++g) {
-    const int rr0 = warp * 8 + g * 4;  // 4 query rows of this pass
-    if (m0 + rr0 >= NBq) break;
+  {
+    const int rr0 = warp * 4;  // the 4 query rows of this warp
+    if (m0 + rr0 >= NBq) return;
     float acc[4][PER];
 #pragma unroll
     for (int a = 0; a < 4; ++a)
@@ -358,11 +369,12 @@ int launch_select_fused(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH
 #define ROLA_SEL(P)                                                                                  \
   do {                                                                                               \
     cudaFuncSetAttribute(select_fused_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-    select_fused_kernel<P><<<grid, 256, smem, s>>>(pq, pk, NBq, NBk, k, lut);                        \
+    select_fused_kernel<P><<<grid, 512, smem, s>>>(pq, pk, NBq, NBk, k, lut);                        \
   } while (0)
   if (per <= 4) ROLA_SEL(4);
   else if (per <= 8) ROLA_SEL(8);
   else if (per <= 16) ROLA_SEL(16);
+  else if (per <= 20) ROLA_SEL(20);
   else ROLA_SEL(24);
 #undef ROLA_SEL
   return (int)cudaGetLastError();
