@@ -53,6 +53,8 @@ def parse_args():
     ap.add_argument("--workload", default="C4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
+                    help="N>1: sequence<->head exchanges fused into the kernels over peer memory, or NCCL all-to-all")
     return ap.parse_args()
 
 
@@ -275,7 +277,8 @@ def main():
         from sparkdiffusion_b200.ulysses import ulysses_rola_attention_params
 
         def step(xin, events=None):
-            return ulysses_rola_attention_params(xin, w_qkv, None, *common, H, wl.topk, group, events=events)
+            return ulysses_rola_attention_params(xin, w_qkv, None, *common, H, wl.topk, group, events=events,
+                                                 transport=args.transport)
 
     # exact selected-block FLOPs from this layer's LUT.  Every rank runs the
     # 1-GPU pipeline once on the full hidden states (selection is bit-exact and
@@ -391,6 +394,8 @@ def main():
         "data": "synthetic (seeded N(0,1) hidden states, N(0,0.02) QKV weights, random low-rank/gate factors)",
         "config": {"workload": workload_desc(wl), "global_batch": B, "seq_len": L,
                    "parallelism": f"ulysses{world}" if world > 1 else "single",
+                   "exchange": (f"fused into the norm pass and attention epilogue (peer stores)"
+                                if args.transport == "peer" else "NCCL all_to_all_single") if world > 1 else None,
                    "l2": "inputs larger than L2 (hidden states 774 MB, QKV 2.3 GB per layer); no flush"},
         "flops_per_layer": flops_total,
         "roofline": roof(dominant, gemm_ach if dominant == "gemm" else attn_ach),
@@ -405,6 +410,9 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        from sparkdiffusion_b200 import peer
+
+        peer.release_all()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -28,7 +28,8 @@ extern "C" {
 
 typedef void* rola_stream_t;
 
-#define ROLA_B200_ABI_VERSION 1
+#define ROLA_B200_ABI_VERSION 2
+#define ROLA_PEER_HANDLE_BYTES 64
 
 #define ROLA_OK 0
 #define ROLA_ERR_INVALID 1 /* bad shape, size, alignment or null pointer */
@@ -88,6 +89,22 @@ int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_r
                            int ssq_ld, const void* x, const void* norm_wq, const void* norm_wk, const void* gate_w,
                            const void* gate_b, int B, int L, int H, int heads_per_chunk, float eps, void* q_send,
                            void* k_send, void* v_send, void* gate_out, rola_stream_t stream);
+
+/* qk_norm_pack with the sequence->head exchange fused into its stores: this
+ * rank (of world ranks on one node) holds tokens [rank*Ls, (rank+1)*Ls); the
+ * q_normed, k_normed and v rows of heads [r*Hl, (r+1)*Hl) (Hl = H / world) go
+ * straight into rank r's buffers q_dst[r], k_dst[r], v_dst[r], each
+ * [B, world*Ls, Hl*D] token-major, at row rank*Ls + t, and the gate into
+ * g_dst[r] [B, world*Ls, Hl].  The destinations are peer mappings
+ * (rola_b200_peer_open); the kernel ends with a system-scope fence, so a
+ * stream-ordered barrier of all ranks after it makes the rows visible.
+ * world <= 8.  No counterpart in the reference, whose context parallelism
+ * (sparkdiffusion/utils/a2a_cp.py:146-186) exchanges with NCCL all-to-all. */
+int rola_b200_qk_norm_scatter(const void* q_raw, const void* k_raw, const void* v_raw, int64_t ld_raw,
+                              const float* ssq, int ssq_ld, const void* x, const void* norm_wq, const void* norm_wk,
+                              const void* gate_w, const void* gate_b, int B, int Ls, int H, int world, int rank,
+                              float eps, void* const* q_dst, void* const* k_dst, void* const* v_dst,
+                              void* const* g_dst, rola_stream_t stream);
 
 /* Head-parallel half (after the all-to-all): RoPE, q-pool and k block sums from
  * the normed q/k (token-major, row stride ld).  Same reference interface as
@@ -154,6 +171,28 @@ int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t q
                           int topk, const void* q_lr, const void* Ct, const void* gate, const void* x, int64_t x_sB,
                           int64_t x_sH, int64_t x_sT, const void* gate_w, const void* gate_b, float eps_lr, void* out,
                           void* o_sparse, int64_t o_sB, int64_t o_sH, int64_t o_sT, rola_stream_t stream);
+
+/* rola_b200_sparse_attn with the head->sequence exchange fused into the
+ * epilogue store: this rank computed heads [head_offset, head_offset + H) of
+ * all L tokens; output row t goes to rank owner = t / (L / world), into
+ * out_dst[owner] [B, L / world, H_total*D] at row t - owner*(L / world),
+ * columns (head_offset + h)*D.  Gate values (gate [B*L, H]) and the low-rank
+ * branch are required.  world <= 8 and divides L.  No counterpart in the
+ * reference (see rola_b200_qk_norm_scatter). */
+int rola_b200_sparse_attn_scatter(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT,
+                                  const void* v, int64_t v_sB, int64_t v_sH, int64_t v_sT, const int32_t* lut, int B,
+                                  int L, int H, int blk, int topk, const void* q_lr, const void* Ct, const void* gate,
+                                  float eps_lr, void* const* out_dst, int world, int head_offset, int H_total,
+                                  rola_stream_t stream);
+
+/* Peer memory of the fused exchanges (CUDA IPC; no counterpart in the
+ * reference).  peer_alloc: cudaMalloc of bytes on the current device and its
+ * ROLA_PEER_HANDLE_BYTES-byte IPC handle; peer_open: map a handle made by
+ * another process of the node; peer_close / peer_free undo them. */
+int rola_b200_peer_alloc(size_t bytes, void** ptr, unsigned char* handle);
+int rola_b200_peer_open(const unsigned char* handle, void** ptr);
+int rola_b200_peer_close(void* ptr);
+int rola_b200_peer_free(void* ptr);
 
 /* Allocation-free variant of rola_b200_lowrank_kv.  No counterpart in the
  * reference: SparkDiffusion lets PyTorch allocate every temporary.

@@ -13,7 +13,8 @@ import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "librola_b200.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
+PEER_HANDLE_BYTES = 64
 
 ROLA_OK = 0
 ROLA_ERR_INVALID = 1
@@ -44,6 +45,8 @@ SIGNATURES = {
                                _P, _P, _P, _P, _P, _P, _P, _P],
     "rola_b200_qk_norm_pack": [_P, _P, _P, _L, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F,
                                _P, _P, _P, _P, _P],
+    "rola_b200_qk_norm_scatter": [_P, _P, _P, _L, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F,
+                                  _P, _P, _P, _P, _P],
     "rola_b200_rope_pool": [_P, _P, _L, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P],
     "rola_b200_mean_pool": [_P, _L, _L, _L, _I, _I, _I, _I, _P, _P, _P],
     "rola_b200_smooth_k_center": [_P, _L, _L, _L, _I, _I, _I, _I, _P, _P, _P],
@@ -54,6 +57,12 @@ SIGNATURES = {
                              _P, _P, _P, _P],
     "rola_b200_sparse_attn": [_P, _P, _L, _L, _L, _P, _L, _L, _L, _P, _I, _I, _I, _I, _I, _P, _P, _P,
                               _P, _L, _L, _L, _P, _P, _F, _P, _P, _L, _L, _L, _P],
+    "rola_b200_sparse_attn_scatter": [_P, _P, _L, _L, _L, _P, _L, _L, _L, _P, _I, _I, _I, _I, _I, _P, _P,
+                                      _P, _F, _P, _I, _I, _I, _P],
+    "rola_b200_peer_alloc": [_Z, ctypes.POINTER(_P), _P],
+    "rola_b200_peer_open": [_P, ctypes.POINTER(_P)],
+    "rola_b200_peer_close": [_P],
+    "rola_b200_peer_free": [_P],
     "rola_b200_lowrank_kv_noalloc": [_P, _L, _L, _L, _P, _L, _L, _L, _P, _P, _P, _I, _I, _I, _I, _I, _I,
                                      _P, _P, _P],
     "rola_b200_forward_workspace_bytes": [_I, _I, _I, _I, _I, _I],

@@ -355,6 +355,11 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         lowrank = __all_sync(0xffffffffu, mbar_wait(bar(B_LR0 + t), 0, abort_flag, kDevTimeoutMma));
       ok = ok && (lowrank || !p.has_lowrank);
       tc_fence_after();
+      // Staging tile of the output: the Q tile of this tile is free once its
+      // last MMAs completed (OF/LR above).  128 rows x 256 B, the 16-byte
+      // chunk k of row r at chunk k ^ (r & 7) (conflict-free both ways).
+      uint8_t* stage = gbase + OFF_Q + t * 2 * TILE;
+      const bool staged = p.out != nullptr || p.peer_n > 0;
       if (ok) {
         const int tok = (m0 + t) * 128 + row;
         const float inv_l = 1.0f / l_run;
@@ -414,7 +419,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             gate = bf2f(p.gate[((int64_t)b * p.L + tok) * p.H + h]);
           }
         }
-        // pass 2: fuse and store (TMEM loads by the whole warp, stores only for rows < L)
+        // pass 2: fuse (TMEM loads by the whole warp).  The fused row goes to
+        // the staging tile (stored out coalesced below); o_sparse directly.
         const bool store = tok < p.L;
         const int64_t orow = (int64_t)b * p.o_sB + (int64_t)h * p.o_sH + (int64_t)tok * p.o_sT;
 #pragma unroll 1
@@ -438,10 +444,11 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
               wo[e] = ws[e];
             }
           }
-          if (p.out && store) {
-            uint4* dst = reinterpret_cast<uint4*>(p.out + orow + c * 16);
-            dst[0] = make_uint4(wo[0], wo[1], wo[2], wo[3]);
-            dst[1] = make_uint4(wo[4], wo[5], wo[6], wo[7]);
+          if (staged) {
+            *reinterpret_cast<uint4*>(stage + row * 256 + (((2 * c) ^ (row & 7)) << 4)) =
+                make_uint4(wo[0], wo[1], wo[2], wo[3]);
+            *reinterpret_cast<uint4*>(stage + row * 256 + (((2 * c + 1) ^ (row & 7)) << 4)) =
+                make_uint4(wo[4], wo[5], wo[6], wo[7]);
           }
           if (p.o_sparse && store) {
             uint4* dst = reinterpret_cast<uint4*>(p.o_sparse + orow + c * 16);
@@ -450,10 +457,41 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           }
         }
       }
+      if (staged) {
+        // coalesced store of the tile: 16 lanes per row, 2 rows per warp
+        // instruction; rows of a warp whose epilogue did not run are skipped.
+        // Every warp of the warpgroup reaches the named barrier (no early exit).
+        int* ok_flags = reinterpret_cast<int*>(gbase + OFF_BAR + 8 * B_COUNT + 16);
+        if (lane == 0) ok_flags[t * 4 + q] = ok ? 1 : 0;
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");
+        const int tid = q * 32 + lane;
+        const int chunk = tid & 15;
+#pragma unroll 4
+        for (int it = 0; it < 16; ++it) {
+          const int r = it * 8 + (tid >> 4);
+          const int tk = (m0 + t) * 128 + r;
+          if (tk >= p.L || ok_flags[t * 4 + (r >> 5)] == 0) continue;
+          const uint4 val = *reinterpret_cast<const uint4*>(stage + r * 256 + ((chunk ^ (r & 7)) << 4));
+          __nv_bfloat16* dst;
+          if (p.peer_n > 0) {
+            // head->sequence exchange: the row goes straight to the rank that owns token tk
+            const int owner = tk / p.peer_Ls;
+            dst = p.out_peer[owner] + (int64_t)b * p.peer_sB + (int64_t)(tk - owner * p.peer_Ls) * p.peer_sT +
+                  (int64_t)(p.head_offset + h) * 128;
+          } else {
+            dst = p.out + (int64_t)b * p.o_sB + (int64_t)h * p.o_sH + (int64_t)tk * p.o_sT;
+          }
+          *reinterpret_cast<uint4*>(dst + chunk * 8) = val;
+        }
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
+  // rows stored into peers' memory: one system-scope fence per CTA after the
+  // block barrier orders every thread's rows before the kernel's completion is
+  // signalled to the other ranks
+  if (p.peer_n > 0 && threadIdx.x == 0) __threadfence_system();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();

@@ -199,9 +199,10 @@ int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw,
   p.gate_b = BF(gate_b);
   p.q_rope = BFm(q_rope);
   p.k_rope = BFm(k_rope);
-  p.q_normed = BFm(q_normed);
-  p.k_normed = BFm(k_normed);
-  p.gate_out = x ? BFm(gate_out) : nullptr;
+  p.qn_dst[0] = BFm(q_normed);
+  p.kn_dst[0] = BFm(k_normed);
+  p.g_dst[0] = x ? BFm(gate_out) : nullptr;
+  p.dst_sB = (int64_t)L * H * 128;
   p.pooled_q = BFm(pooled_q);
   p.ksum = ksum;
   p.B = B;
@@ -220,8 +221,9 @@ int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_r
                            void* k_send, void* v_send, void* gate_out, rola_stream_t stream) {
   ROLA_CHECK(q_raw && k_raw && v_raw && norm_wq && norm_wk && q_send && k_send && v_send,
              "qk_norm_pack: null pointer");
-  ROLA_CHECK(B > 0 && L > 0 && H > 0 && heads_per_chunk > 0 && H % heads_per_chunk == 0,
-             "qk_norm_pack: bad sizes");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && heads_per_chunk > 0 && H % heads_per_chunk == 0 &&
+                 H / heads_per_chunk <= kMaxChunks,
+             "qk_norm_pack: bad sizes (at most 8 head chunks)");
   ROLA_CHECK(ld_raw % 8 == 0, "qk_norm_pack: 16-byte aligned rows required");
   ROLA_CHECK(x == nullptr || (gate_w && gate_b && gate_out), "qk_norm_pack: the gate needs gate_w, gate_b, gate_out");
   ROLA_CHECK(ssq == nullptr || (H % 2 == 0 && ssq_ld >= H), "qk_norm_pack: sums of squares need an even head count");
@@ -236,10 +238,15 @@ int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_r
   p.norm_wk = BF(norm_wk);
   p.gate_w = BF(gate_w);
   p.gate_b = BF(gate_b);
-  p.q_normed = BFm(q_send);
-  p.k_normed = BFm(k_send);
-  p.v_out = BFm(v_send);
-  p.gate_out = x ? BFm(gate_out) : nullptr;
+  // send block c of batch b: [B][H / heads_per_chunk][L][heads_per_chunk * D]
+  for (int c = 0; c < H / heads_per_chunk && c < kMaxChunks; ++c) {
+    const int64_t off = (int64_t)c * L * heads_per_chunk * 128;
+    p.qn_dst[c] = BFm(q_send) + off;
+    p.kn_dst[c] = BFm(k_send) + off;
+    p.v_dst[c] = BFm(v_send) + off;
+    p.g_dst[c] = x ? BFm(gate_out) + (int64_t)c * L * heads_per_chunk : nullptr;
+  }
+  p.dst_sB = (int64_t)L * H * 128;
   p.B = B;
   p.L = L;
   p.H = H;
@@ -248,6 +255,53 @@ int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_r
   p.heads_per_chunk = heads_per_chunk;
   p.eps = eps;
   return run_norm_pass(p, true, false, false, ssq, ssq_ld, S(stream), "qk_norm_pack");
+}
+
+int rola_b200_qk_norm_scatter(const void* q_raw, const void* k_raw, const void* v_raw, int64_t ld_raw,
+                              const float* ssq, int ssq_ld, const void* x, const void* norm_wq, const void* norm_wk,
+                              const void* gate_w, const void* gate_b, int B, int Ls, int H, int world, int rank,
+                              float eps, void* const* q_dst, void* const* k_dst, void* const* v_dst,
+                              void* const* g_dst, rola_stream_t stream) {
+  ROLA_CHECK(q_raw && k_raw && v_raw && norm_wq && norm_wk && x && gate_w && gate_b && q_dst && k_dst && v_dst && g_dst,
+             "qk_norm_scatter: null pointer");
+  ROLA_CHECK(world >= 1 && world <= kMaxChunks && rank >= 0 && rank < world, "qk_norm_scatter: bad rank/world (<= 8)");
+  ROLA_CHECK(B > 0 && Ls > 0 && H > 0 && H % world == 0, "qk_norm_scatter: world must divide the head count");
+  ROLA_CHECK(ld_raw % 8 == 0 && aligned16(q_raw) && aligned16(k_raw) && aligned16(v_raw) && aligned16(x),
+             "qk_norm_scatter: 16-byte aligned rows required");
+  ROLA_CHECK(ssq == nullptr || (H % 2 == 0 && ssq_ld >= H), "qk_norm_scatter: sums of squares need an even head count");
+  for (int r = 0; r < world; ++r)
+    ROLA_CHECK(q_dst[r] && k_dst[r] && v_dst[r] && g_dst[r] && aligned16(q_dst[r]) && aligned16(k_dst[r]) &&
+                   aligned16(v_dst[r]),
+               "qk_norm_scatter: destination %d null or not 16-byte aligned", r);
+  NormRopeParams p{};
+  p.q_in = BF(q_raw);
+  p.k_in = BF(k_raw);
+  p.v_in = BF(v_raw);
+  p.ld_in = ld_raw;
+  p.x = BF(x);
+  p.ld_x = (int64_t)H * 128;
+  p.norm_wq = BF(norm_wq);
+  p.norm_wk = BF(norm_wk);
+  p.gate_w = BF(gate_w);
+  p.gate_b = BF(gate_b);
+  // destination r holds heads [r*Hl, (r+1)*Hl) of all world*Ls tokens; this
+  // rank's tokens start at row rank*Ls there
+  for (int r = 0; r < world; ++r) {
+    p.qn_dst[r] = BFm(q_dst[r]);
+    p.kn_dst[r] = BFm(k_dst[r]);
+    p.v_dst[r] = BFm(v_dst[r]);
+    p.g_dst[r] = BFm(g_dst[r]);
+  }
+  p.dst_sB = (int64_t)Ls * H * 128;
+  p.dst_t0 = rank * Ls;
+  p.B = B;
+  p.L = Ls;
+  p.H = H;
+  p.blk = 128;
+  p.NB = (Ls + 127) / 128;
+  p.heads_per_chunk = H / world;
+  p.eps = eps;
+  return run_norm_pass(p, true, false, false, ssq, ssq_ld, S(stream), "qk_norm_scatter");
 }
 
 int rola_b200_rope_pool(const void* q_normed, const void* k_normed, int64_t ld, const float* cos_sin, int B, int L,
@@ -388,13 +442,20 @@ static int make_head_map(CUtensorMap* m, const void* ptr, int cols, int64_t sB, 
   return make_map(m, ptr, 4, dims, strides, box, what);
 }
 
-int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT, const void* v,
-                          int64_t v_sB, int64_t v_sH, int64_t v_sT, const int32_t* lut, int B, int L, int H, int blk,
-                          int topk, const void* q_lr, const void* Ct, const void* gate, const void* x, int64_t x_sB,
-                          int64_t x_sH, int64_t x_sT, const void* gate_w, const void* gate_b, float eps_lr, void* out,
-                          void* o_sparse, int64_t o_sB, int64_t o_sH, int64_t o_sT, rola_stream_t stream) {
+// Output routing of the head->sequence exchange fused into the attention store.
+struct PeerOut {
+  void* const* dst;  // dst[r]: rank r's output buffer [B, L / world, H_total * D]
+  int world, head_offset, H_total;
+};
+
+static int sparse_attn_impl(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT, const void* v,
+                            int64_t v_sB, int64_t v_sH, int64_t v_sT, const int32_t* lut, int B, int L, int H, int blk,
+                            int topk, const void* q_lr, const void* Ct, const void* gate, const void* x, int64_t x_sB,
+                            int64_t x_sH, int64_t x_sT, const void* gate_w, const void* gate_b, float eps_lr,
+                            void* out, void* o_sparse, int64_t o_sB, int64_t o_sH, int64_t o_sT, const PeerOut* peer,
+                            rola_stream_t stream) {
   ROLA_CHECK(q && k && v && lut, "sparse_attn: null pointer");
-  ROLA_CHECK(out || o_sparse, "sparse_attn: no output requested");
+  ROLA_CHECK(out || o_sparse || peer, "sparse_attn: no output requested");
   ROLA_CHECK(blk == 128, "sparse_attn: block size must be 128");
   ROLA_CHECK(B > 0 && L > 0 && H > 0 && (int64_t)B * H < 65536, "sparse_attn: bad sizes");
   const int NB = (L + blk - 1) / blk;
@@ -442,7 +503,39 @@ int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t q
   p.qk_scale = (float)(0.08838834764831845 * 1.4426950408889634);  // 128^-0.5 * log2(e)
   p.eps_lr = eps_lr;
   p.rescale_threshold = 0.0f;
+  if (peer) {
+    p.peer_n = peer->world;
+    p.peer_Ls = L / peer->world;
+    p.head_offset = peer->head_offset;
+    p.peer_sT = (int64_t)peer->H_total * 128;
+    p.peer_sB = p.peer_Ls * p.peer_sT;
+    for (int r = 0; r < peer->world; ++r) p.out_peer[r] = BFm(peer->dst[r]);
+  }
   return cuda_status(launch_sparse_attn(tq, tk, tv, tqlr, tct, tx, p, S(stream)), "sparse_attn");
+}
+
+int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT, const void* v,
+                          int64_t v_sB, int64_t v_sH, int64_t v_sT, const int32_t* lut, int B, int L, int H, int blk,
+                          int topk, const void* q_lr, const void* Ct, const void* gate, const void* x, int64_t x_sB,
+                          int64_t x_sH, int64_t x_sT, const void* gate_w, const void* gate_b, float eps_lr, void* out,
+                          void* o_sparse, int64_t o_sB, int64_t o_sH, int64_t o_sT, rola_stream_t stream) {
+  return sparse_attn_impl(q, k, qk_sB, qk_sH, qk_sT, v, v_sB, v_sH, v_sT, lut, B, L, H, blk, topk, q_lr, Ct, gate, x,
+                          x_sB, x_sH, x_sT, gate_w, gate_b, eps_lr, out, o_sparse, o_sB, o_sH, o_sT, nullptr, stream);
+}
+
+int rola_b200_sparse_attn_scatter(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT,
+                                  const void* v, int64_t v_sB, int64_t v_sH, int64_t v_sT, const int32_t* lut, int B,
+                                  int L, int H, int blk, int topk, const void* q_lr, const void* Ct, const void* gate,
+                                  float eps_lr, void* const* out_dst, int world, int head_offset, int H_total,
+                                  rola_stream_t stream) {
+  ROLA_CHECK(out_dst && q_lr && gate, "sparse_attn_scatter: null pointer");
+  ROLA_CHECK(world >= 1 && world <= kMaxChunks && L % world == 0, "sparse_attn_scatter: world must divide L (<= 8 ranks)");
+  ROLA_CHECK(head_offset >= 0 && head_offset + H <= H_total, "sparse_attn_scatter: head range outside H_total");
+  for (int r = 0; r < world; ++r)
+    ROLA_CHECK(out_dst[r] && aligned16(out_dst[r]), "sparse_attn_scatter: output %d null or not 16-byte aligned", r);
+  const PeerOut peer{out_dst, world, head_offset, H_total};
+  return sparse_attn_impl(q, k, qk_sB, qk_sH, qk_sT, v, v_sB, v_sH, v_sT, lut, B, L, H, blk, topk, q_lr, Ct, gate,
+                          nullptr, 0, 0, 0, nullptr, nullptr, eps_lr, nullptr, nullptr, 0, 0, 0, &peer, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -9,10 +9,11 @@
 namespace rola {
 
 // prologue.cu
+constexpr int kMaxChunks = 8;  // destinations of the sequence->head exchange (ranks of one node)
 struct NormRopeParams {
   const __nv_bfloat16* q_in;
   const __nv_bfloat16* k_in;
-  const __nv_bfloat16* v_in;  // only read when v_out != nullptr
+  const __nv_bfloat16* v_in;  // only read when v_dst[0] != nullptr
   int64_t ld_in;              // row stride (elements) of q_in/k_in/v_in
   const __nv_bfloat16* x;     // gate input [B*L, dim] (row stride ld_x) or nullptr
   int64_t ld_x;
@@ -24,10 +25,19 @@ struct NormRopeParams {
   // outputs (any may be nullptr)
   __nv_bfloat16* q_rope;  // [B*L, dim]
   __nv_bfloat16* k_rope;
-  __nv_bfloat16* q_normed;  // [B][H/heads_per_chunk][L][heads_per_chunk*D] (see out_offset)
-  __nv_bfloat16* k_normed;
-  __nv_bfloat16* v_out;
-  __nv_bfloat16* gate_out;  // [B][H/heads_per_chunk][L][heads_per_chunk]
+  // q_normed / k_normed / v / gate go out in head chunks of heads_per_chunk heads:
+  // chunk c of token t of batch b lands at
+  //   qn_dst[c] + b*dst_sB + (dst_t0 + t)*heads_per_chunk*D + column within the chunk
+  //   g_dst[c]  + b*(dst_sB/D) + (dst_t0 + t)*heads_per_chunk + head within the chunk
+  // (a null entry 0 disables that output).  One chunk of H heads is the plain
+  // token-major layout; p chunks into peers' buffers (dst_t0 = rank * L) is the
+  // sequence->head exchange itself.
+  __nv_bfloat16* qn_dst[kMaxChunks];
+  __nv_bfloat16* kn_dst[kMaxChunks];
+  __nv_bfloat16* v_dst[kMaxChunks];
+  __nv_bfloat16* g_dst[kMaxChunks];
+  int64_t dst_sB;
+  int dst_t0;
   __nv_bfloat16* pooled_q;  // [B, H, NB, D]
   float* ksum;              // [B, NB, dim]
   const float* ssq;         // [B*L, ssq_ld] per-tile sums of squares (q tiles, then k tiles); needed to normalise
@@ -95,6 +105,12 @@ struct AttnParams {
   __nv_bfloat16* out;         // fused output, element (b,h,t,d) at out + b*o_sB + h*o_sH + t*o_sT + d (nullptr: skip)
   int64_t o_sB, o_sH, o_sT;
   __nv_bfloat16* o_sparse;    // optional, same layout as out
+  // head->sequence exchange fused into the store (peer_n > 0, out unused): row t
+  // of head h goes to rank owner = t / peer_Ls at
+  //   out_peer[owner] + b*peer_sB + (t - owner*peer_Ls)*peer_sT + (head_offset + h)*D + d
+  __nv_bfloat16* out_peer[kMaxChunks];
+  int peer_n, peer_Ls, head_offset;
+  int64_t peer_sB, peer_sT;
   int B, L, H, NBq, NBk, topk, has_lowrank;
   float qk_scale;  // D^-1/2 * log2(e)
   float eps_lr;    // finfo(dtype).eps

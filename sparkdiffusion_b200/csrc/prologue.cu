@@ -19,20 +19,17 @@ namespace rola {
 
 
 
-// Output offset of (batch b, token t, hidden column c) in the chunked layout
-// [B][H / heads_per_chunk][L][heads_per_chunk * D]: one contiguous block per
-// destination rank of the sequence->head all-to-all.  With heads_per_chunk == H
-// this is the plain token-major [B, L, H*D] layout.
-__device__ __forceinline__ int64_t out_offset(const NormRopeParams& p, int b, int t, int col) {
+// Destination of (batch b, token t, hidden column col) of a chunked output
+// (see NormRopeParams): chunk = col / (heads_per_chunk * D).
+__device__ __forceinline__ __nv_bfloat16* chunk_dst(__nv_bfloat16* const (&table)[kMaxChunks],
+                                                    const NormRopeParams& p, int b, int t, int col) {
   const int chunk_cols = p.heads_per_chunk * 128;
   const int chunk = col / chunk_cols;
-  return (int64_t)b * p.L * (p.H * 128) + (int64_t)chunk * p.L * chunk_cols + (int64_t)t * chunk_cols +
-         (col - chunk * chunk_cols);
+  return table[chunk] + (int64_t)b * p.dst_sB + (int64_t)(p.dst_t0 + t) * chunk_cols + (col - chunk * chunk_cols);
 }
-// same layout for the per-(token, head) gate: [B][H / heads_per_chunk][L][heads_per_chunk]
-__device__ __forceinline__ int64_t gate_offset(const NormRopeParams& p, int b, int t, int h) {
+__device__ __forceinline__ __nv_bfloat16* gate_dst(const NormRopeParams& p, int b, int t, int h) {
   const int chunk = h / p.heads_per_chunk;
-  return (int64_t)b * p.L * p.H + (int64_t)chunk * p.L * p.heads_per_chunk + (int64_t)t * p.heads_per_chunk +
+  return p.g_dst[chunk] + (int64_t)b * (p.dst_sB / 128) + (int64_t)(p.dst_t0 + t) * p.heads_per_chunk +
          (h - chunk * p.heads_per_chunk);
 }
 
@@ -83,7 +80,7 @@ __device__ __forceinline__ void unpack8(const uint4 u, float (&v)[8]) {
 template <bool NORM, bool ROPE, bool POOL>
 __global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParams p) {
   extern __shared__ __align__(16) uint8_t nsm[];
-  const int nslots = 2 + (p.v_out != nullptr) + (p.x != nullptr && p.gate_out != nullptr);
+  const int nslots = 2 + (p.v_dst[0] != nullptr) + (p.x != nullptr && p.g_dst[0] != nullptr);
   const int slot_bytes = nslots * kNormRow;
   float* s_rstd = reinterpret_cast<float*>(nsm + kNormRing * slot_bytes);  // [2][blk]
   const int m = blockIdx.x, grp = blockIdx.y, b = blockIdx.z;
@@ -96,8 +93,8 @@ __global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParam
   const int t0 = m * p.blk;
   const int t1 = min(p.L, t0 + p.blk);
   const int n = t1 - t0;
-  const bool has_v = p.v_out != nullptr;
-  const bool gate = p.x != nullptr && p.gate_out != nullptr;
+  const bool has_v = p.v_dst[0] != nullptr;
+  const bool gate = p.x != nullptr && p.g_dst[0] != nullptr;
   const uint32_t ring = smem_u32(nsm);
   auto issue = [&](int tl) {
     if (tl < n && active) {
@@ -150,7 +147,7 @@ __global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParam
     if (gate) unpack8(*reinterpret_cast<const uint4*>(slot + (2 + has_v) * kNormRow), xv);
     issue(tl + kNormRing);  // refill the slot just read (own chunks only)
     if (!active) continue;
-    if (has_v) *reinterpret_cast<uint4*>(p.v_out + out_offset(p, b, t, col)) = vraw;
+    if (has_v) *reinterpret_cast<uint4*>(chunk_dst(p.v_dst, p, b, t, col)) = vraw;
     if (NORM) {
       const float rq = s_rstd[tl], rk = s_rstd[p.blk + tl];
 #pragma unroll
@@ -158,8 +155,8 @@ __global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParam
         q[i] = rbf(rbf(q[i] * rq) * wq[i]);  // unit in bf16, then x weight in bf16
         k[i] = rbf(rbf(k[i] * rk) * wk[i]);
       }
-      if (p.q_normed) store8(p.q_normed + out_offset(p, b, t, col), q);
-      if (p.k_normed) store8(p.k_normed + out_offset(p, b, t, col), k);
+      if (p.qn_dst[0]) store8(chunk_dst(p.qn_dst, p, b, t, col), q);
+      if (p.kn_dst[0]) store8(chunk_dst(p.kn_dst, p, b, t, col), k);
     }
     if (ROPE) {
       const float4* cs = reinterpret_cast<const float4*>(p.cos_sin + (int64_t)t * 128 + d0);
@@ -198,11 +195,18 @@ __global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParam
       if ((j & 15) == 0) {
         const float lin = rbf(g);
         const float logit = rbf(lin + gbias);
-        p.gate_out[gate_offset(p, b, t, h)] = f2bf(1.0f / (1.0f + expf(-logit)));
+        *gate_dst(p, b, t, h) = f2bf(1.0f / (1.0f + expf(-logit)));
       }
     }
   }
   cp_async_wait_grp<0>();
+  // chunked outputs may live in peers' memory: one system-scope fence per CTA
+  // after the block barrier orders every thread's rows before the kernel's
+  // completion is signalled to the other ranks
+  if (p.heads_per_chunk != p.H) {
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
+  }
   if (POOL && active) {
     const float nx = (float)n;
     float pq[8];
@@ -245,7 +249,7 @@ int launch_row_ssq(const __nv_bfloat16* q, const __nv_bfloat16* k, int64_t ld, i
 
 int launch_norm_rope_pool(const NormRopeParams& p, bool norm, bool rope, bool pool, cudaStream_t s) {
   if (norm && (p.ssq == nullptr || p.ssq_tile <= 0 || (p.H * 128) % p.ssq_tile != 0)) return -1;
-  const int nslots = 2 + (p.v_out != nullptr) + (p.x != nullptr && p.gate_out != nullptr);
+  const int nslots = 2 + (p.v_dst[0] != nullptr) + (p.x != nullptr && p.g_dst[0] != nullptr);
   const int smem = kNormRing * nslots * kNormRow + (norm ? 2 * p.blk * (int)sizeof(float) : 0);
   if (smem > 227 * 1024) return -1;
   dim3 grid(p.NB, (p.H + kNormHeads - 1) / kNormHeads, p.B);

@@ -7,4 +7,5 @@
 #include "gemm.cu"
 #include "attn.cu"
 #include "capi.cu"
+#include "peer.cu"
 #include "noalloc.cu"

@@ -94,14 +94,17 @@ def qkv_gemm(x2d: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = Non
 def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, ksum, lr_cos, lr_sin, rope_dim,
                          proj_q, proj_k, num_heads: int, blk: int, topk: int, splits: int | None = None,
                          keep: bool = False, lut=None, events: dict | None = None, x=None, gate_w=None,
-                         gate_b=None):
+                         gate_b=None, scatter: dict | None = None):
     """Selection, low-rank branch and fused attention for ``num_heads`` heads
     over the full sequence.  q_rope/k_rope/q_normed/k_normed/v are token-major
     ``[B, L, H*D]`` (unit column stride; q/k tensors contiguous), pooled_q
     ``[B, H, NB, D]`` and ksum ``[B, NB, H*D]`` come from the prologue pass.  The
     gate is either given (``gate [B, L, H]``) or computed inside the attention
     epilogue from the hidden states ``x [B, L, H*D]`` with ``gate_w``/``gate_b``.
-    Returns the gated output ``[B, L, H*D]``."""
+    Returns the gated output ``[B, L, H*D]``, or None with ``scatter``
+    (``dst``: per-rank output pointers, ``world``, ``head_offset``, ``H_total``),
+    which stores each output row straight into the rank owning its token
+    (``rola_b200_sparse_attn_scatter``)."""
     B, L, dim = q_rope.shape
     H = num_heads
     dev = q_rope.device
@@ -116,7 +119,7 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
     c_part = e(splits, B * H, R, HEAD_DIM, dt=torch.float32)
     C = e(B * H, R, HEAD_DIM) if keep else None
     Ct = e(B * H, HEAD_DIM, R)
-    out = e(B, L, dim)
+    out = e(B, L, dim) if scatter is None else None
     o_sparse = e(B, L, dim) if keep else None
     scores = None
     _lib.call("rola_b200_center_from_sums", _ptr(ksum), B, NB, dim, L, _ptr(center), st)
@@ -150,9 +153,15 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
         gate = None
     else:
         xs, gw, gb = (0, 0, 0), None, None
-    _lib.call("rola_b200_sparse_attn", _ptr(q_rope), _ptr(k_rope), L * dim, HEAD_DIM, dim, _ptr(v), vs[0],
-              HEAD_DIM, vs[1], _ptr(lut), B, L, H, blk, topk, _ptr(q_lr), _ptr(Ct), _ptr(gate), _ptr(x), xs[0],
-              HEAD_DIM, xs[1], _ptr(gw), _ptr(gb), eps_lr, _ptr(out), _ptr(o_sparse), L * dim, HEAD_DIM, dim, st)
+    if scatter is not None:
+        _lib.call("rola_b200_sparse_attn_scatter", _ptr(q_rope), _ptr(k_rope), L * dim, HEAD_DIM, dim, _ptr(v),
+                  vs[0], HEAD_DIM, vs[1], _ptr(lut), B, L, H, blk, topk, _ptr(q_lr), _ptr(Ct), _ptr(gate), eps_lr,
+                  scatter["dst"], scatter["world"], scatter["head_offset"], scatter["H_total"], st)
+    else:
+        _lib.call("rola_b200_sparse_attn", _ptr(q_rope), _ptr(k_rope), L * dim, HEAD_DIM, dim, _ptr(v), vs[0],
+                  HEAD_DIM, vs[1], _ptr(lut), B, L, H, blk, topk, _ptr(q_lr), _ptr(Ct), _ptr(gate), _ptr(x),
+                  xs[0], HEAD_DIM, xs[1], _ptr(gw), _ptr(gb), eps_lr, _ptr(out), _ptr(o_sparse), L * dim, HEAD_DIM,
+                  dim, st)
     if events is not None:
         events["attn"][1].record()
     if not keep:

@@ -1,0 +1,156 @@
+"""Peer-mapped device buffers for the fused sequence<->head exchanges.
+
+Every rank of a process group allocates one buffer with ``cudaMalloc``
+(``rola_b200_peer_alloc``), the ranks all-gather the CUDA IPC handles and map
+each other's buffers (``rola_b200_peer_open``).  Kernels then store rows
+straight into the buffer of the rank that consumes them: plain peer stores over
+NVLink / NVSwitch, no multicast object and no staging copy.
+
+A buffer is carved into named regions (``PeerBuffer.region``), each a dense
+tensor view of this rank's copy plus the table of all ranks' addresses of the
+same region, as the ``void* const*`` arrays the scatter entry points take.
+
+Ordering: the writer kernels end with a system-scope fence; ``stream_barrier``
+(a one-element NCCL all-reduce on the current stream) after them makes every
+rank's rows visible before the next kernel on any rank reads them.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+_ALIGN = 256
+
+
+class _DeviceArray:
+    """Zero-copy ``__cuda_array_interface__`` view of device memory."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], typestr: str, owner):
+        self._owner = owner  # keeps the buffer alive while a view exists
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None, "stream": None}
+
+
+_TYPESTR = {torch.bfloat16: ("<i2", torch.int16), torch.float32: ("<f4", torch.float32),
+            torch.int32: ("<i4", torch.int32), torch.uint8: ("|u1", torch.uint8)}
+
+
+@dataclass
+class Region:
+    offset: int
+    shape: tuple[int, ...]
+    dtype: torch.dtype
+    tensor: torch.Tensor          # this rank's copy
+    table: ctypes.Array           # (void* * world): every rank's copy
+
+
+class PeerBuffer:
+    """``layout`` = {name: (shape, dtype)}: one buffer per rank holding every
+    region, mapped by all ranks of ``group``."""
+
+    def __init__(self, layout: dict, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        offsets, off = {}, 0
+        for name, (shape, dtype) in layout.items():
+            offsets[name] = off
+            nbytes = int(torch.Size(shape).numel()) * torch.empty((), dtype=dtype).element_size()
+            off = (off + nbytes + _ALIGN - 1) // _ALIGN * _ALIGN
+        self.nbytes = max(off, _ALIGN)
+        lib = _lib.lib()
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * _lib.PEER_HANDLE_BYTES)()
+        _lib.check(lib.rola_b200_peer_alloc(self.nbytes, ctypes.byref(ptr), handle), "rola_b200_peer_alloc")
+        self.local = ptr.value
+        self._opened: list[int] = []
+        self.ptrs: list[int] = []
+        try:
+            mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+            every = torch.empty(self.world * _lib.PEER_HANDLE_BYTES, dtype=torch.uint8, device=self.device)
+            dist.all_gather_into_tensor(every, mine, group=group)
+            handles = every.view(self.world, _lib.PEER_HANDLE_BYTES).cpu()
+            for r in range(self.world):
+                if r == self.rank:
+                    self.ptrs.append(self.local)
+                    continue
+                h = (ctypes.c_ubyte * _lib.PEER_HANDLE_BYTES)(*handles[r].tolist())
+                p = ctypes.c_void_p()
+                _lib.check(lib.rola_b200_peer_open(h, ctypes.byref(p)), "rola_b200_peer_open")
+                self._opened.append(p.value)
+                self.ptrs.append(p.value)
+        except Exception:
+            self._release_local()
+            raise
+        self.regions: dict[str, Region] = {}
+        for name, (shape, dtype) in layout.items():
+            o = offsets[name]
+            typestr, view_dtype = _TYPESTR[dtype]
+            arr = _DeviceArray(self.local + o, shape, typestr, self)
+            t = torch.as_tensor(arr, device=self.device)
+            if view_dtype != dtype:
+                t = t.view(dtype)
+            table = (ctypes.c_void_p * self.world)(*[p + o for p in self.ptrs])
+            self.regions[name] = Region(o, tuple(shape), dtype, t, table)
+
+    def region(self, name: str) -> Region:
+        return self.regions[name]
+
+    def _release_local(self) -> None:
+        lib = _lib.lib()
+        for p in self._opened:
+            lib.rola_b200_peer_close(ctypes.c_void_p(p))
+        self._opened = []
+        if self.local:
+            lib.rola_b200_peer_free(ctypes.c_void_p(self.local))
+            self.local = 0
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers, then free this rank's once no
+        rank can still write into it."""
+        if not self.local:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        lib = _lib.lib()
+        for p in self._opened:
+            lib.rola_b200_peer_close(ctypes.c_void_p(p))
+        self._opened = []
+        dist.barrier(group=self.group)
+        lib.rola_b200_peer_free(ctypes.c_void_p(self.local))
+        self.local = 0
+        self.regions = {}
+
+
+def stream_barrier(group=None) -> None:
+    """Stream-ordered barrier of all ranks: returns at once on the host; work
+    queued after it on the current stream starts only when every rank's work
+    queued before it has finished."""
+    flag = torch.zeros(1, device="cuda", dtype=torch.int32)
+    dist.all_reduce(flag, group=group)
+
+
+_CACHE: dict = {}
+
+
+def cached_buffer(key, layout: dict, group=None) -> PeerBuffer:
+    """One PeerBuffer per (group, key), created collectively on first use."""
+    k = (id(group), key)
+    buf = _CACHE.get(k)
+    if buf is None or not buf.local:
+        buf = PeerBuffer(layout, group)
+        _CACHE[k] = buf
+    return buf
+
+
+def release_all() -> None:
+    """Collective: close every cached buffer (call before destroy_process_group)."""
+    for k in list(_CACHE):
+        _CACHE.pop(k).close()

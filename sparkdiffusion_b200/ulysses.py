@@ -19,6 +19,18 @@ This follows the reference's DistributedAttention pattern
 multi-GPU result equals the single-GPU one (the reference's own context
 parallel RoLa attends only within each rank's shard).
 
+Two transports carry steps 2 and 4:
+
+* ``"peer"`` (default): the exchanges are fused into the kernels.  The norm
+  pass stores each head group's rows straight into the owning rank's buffers
+  (``rola_b200_qk_norm_scatter``) and the attention epilogue stores each output
+  row into the buffer of the rank that owns its token
+  (``rola_b200_sparse_attn_scatter``); the buffers are CUDA-IPC peer mappings
+  (``peer.PeerBuffer``) and a stream-ordered barrier follows each scatter.  No
+  all-to-all, send buffer or output permutation is left.
+* ``"nccl"``: send buffers plus NCCL ``all_to_all_single`` (the reference's
+  pattern), kept as the comparison point.
+
 ``seq_to_head`` / ``head_to_seq`` are device-agnostic (they also run on gloo
 CPU ranks in the tests); ``ulysses_rola_attention`` runs the CUDA kernels.
 """
@@ -28,7 +40,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from . import _lib, ops
+from . import _lib, ops, peer
 from .ops import BF16, HEAD_DIM, _bf16_vec, _ptr, _stream
 
 
@@ -52,12 +64,29 @@ def head_to_seq(out_heads: torch.Tensor, p: int, group=None) -> torch.Tensor:
     return recv.permute(0, 2, 1, 3).reshape(B, Ls, p * X)
 
 
+def _peer_layout(B: int, Ls: int, H: int, p: int) -> dict:
+    L, Hl = Ls * p, H // p
+    return {"q": ((B, L, Hl * HEAD_DIM), BF16), "k": ((B, L, Hl * HEAD_DIM), BF16),
+            "v": ((B, L, Hl * HEAD_DIM), BF16), "gate": ((B, L, Hl), BF16),
+            "out0": ((B, Ls, H * HEAD_DIM), BF16), "out1": ((B, Ls, H * HEAD_DIM), BF16)}
+
+
+_out_slot: dict = {}
+
+
 def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk,
                                   proj_q, proj_k, gate_w, gate_b, num_heads: int, topk: int, group=None,
-                                  eps: float = 1e-6, splits: int | None = None, events: dict | None = None):
+                                  eps: float = 1e-6, splits: int | None = None, events: dict | None = None,
+                                  transport: str = "peer"):
     """Sequence-sharded RoLa forward: ``x_local [B, Ls, H*D]`` on this rank ->
     ``[B, Ls, H*D]`` (excluding the output projection).  ``cos_sin`` and the
-    low-rank tables cover the whole sequence (global positions)."""
+    low-rank tables cover the whole sequence (global positions).
+
+    With ``transport="peer"`` the result is a view of one of two alternating
+    peer-mapped output buffers: it stays valid until the second-next call with
+    the same shapes and group, and consumers must run on the current stream."""
+    if transport not in ("peer", "nccl"):
+        raise ValueError(f"unknown transport {transport!r}")
     p = dist.get_world_size(group)
     B, Ls, dim = x_local.shape
     H = num_heads
@@ -75,27 +104,39 @@ def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin
     qkv = ops.qkv_gemm(x_local.reshape(B * Ls, dim), w_qkv, b_qkv, ssq)
     if events is not None:
         events["gemm"][1].record()
-    q_send = torch.empty(B, p, Ls, Hl * HEAD_DIM, device=dev, dtype=BF16)
-    k_send = torch.empty_like(q_send)
-    v_send = torch.empty_like(q_send)
-    g_send = torch.empty(B, p, Ls, Hl, device=dev, dtype=BF16)
     gw = _bf16_vec(gate_w, HEAD_DIM, "gate_w")
     gb = _bf16_vec(gate_b, H, "gate_b")
+    nwq = _bf16_vec(norm_wq, dim, "norm_wq")
+    nwk = _bf16_vec(norm_wk, dim, "norm_wk")
     xc = x_local.contiguous()
-    _lib.call("rola_b200_qk_norm_pack", _ptr(qkv), _ptr(qkv[:, dim:]), _ptr(qkv[:, 2 * dim:]), 3 * dim, _ptr(ssq),
-              ssq.shape[-1], _ptr(xc),
-              _ptr(_bf16_vec(norm_wq, dim, "norm_wq")), _ptr(_bf16_vec(norm_wk, dim, "norm_wk")), _ptr(gw),
-              _ptr(gb), B, Ls, H, Hl, eps, _ptr(q_send), _ptr(k_send), _ptr(v_send), _ptr(g_send), st)
-    q_n, w1 = seq_to_head(q_send, group, async_op=True)
-    k_n, w2 = seq_to_head(k_send, group, async_op=True)
-    v, w3 = seq_to_head(v_send, group, async_op=True)
-    gate, w4 = seq_to_head(g_send, group, async_op=True)
-    for w in (*w1, *w2, *w3, *w4):
-        w.wait()
-    q_n = q_n.view(B, L, Hl * HEAD_DIM)
-    k_n = k_n.view(B, L, Hl * HEAD_DIM)
-    v = v.view(B, L, Hl * HEAD_DIM)
-    gate = gate.view(B, L, Hl)
+    rank = dist.get_rank(group)
+    if transport == "peer":
+        key = ("ulysses", B, Ls, H, str(dev))
+        buf = peer.cached_buffer(key, _peer_layout(B, Ls, H, p), group)
+        rq, rk, rv, rg = (buf.region(n) for n in ("q", "k", "v", "gate"))
+        _lib.call("rola_b200_qk_norm_scatter", _ptr(qkv), _ptr(qkv[:, dim:]), _ptr(qkv[:, 2 * dim:]), 3 * dim,
+                  _ptr(ssq), ssq.shape[-1], _ptr(xc), _ptr(nwq), _ptr(nwk), _ptr(gw), _ptr(gb), B, Ls, H, p, rank,
+                  eps, rq.table, rk.table, rv.table, rg.table, st)
+        peer.stream_barrier(group)
+        q_n, k_n, v, gate = rq.tensor, rk.tensor, rv.tensor, rg.tensor
+    else:
+        q_send = torch.empty(B, p, Ls, Hl * HEAD_DIM, device=dev, dtype=BF16)
+        k_send = torch.empty_like(q_send)
+        v_send = torch.empty_like(q_send)
+        g_send = torch.empty(B, p, Ls, Hl, device=dev, dtype=BF16)
+        _lib.call("rola_b200_qk_norm_pack", _ptr(qkv), _ptr(qkv[:, dim:]), _ptr(qkv[:, 2 * dim:]), 3 * dim,
+                  _ptr(ssq), ssq.shape[-1], _ptr(xc), _ptr(nwq), _ptr(nwk), _ptr(gw), _ptr(gb), B, Ls, H, Hl, eps,
+                  _ptr(q_send), _ptr(k_send), _ptr(v_send), _ptr(g_send), st)
+        q_n, w1 = seq_to_head(q_send, group, async_op=True)
+        k_n, w2 = seq_to_head(k_send, group, async_op=True)
+        v, w3 = seq_to_head(v_send, group, async_op=True)
+        gate, w4 = seq_to_head(g_send, group, async_op=True)
+        for w in (*w1, *w2, *w3, *w4):
+            w.wait()
+        q_n = q_n.view(B, L, Hl * HEAD_DIM)
+        k_n = k_n.view(B, L, Hl * HEAD_DIM)
+        v = v.view(B, L, Hl * HEAD_DIM)
+        gate = gate.view(B, L, Hl)
     blk = 128
     NB = (L + blk - 1) // blk
     q_rope = torch.empty_like(q_n)
@@ -105,6 +146,15 @@ def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin
     cs = cos_sin.to(torch.float32).contiguous()
     _lib.call("rola_b200_rope_pool", _ptr(q_n), _ptr(k_n), Hl * HEAD_DIM, _ptr(cs), B, L, Hl, blk, _ptr(q_rope),
               _ptr(k_rope), _ptr(pooled_q), _ptr(ksum), st)
+    if transport == "peer":
+        slot = _out_slot.get(key, 0)
+        _out_slot[key] = slot ^ 1
+        rout = buf.region(f"out{slot}")
+        ops.head_local_attention(q_rope, k_rope, q_n, k_n, v, gate, pooled_q, ksum, lr_cos, lr_sin, rope_dim,
+                                 proj_q, proj_k, Hl, blk, topk, splits, events=events,
+                                 scatter=dict(dst=rout.table, world=p, head_offset=rank * Hl, H_total=H))
+        peer.stream_barrier(group)
+        return rout.tensor
     out_heads = ops.head_local_attention(q_rope, k_rope, q_n, k_n, v, gate, pooled_q, ksum, lr_cos, lr_sin,
                                          rope_dim, proj_q, proj_k, Hl, blk, topk, splits, events=events)
     return head_to_seq(out_heads, p, group)

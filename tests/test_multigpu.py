@@ -1,10 +1,12 @@
-"""Ulysses sequence<->head parallel forward on 2 GPUs (NCCL) vs the 1-GPU forward.
+"""Ulysses sequence<->head parallel forward on 2, 4 and 8 GPUs vs the 1-GPU forward.
 
-Skipped unless at least two CUDA devices are visible.  Each rank holds a
-sequence shard of the hidden states; the result gathered from both ranks must
-select exactly the same key blocks as the single-GPU forward and match its
-output within the bf16 tolerance (the gate is summed in a different order on
-the two paths, so outputs may differ by bf16 rounding).
+Skipped unless enough CUDA devices are visible.  Each rank holds a sequence
+shard of the hidden states; the result gathered from all ranks must match the
+single-GPU forward within the bf16 tolerance (the gate is summed in a different
+order on the two paths, so outputs may differ by bf16 rounding).  Both
+transports run: the exchanges fused into the kernels over peer memory, and the
+NCCL all-to-all.  With 8 ranks the shards (90 tokens) do not align with the
+128-token blocks, so blocks straddle ranks in both exchanges.
 """
 
 import os
@@ -18,8 +20,6 @@ from conftest import assert_bf16_close
 
 pytestmark = pytest.mark.gpu
 
-WORLD = 2
-
 
 def _free_port():
     s = socket.socket()
@@ -32,7 +32,7 @@ def _free_port():
 def _workload():
     from sparkdiffusion_b200.workloads import C3
 
-    wl = C3.scaled(H=4, grid=(3, 10, 24), B=1)  # L = 720 (NB = 6, ragged tail)
+    wl = C3.scaled(H=8, grid=(3, 10, 24), B=1)  # L = 720 (NB = 6, ragged tail)
     return wl.__class__(**{**wl.__dict__, "topk": 3})
 
 
@@ -50,45 +50,59 @@ def _inputs(wl, dev):
     return inp, common
 
 
-def _rank_main(rank, port, out_path):
+def _rank_main(rank, world, transport, port, out_path):
     import datetime
 
     import torch.distributed as dist
 
-    from sparkdiffusion_b200 import _lib
+    from sparkdiffusion_b200 import _lib, peer
     from sparkdiffusion_b200.ulysses import ulysses_rola_attention_params
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=60),
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     wl = _workload()
     inp, common = _inputs(wl, dev)
-    Ls = wl.L // WORLD
+    Ls = wl.L // world
     x_local = inp["x"][:, rank * Ls:(rank + 1) * Ls].contiguous()
-    out = ulysses_rola_attention_params(x_local, inp["w_qkv"], None, *common, wl.H, wl.topk)
+    outs = []
+    for _ in range(3):  # both alternating output buffers, then the first again
+        out = ulysses_rola_attention_params(x_local, inp["w_qkv"], None, *common, wl.H, wl.topk,
+                                            transport=transport)
+        outs.append(out.clone())
     torch.cuda.synchronize()
     status = _lib.device_status()
-    parts = [torch.empty_like(out) for _ in range(WORLD)]
-    dist.all_gather(parts, out)
+    parts = [torch.empty_like(outs[0]) for _ in range(world)]
+    dist.all_gather(parts, outs[0])
+    repeat_equal = all(torch.equal(o, outs[0]) for o in outs[1:])
     if rank == 0:
-        torch.save({"out": torch.cat(parts, dim=1).cpu(), "status": status}, out_path)
+        torch.save({"out": torch.cat(parts, dim=1).cpu(), "status": status, "repeat_equal": repeat_equal},
+                   out_path)
+    peer.release_all()
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-def test_ulysses_two_gpus_match_single_gpu(tmp_path):
+CASES = [(2, "peer"), (2, "nccl"), (4, "peer"), (8, "peer")]
+
+
+@pytest.mark.parametrize("world,transport", CASES, ids=[f"{w}gpu-{t}" for w, t in CASES])
+def test_ulysses_matches_single_gpu(tmp_path, world, transport):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     from sparkdiffusion_b200 import ops
 
     out_path = str(tmp_path / "ulysses.pt")
-    mp.start_processes(_rank_main, args=(_free_port(), out_path), nprocs=WORLD, start_method="spawn")
+    mp.start_processes(_rank_main, args=(world, transport, _free_port(), out_path), nprocs=world,
+                       start_method="spawn")
     got = torch.load(out_path)
     assert got["status"] == 0
+    assert got["repeat_equal"]
     wl = _workload()
     inp, common = _inputs(wl, "cuda:0")
     ref = ops.rola_attention_core(inp["x"], inp["w_qkv"], None, *common, wl.H, 128, wl.topk)
     torch.cuda.synchronize()
-    assert_bf16_close(got["out"], ref.cpu(), "ulysses vs single GPU")
+    assert_bf16_close(got["out"], ref.cpu(), f"ulysses {world} GPUs ({transport}) vs single GPU")
