@@ -55,6 +55,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="N>1: sequence<->head exchanges fused into the kernels over peer memory, or NCCL all-to-all")
+    ap.add_argument("--chunks", type=int, default=None,
+                    help="N>1, peer transport: equal token chunks of the QKV GEMM / scattering norm pass overlap "
+                         "(default: the automatic halving plan; 1: no overlap)")
     return ap.parse_args()
 
 
@@ -278,7 +281,7 @@ def main():
 
         def step(xin, events=None):
             return ulysses_rola_attention_params(xin, w_qkv, None, *common, H, wl.topk, group, events=events,
-                                                 transport=args.transport)
+                                                 transport=args.transport, chunks=args.chunks)
 
     # exact selected-block FLOPs from this layer's LUT.  Every rank runs the
     # 1-GPU pipeline once on the full hidden states (selection is bit-exact and
@@ -394,7 +397,8 @@ def main():
         "data": "synthetic (seeded N(0,1) hidden states, N(0,0.02) QKV weights, random low-rank/gate factors)",
         "config": {"workload": workload_desc(wl), "global_batch": B, "seq_len": L,
                    "parallelism": f"ulysses{world}" if world > 1 else "single",
-                   "exchange": (f"fused into the norm pass and attention epilogue (peer stores)"
+                   "exchange": (f"fused into the norm pass and attention epilogue (peer stores), "
+                                f"GEMM/scatter overlap in {args.chunks or 'auto'} chunks"
                                 if args.transport == "peer" else "NCCL all_to_all_single") if world > 1 else None,
                    "l2": "inputs larger than L2 (hidden states 774 MB, QKV 2.3 GB per layer); no flush"},
         "flops_per_layer": flops_total,

@@ -90,21 +90,55 @@ int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_r
                            const void* gate_b, int B, int L, int H, int heads_per_chunk, float eps, void* q_send,
                            void* k_send, void* v_send, void* gate_out, rola_stream_t stream);
 
-/* qk_norm_pack with the sequence->head exchange fused into its stores: this
- * rank (of world ranks on one node) holds tokens [rank*Ls, (rank+1)*Ls); the
- * q_normed, k_normed and v rows of heads [r*Hl, (r+1)*Hl) (Hl = H / world) go
- * straight into rank r's buffers q_dst[r], k_dst[r], v_dst[r], each
- * [B, world*Ls, Hl*D] token-major, at row rank*Ls + t, and the gate into
- * g_dst[r] [B, world*Ls, Hl].  The destinations are peer mappings
- * (rola_b200_peer_open); the kernel ends with a system-scope fence, so a
- * stream-ordered barrier of all ranks after it makes the rows visible.
- * world <= 8.  No counterpart in the reference, whose context parallelism
- * (sparkdiffusion/utils/a2a_cp.py:146-186) exchanges with NCCL all-to-all. */
-int rola_b200_qk_norm_scatter(const void* q_raw, const void* k_raw, const void* v_raw, int64_t ld_raw,
-                              const float* ssq, int ssq_ld, const void* x, const void* norm_wq, const void* norm_wk,
-                              const void* gate_w, const void* gate_b, int B, int Ls, int H, int world, int rank,
-                              float eps, void* const* q_dst, void* const* k_dst, void* const* v_dst,
-                              void* const* g_dst, rola_stream_t stream);
+/* One sequence->head scatter: qk_norm_pack with the exchange fused into its
+ * stores.  The rows of heads [r*Hl, (r+1)*Hl) (Hl = H / world) of L tokens
+ * per batch (B batches, rows token-major with stride ld_raw; ssq the QKV GEMM
+ * sums, row stride ssq_ld) go straight into rank r's buffers q_dst[r],
+ * k_dst[r], v_dst[r], each [B, dst_rows, Hl*D], at rows [dst_row0,
+ * dst_row0 + L), and the gate into g_dst[r] [B, dst_rows, Hl].  A whole
+ * sequence shard of rank rk is L = Ls, dst_rows = world*Ls, dst_row0 = rk*Ls;
+ * a chunk of it (B = 1) shifts dst_row0.  The destinations are peer mappings
+ * (rola_b200_peer_open); the kernels end with a system-scope fence, so a
+ * stream-ordered barrier of all ranks after them makes the rows visible.
+ * world <= ROLA_MAX_RANKS.  No counterpart in the reference, whose context
+ * parallelism (sparkdiffusion/utils/a2a_cp.py:146-186) exchanges with NCCL
+ * all-to-all. */
+#define ROLA_MAX_RANKS 8
+typedef struct rola_scatter_args {
+  const void* q_raw;
+  const void* k_raw;
+  const void* v_raw;
+  int64_t ld_raw;
+  const float* ssq;
+  int32_t ssq_ld;
+  int32_t B;
+  int32_t L;
+  int32_t H;
+  int32_t world;
+  float eps;
+  int64_t dst_rows;
+  int64_t dst_row0;
+  const void* x;
+  const void* norm_wq;
+  const void* norm_wk;
+  const void* gate_w;
+  const void* gate_b;
+  void* q_dst[ROLA_MAX_RANKS];
+  void* k_dst[ROLA_MAX_RANKS];
+  void* v_dst[ROLA_MAX_RANKS];
+  void* g_dst[ROLA_MAX_RANKS];
+} rola_scatter_args;
+
+/* The scatter as its own pass.  compact != 0 selects the small-footprint
+ * kernel (3-token ring); 0 the 8-token ring. */
+int rola_b200_qk_norm_scatter(const rola_scatter_args* args, int compact, rola_stream_t stream);
+
+/* rola_b200_qkv_gemm on rows of this chunk while four spare warps of every
+ * GEMM CTA run the scatter `side` of an earlier chunk (B == 1, ssq given):
+ * the NVLink traffic of the exchange hides under the tensor-core work of the
+ * next projection.  No counterpart in the reference. */
+int rola_b200_qkv_gemm_scatter(const void* x, const void* w, const void* bias, void* out, float* ssq, int64_t M,
+                               int64_t N, int64_t K, const rola_scatter_args* side, rola_stream_t stream);
 
 /* Head-parallel half (after the all-to-all): RoPE, q-pool and k block sums from
  * the normed q/k (token-major, row stride ld).  Same reference interface as

@@ -45,8 +45,8 @@ SIGNATURES = {
                                _P, _P, _P, _P, _P, _P, _P, _P],
     "rola_b200_qk_norm_pack": [_P, _P, _P, _L, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F,
                                _P, _P, _P, _P, _P],
-    "rola_b200_qk_norm_scatter": [_P, _P, _P, _L, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F,
-                                  _P, _P, _P, _P, _P],
+    "rola_b200_qk_norm_scatter": [_P, _I, _P],
+    "rola_b200_qkv_gemm_scatter": [_P, _P, _P, _P, _P, _L, _L, _L, _P, _P],
     "rola_b200_rope_pool": [_P, _P, _L, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P],
     "rola_b200_mean_pool": [_P, _L, _L, _L, _I, _I, _I, _I, _P, _P, _P],
     "rola_b200_smooth_k_center": [_P, _L, _L, _L, _I, _I, _I, _I, _P, _P, _P],
@@ -73,6 +73,19 @@ _RESTYPES = {
     "rola_b200_last_error": ctypes.c_char_p,
     "rola_b200_forward_workspace_bytes": _Z,
 }
+
+MAX_RANKS = 8
+
+
+class ScatterArgs(ctypes.Structure):
+    """``rola_scatter_args`` of include/rola_b200.h."""
+
+    _fields_ = [("q_raw", _P), ("k_raw", _P), ("v_raw", _P), ("ld_raw", _L), ("ssq", _P), ("ssq_ld", ctypes.c_int32),
+                ("B", ctypes.c_int32), ("L", ctypes.c_int32), ("H", ctypes.c_int32), ("world", ctypes.c_int32),
+                ("eps", _F), ("dst_rows", _L), ("dst_row0", _L), ("x", _P), ("norm_wq", _P), ("norm_wk", _P),
+                ("gate_w", _P), ("gate_b", _P), ("q_dst", _P * MAX_RANKS), ("k_dst", _P * MAX_RANKS),
+                ("v_dst", _P * MAX_RANKS), ("g_dst", _P * MAX_RANKS)]
+
 
 _lock = threading.Lock()
 _lib = None

@@ -121,8 +121,8 @@ int rola_b200_device_status(int clear) {
   return v;
 }
 
-int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out, float* ssq, int64_t M, int64_t N,
-                       int64_t K, rola_stream_t stream) {
+static int qkv_gemm_impl(const void* x, const void* w, const void* bias, void* out, float* ssq, int64_t M, int64_t N,
+                         int64_t K, const NormRopeParams* side, rola_stream_t stream) {
   ROLA_CHECK(x && w && out, "qkv_gemm: null pointer");
   ROLA_CHECK(M > 0 && M < (1ll << 31), "qkv_gemm: M out of range");
   ROLA_CHECK(N > 0 && N % 256 == 0 && N <= 65536, "qkv_gemm: N must be a positive multiple of 256");
@@ -141,8 +141,13 @@ int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out
     const uint32_t box[2] = {64, 256};
     ROLA_TRY(make_map(&tb, w, 2, dims, strides, box, "qkv_gemm: w"));
   }
-  return cuda_status(launch_gemm_bf16(ta, tb, BF(bias), BFm(out), N, ssq, (int)M, (int)N, (int)K, S(stream)),
+  return cuda_status(launch_gemm_bf16(ta, tb, BF(bias), BFm(out), N, ssq, (int)M, (int)N, (int)K, side, S(stream)),
                      "qkv_gemm");
+}
+
+int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out, float* ssq, int64_t M, int64_t N,
+                       int64_t K, rola_stream_t stream) {
+  return qkv_gemm_impl(x, w, bias, out, ssq, M, N, K, nullptr, stream);
 }
 
 // Runs the streaming norm pass.  ssq: the QKV GEMM's per-256-column sums of
@@ -250,58 +255,80 @@ int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_r
   p.B = B;
   p.L = L;
   p.H = H;
-  p.blk = 128;
-  p.NB = (L + 127) / 128;
+  p.blk = 32;  // no pooling: short work items
+  p.NB = (L + 31) / 32;
   p.heads_per_chunk = heads_per_chunk;
   p.eps = eps;
   return run_norm_pass(p, true, false, false, ssq, ssq_ld, S(stream), "qk_norm_pack");
 }
 
-int rola_b200_qk_norm_scatter(const void* q_raw, const void* k_raw, const void* v_raw, int64_t ld_raw,
-                              const float* ssq, int ssq_ld, const void* x, const void* norm_wq, const void* norm_wk,
-                              const void* gate_w, const void* gate_b, int B, int Ls, int H, int world, int rank,
-                              float eps, void* const* q_dst, void* const* k_dst, void* const* v_dst,
-                              void* const* g_dst, rola_stream_t stream) {
-  ROLA_CHECK(q_raw && k_raw && v_raw && norm_wq && norm_wk && x && gate_w && gate_b && q_dst && k_dst && v_dst && g_dst,
-             "qk_norm_scatter: null pointer");
-  ROLA_CHECK(world >= 1 && world <= kMaxChunks && rank >= 0 && rank < world, "qk_norm_scatter: bad rank/world (<= 8)");
-  ROLA_CHECK(B > 0 && Ls > 0 && H > 0 && H % world == 0, "qk_norm_scatter: world must divide the head count");
-  ROLA_CHECK(ld_raw % 8 == 0 && aligned16(q_raw) && aligned16(k_raw) && aligned16(v_raw) && aligned16(x),
-             "qk_norm_scatter: 16-byte aligned rows required");
-  ROLA_CHECK(ssq == nullptr || (H % 2 == 0 && ssq_ld >= H), "qk_norm_scatter: sums of squares need an even head count");
-  for (int r = 0; r < world; ++r)
-    ROLA_CHECK(q_dst[r] && k_dst[r] && v_dst[r] && g_dst[r] && aligned16(q_dst[r]) && aligned16(k_dst[r]) &&
-                   aligned16(v_dst[r]),
-               "qk_norm_scatter: destination %d null or not 16-byte aligned", r);
+// Validates a scatter description and turns it into norm-pass parameters.
+static int scatter_params(const rola_scatter_args* a, bool compact, NormRopeParams* out, const char* what) {
+  ROLA_CHECK(a, "%s: null arguments", what);
+  ROLA_CHECK(a->q_raw && a->k_raw && a->v_raw && a->norm_wq && a->norm_wk && a->x && a->gate_w && a->gate_b,
+             "%s: null pointer", what);
+  ROLA_CHECK(a->world >= 1 && a->world <= kMaxChunks, "%s: bad world size (<= 8)", what);
+  ROLA_CHECK(a->B > 0 && a->L > 0 && a->H > 0 && a->H % a->world == 0, "%s: world must divide the head count", what);
+  ROLA_CHECK(a->dst_row0 >= 0 && a->dst_row0 + a->L <= a->dst_rows && a->dst_rows < (1ll << 31),
+             "%s: rows [dst_row0, dst_row0 + L) outside the destination", what);
+  ROLA_CHECK(a->ld_raw % 8 == 0 && aligned16(a->q_raw) && aligned16(a->k_raw) && aligned16(a->v_raw) &&
+                 aligned16(a->x),
+             "%s: 16-byte aligned rows required", what);
+  ROLA_CHECK(a->ssq == nullptr || (a->H % 2 == 0 && a->ssq_ld >= a->H),
+             "%s: sums of squares need an even head count", what);
+  for (int r = 0; r < a->world; ++r)
+    ROLA_CHECK(a->q_dst[r] && a->k_dst[r] && a->v_dst[r] && a->g_dst[r] && aligned16(a->q_dst[r]) &&
+                   aligned16(a->k_dst[r]) && aligned16(a->v_dst[r]),
+               "%s: destination %d null or not 16-byte aligned", what, r);
   NormRopeParams p{};
-  p.q_in = BF(q_raw);
-  p.k_in = BF(k_raw);
-  p.v_in = BF(v_raw);
-  p.ld_in = ld_raw;
-  p.x = BF(x);
-  p.ld_x = (int64_t)H * 128;
-  p.norm_wq = BF(norm_wq);
-  p.norm_wk = BF(norm_wk);
-  p.gate_w = BF(gate_w);
-  p.gate_b = BF(gate_b);
-  // destination r holds heads [r*Hl, (r+1)*Hl) of all world*Ls tokens; this
-  // rank's tokens start at row rank*Ls there
-  for (int r = 0; r < world; ++r) {
-    p.qn_dst[r] = BFm(q_dst[r]);
-    p.kn_dst[r] = BFm(k_dst[r]);
-    p.v_dst[r] = BFm(v_dst[r]);
-    p.g_dst[r] = BFm(g_dst[r]);
+  p.q_in = BF(a->q_raw);
+  p.k_in = BF(a->k_raw);
+  p.v_in = BF(a->v_raw);
+  p.ld_in = a->ld_raw;
+  p.x = BF(a->x);
+  p.ld_x = (int64_t)a->H * 128;
+  p.norm_wq = BF(a->norm_wq);
+  p.norm_wk = BF(a->norm_wk);
+  p.gate_w = BF(a->gate_w);
+  p.gate_b = BF(a->gate_b);
+  // destination r holds heads [r*Hl, (r+1)*Hl) of dst_rows tokens per batch;
+  // this call's tokens start at row dst_row0 there
+  for (int r = 0; r < a->world; ++r) {
+    p.qn_dst[r] = BFm(a->q_dst[r]);
+    p.kn_dst[r] = BFm(a->k_dst[r]);
+    p.v_dst[r] = BFm(a->v_dst[r]);
+    p.g_dst[r] = BFm(a->g_dst[r]);
   }
-  p.dst_sB = (int64_t)Ls * H * 128;
-  p.dst_t0 = rank * Ls;
-  p.B = B;
-  p.L = Ls;
-  p.H = H;
-  p.blk = 128;
-  p.NB = (Ls + 127) / 128;
-  p.heads_per_chunk = H / world;
-  p.eps = eps;
-  return run_norm_pass(p, true, false, false, ssq, ssq_ld, S(stream), "qk_norm_scatter");
+  p.dst_sB = a->dst_rows * (a->H / a->world) * 128;
+  p.dst_t0 = (int)a->dst_row0;
+  p.B = a->B;
+  p.L = a->L;
+  p.H = a->H;
+  // no pooling here: short 32-token work items give the pass enough CTAs on small chunks
+  p.blk = 32;
+  p.NB = (a->L + 31) / 32;
+  p.heads_per_chunk = a->H / a->world;
+  p.compact = compact;
+  p.eps = a->eps;
+  p.ssq = a->ssq;
+  p.ssq_ld = a->ssq_ld;
+  p.ssq_tile = 256;
+  *out = p;
+  return ROLA_OK;
+}
+
+int rola_b200_qk_norm_scatter(const rola_scatter_args* args, int compact, rola_stream_t stream) {
+  NormRopeParams p{};
+  ROLA_TRY(scatter_params(args, compact != 0, &p, "qk_norm_scatter"));
+  return run_norm_pass(p, true, false, false, args->ssq, args->ssq_ld, S(stream), "qk_norm_scatter");
+}
+
+int rola_b200_qkv_gemm_scatter(const void* x, const void* w, const void* bias, void* out, float* ssq, int64_t M,
+                               int64_t N, int64_t K, const rola_scatter_args* side, rola_stream_t stream) {
+  NormRopeParams p{};
+  ROLA_TRY(scatter_params(side, true, &p, "qkv_gemm_scatter"));
+  ROLA_CHECK(side->B == 1 && side->ssq != nullptr, "qkv_gemm_scatter: the side job needs B == 1 and the GEMM sums");
+  return qkv_gemm_impl(x, w, bias, out, ssq, M, N, K, &p, stream);
 }
 
 int rola_b200_rope_pool(const void* q_normed, const void* k_normed, int64_t ld, const float* cos_sin, int B, int L,

@@ -5,13 +5,22 @@
 // reference prologue (sparkdiffusion/ops/fused_kernel/fused_qkv_rope.py:287-289)
 // with one GEMM over the concatenated [3*dim, dim] weight.
 //
-// CTA tile 128 x 256, K step 64 (one 128-byte swizzle atom), 4-stage TMA ring.
+// Persistent kernel: one CTA per SM walks the 128 x 256 output tiles
+// (tile = blockIdx.x + i * gridDim.x, rasterised in groups of 16 M-tiles so
+// the tiles in flight at one time share A and W through L2).  K step 64 (one
+// 128-byte swizzle atom), 4-stage TMA ring that runs across tile boundaries.
 // Warp roles: warp 0 issues TMA loads, warp 1 owns TMEM and issues the MMAs
-// from one elected thread (tcgen05.mma M=128 N=256 K=16), warps 2..5 drain the
-// accumulator from TMEM (each warp reads the 32 TMEM lanes its warp id allows)
-// and write bf16 rows (optionally also each row's sum of squares of its bf16
-// outputs per 256-column tile, which the qk-RMSNorm pass consumes).  Tiles are rasterised in groups of 16 M-tiles so the
-// CTAs resident at one time share A and W tiles through L2.
+// from one elected thread (tcgen05.mma M=128 N=256 K=16) into one of two
+// 256-column accumulators, warps 2..5 drain the other accumulator (each warp
+// reads the 32 TMEM lanes its warp id allows) and write bf16 rows, optionally
+// with each row's sum of squares of its bf16 outputs per 256-column tile (the
+// qk-RMSNorm statistics).  The epilogue of tile i thus overlaps the MMAs of
+// tile i+1.
+//
+// Optional side job (warps 6..9): work items of the streaming norm pass of an
+// EARLIER chunk of rows (norm_block), e.g. the Ulysses scatter of chunk c-1
+// while the tensor cores project chunk c; the side job shares nothing with the
+// GEMM but the SM.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -22,46 +31,59 @@ constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_BYTES = BN * BK * 2;  // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*alignment*/;
+constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+constexpr int OFF_NORM = OFF_BAR + 1024;  // side-job shared memory
+constexpr int SMEM_BYTES = OFF_NORM + 1024 /*alignment*/;
 constexpr int THREADS = 192;
+constexpr int THREADS_SIDE = THREADS + kNormThreads;
 constexpr int GROUP_M = 16;
+constexpr int ACC_COLS = 2 * BN;  // two accumulators
 }  // namespace gemm
 
-__global__ void __launch_bounds__(gemm::THREADS, 1)
+__global__ void __launch_bounds__(gemm::THREADS_SIDE, 1)
     gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
                       const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out, int64_t ldo,
-                      float* __restrict__ ssq, int M, int N, int K) {
+                      float* __restrict__ ssq, int M, int N, int K, const __grid_constant__ NormRopeParams side,
+                      int side_items) {
   using namespace gemm;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
-  const uint32_t bar0 = base + STAGES * STAGE_BYTES;
-  // barriers: full[S], empty[S], acc_full, drain
+  const uint32_t bar0 = base + OFF_BAR;
+  // barriers: full[S], empty[S], acc_full[2], acc_empty[2], drain
   auto full = [&](int s) { return bar0 + 8u * s; };
   auto empty = [&](int s) { return bar0 + 8u * (STAGES + s); };
-  const uint32_t acc_full = bar0 + 8u * (2 * STAGES);
-  const uint32_t drain = acc_full + 8u;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + STAGES * STAGE_BYTES + 256);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + STAGES * STAGE_BYTES + 264);
+  auto acc_full = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+  auto acc_empty = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+  const uint32_t drain = bar0 + 8u * (2 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_BAR + 256);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 264);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (M + BM - 1) / BM, num_n = N / BN;
-  // grouped rasterisation
-  const int bid = blockIdx.x;
-  const int per_group = GROUP_M * num_n;
-  const int g = bid / per_group, r = bid % per_group;
-  const int gm = min(GROUP_M, num_m - g * GROUP_M);
-  const int m_tile = g * GROUP_M + r % gm, n_tile = r / gm;
-  const int m0 = m_tile * BM, n0 = n_tile * BN;
+  const int num_tiles = num_m * num_n;
   const int nk = K / BK;
+  // my tiles: blockIdx.x, blockIdx.x + gridDim.x, ...
+  const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  auto tile_coords = [&](int lt, int& m0, int& n_tile) {
+    const int tile = blockIdx.x + lt * gridDim.x;
+    const int per_group = GROUP_M * num_n;
+    const int g = tile / per_group, r = tile % per_group;
+    const int gm = min(GROUP_M, num_m - g * GROUP_M);
+    m0 = (g * GROUP_M + r % gm) * BM;
+    n_tile = r / gm;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full(s), 1);
       mbar_init(empty(s), 1);
     }
-    mbar_init(acc_full, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(acc_full(a), 1);
+      mbar_init(acc_empty(a), 4);  // one arrival per epilogue warp
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -69,7 +91,7 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
     prefetch_tmap(&tb);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), BN);
+    tmem_alloc(smem_u32(tmem_slot), ACC_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -79,58 +101,81 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
 
   if (warp == 0) {
     if (elect_one()) {
-      int issued = 0;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        if (!mbar_wait(empty(s), ((kb / STAGES) & 1) ^ 1, abort_flag, kDevTimeoutMma)) break;
-        const uint32_t sa = base + s * STAGE_BYTES;
-        mbar_expect_tx(full(s), STAGE_BYTES);
-        tma_load_2d(sa, &ta, full(s), kb * BK, m0);
-        tma_load_2d(sa + A_BYTES, &tb, full(s), kb * BK, n0);
-        ++issued;
+      int it = 0;
+      bool ok = true;
+      for (int lt = 0; lt < my_tiles && ok; ++lt) {
+        int m0, n_tile;
+        tile_coords(lt, m0, n_tile);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(empty(s), ((it / STAGES) & 1) ^ 1, abort_flag, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + s * STAGE_BYTES;
+          mbar_expect_tx(full(s), STAGE_BYTES);
+          tma_load_2d(sa, &ta, full(s), kb * BK, m0);
+          tma_load_2d(sa + A_BYTES, &tb, full(s), kb * BK, n_tile * BN);
+        }
       }
       // make sure no load is still writing shared memory when the CTA exits
-      for (int kb = max(0, issued - STAGES); kb < issued; ++kb)
-        mbar_wait(full(kb % STAGES), (kb / STAGES) & 1, abort_flag, kDevTimeoutLoad);
+      for (int k = max(0, it - STAGES); k < it; ++k)
+        mbar_wait(full(k % STAGES), (k / STAGES) & 1, abort_flag, kDevTimeoutLoad);
     }
   } else if (warp == 1) {
     if (elect_one()) {
       const uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
       bool ok = true;
-      for (int kb = 0; kb < nk && ok; ++kb) {
-        const int s = kb % STAGES;
-        if (!mbar_wait(full(s), (kb / STAGES) & 1, abort_flag, kDevTimeoutLoad)) { ok = false; break; }
+      int it = 0;
+      for (int lt = 0; lt < my_tiles && ok; ++lt) {
+        const int a = lt & 1;
+        // the epilogue has drained this accumulator (tile lt - 2)
+        if (!mbar_wait(acc_empty(a), ((lt >> 1) & 1) ^ 1, abort_flag, kDevTimeoutSoftmax)) break;
         tc_fence_after();
-        const uint32_t sa = base + s * STAGE_BYTES;
-        const uint32_t sb = sa + A_BYTES;
+        const uint32_t acc = tmem + a * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(full(s), (it / STAGES) & 1, abort_flag, kDevTimeoutLoad)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + s * STAGE_BYTES;
+          const uint32_t sb = sa + A_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t da = sdesc_sw128(sa + kk * 32, 16, 1024);
-          const uint64_t db = sdesc_sw128(sb + kk * 32, 16, 1024);
-          mma_bf16_ss(tmem, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t da = sdesc_sw128(sa + kk * 32, 16, 1024);
+            const uint64_t db = sdesc_sw128(sb + kk * 32, 16, 1024);
+            mma_bf16_ss(acc, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(empty(s));
         }
-        mma_commit(empty(s));
+        if (ok) mma_commit(acc_full(a));
       }
-      if (ok) mma_commit(acc_full);
       mma_commit(drain);
       mbar_wait(drain, 0, abort_flag, kDevTimeoutMma);
     }
-  } else {
+  } else if (warp < 6) {
     // epilogue warps 2..5: TMEM lane quadrant = warp % 4
     const int q = warp & 3;
     const int row = q * 32 + lane;
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort_flag, kDevTimeoutMma));
-    tc_fence_after();
-    if (ok) {
+    for (int lt = 0; lt < my_tiles; ++lt) {
+      const int a = lt & 1;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full(a), (lt >> 1) & 1, abort_flag, kDevTimeoutMma));
+      if (!ok) break;
+      tc_fence_after();
+      int m0, n_tile;
+      tile_coords(lt, m0, n_tile);
       const int gm_row = m0 + row;
+      const uint32_t acc = tmem + a * BN + ((uint32_t)(q * 32) << 16);
       float ss = 0.f;  // sum of squares of this row's bf16 outputs in this tile
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, v);
+        tmem_ld32(acc + c * 32, v);
         tmem_ld_wait();
         if (gm_row < M) {
-          const int col = n0 + c * 32;
+          const int col = n_tile * BN + c * 32;
           float f[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
@@ -157,25 +202,57 @@ __global__ void __launch_bounds__(gemm::THREADS, 1)
           }
         }
       }
+      // the accumulator may be overwritten once every warp's loads completed
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty(a));
       if (ssq && gm_row < M) ssq[(int64_t)gm_row * (N / BN) + n_tile] = ss;
     }
+  } else {
+    // side job, warps 6..9 (only launched with side_items > 0)
+    uint8_t* nsm = gbase + OFF_NORM;
+    const int ngrp = (side.H + kNormHeads - 1) / kNormHeads;
+    for (int item = blockIdx.x; item < side_items; item += gridDim.x)
+      norm_block<true, false, false, kNormRingCompact>(side, item / ngrp, item % ngrp, 0, nsm,
+                                                        threadIdx.x - THREADS, 1);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, ACC_COLS);
   }
 }
 
+static int g_num_sms = 0;
+
 int launch_gemm_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const __nv_bfloat16* bias, __nv_bfloat16* out,
-                     int64_t ldo, float* ssq, int M, int N, int K, cudaStream_t s) {
+                     int64_t ldo, float* ssq, int M, int N, int K, const NormRopeParams* side, cudaStream_t s) {
   using namespace gemm;
   if (N % BN != 0 || K % BK != 0 || M <= 0) return -1;
-  cudaFuncSetAttribute(gemm_bf16_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  const int num_m = (M + BM - 1) / BM, num_n = N / BN;
-  gemm_bf16_tcgen05<<<num_m * num_n, THREADS, SMEM_BYTES, s>>>(ta, tb, bias, out, ldo, ssq, M, N, K);
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) return (int)cudaGetLastError();
+  }
+  int side_items = 0, smem = SMEM_BYTES;
+  NormRopeParams sp{};
+  if (side) {
+    // norm-only pass of B = 1 rows with the compact ring, items = blocks x head groups
+    if (side->B != 1 || side->ssq == nullptr || !side->compact) return -1;
+    sp = *side;
+    side_items = sp.NB * ((sp.H + kNormHeads - 1) / kNormHeads);
+    const int nslots = 2 + (sp.v_dst[0] != nullptr) + (sp.x != nullptr && sp.g_dst[0] != nullptr);
+    smem += norm_smem_bytes(kNormRingCompact, nslots, sp.blk, true);
+    if (smem > 227 * 1024) return -1;
+  }
+  cudaFuncSetAttribute(gemm_bf16_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  const int num_tiles = ((M + BM - 1) / BM) * (N / BN);
+  const int grid = num_tiles < g_num_sms ? num_tiles : g_num_sms;
+  gemm_bf16_tcgen05<<<grid, side_items ? THREADS_SIDE : THREADS, smem, s>>>(ta, tb, bias, out, ldo, ssq, M, N, K, sp,
+                                                                           side_items);
   return (int)cudaGetLastError();
 }
 

@@ -45,6 +45,7 @@ struct NormRopeParams {
   int ssq_tile;             // columns per partial sum (256 from the QKV GEMM, 128 from row_ssq)
   int B, L, H, blk, NB;
   int heads_per_chunk;     // chunked output layout for the all-to-all send buffers (H: plain layout)
+  int compact;             // small-footprint variant (3-token ring) that fits beside a QKV GEMM CTA
   float eps;
 };
 int launch_norm_rope_pool(const NormRopeParams& p, bool norm, bool rope, bool pool, cudaStream_t s);
@@ -92,8 +93,10 @@ int launch_lowrank_reduce(const float* c_partial, int splits, int BH, int R, __n
 // gemm.cu -----------------------------------------------------------------
 // out[M, N] (row stride ldo) = A[M, K] * W[N, K]^T (+ bias[N]), bf16 in/out, fp32 accumulate;
 // ssq (optional) [M, N/256]: per-row sum of squares of the bf16 outputs of each 256-column tile
+// side (optional): a compact norm-only pass (B = 1) that spare warps of the
+// persistent GEMM run alongside the tensor-core work
 int launch_gemm_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const __nv_bfloat16* bias, __nv_bfloat16* out,
-                     int64_t ldo, float* ssq, int M, int N, int K, cudaStream_t s);
+                     int64_t ldo, float* ssq, int M, int N, int K, const NormRopeParams* side, cudaStream_t s);
 
 // attn.cu -----------------------------------------------------------------
 struct AttnParams {

@@ -61,6 +61,7 @@ __device__ __forceinline__ void store8(__nv_bfloat16* dst, const float (&v)[8]) 
 constexpr int kNormHeads = 8;                   // heads per CTA
 constexpr int kNormThreads = kNormHeads * 16;   // 128
 constexpr int kNormRing = 8;                    // tokens in flight
+constexpr int kNormRingCompact = 3;             // co-resident variant (fits beside a GEMM CTA)
 constexpr int kNormRow = kNormHeads * 128 * 2;  // bytes of one tensor row segment (2 KB)
 
 __device__ __forceinline__ void cp_async16_ca(uint32_t dst, const void* src) {
@@ -77,15 +78,26 @@ __device__ __forceinline__ void unpack8(const uint4 u, float (&v)[8]) {
   unpack_bf2(u.w, v[6], v[7]);
 }
 
-template <bool NORM, bool ROPE, bool POOL>
-__global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParams p) {
-  extern __shared__ __align__(16) uint8_t nsm[];
+__device__ __forceinline__ void named_bar_sync(int id) {
+  asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory");
+}
+
+// Shared memory of one norm work item: the token ring plus [2][blk] rstd.
+__host__ __device__ constexpr int norm_smem_bytes(int ring, int nslots, int blk, bool norm) {
+  return ring * nslots * kNormRow + (norm ? 2 * blk * 4 : 0);
+}
+
+// One work item of the streaming pass: token block m, head group grp, batch b,
+// run by 128 threads (j = 0..127, whole warps) that synchronise on the named
+// barrier bar_id only, so the item can also run on spare warps of another
+// kernel (the QKV GEMM).  nsm: norm_smem_bytes(RING, ...) of shared memory.
+template <bool NORM, bool ROPE, bool POOL, int RING>
+__device__ __forceinline__ void norm_block(const NormRopeParams& p, int m, int grp, int b, uint8_t* nsm, int j,
+                                           int bar_id) {
   const int nslots = 2 + (p.v_dst[0] != nullptr) + (p.x != nullptr && p.g_dst[0] != nullptr);
   const int slot_bytes = nslots * kNormRow;
-  float* s_rstd = reinterpret_cast<float*>(nsm + kNormRing * slot_bytes);  // [2][blk]
-  const int m = blockIdx.x, grp = blockIdx.y, b = blockIdx.z;
+  float* s_rstd = reinterpret_cast<float*>(nsm + RING * slot_bytes);  // [2][blk]
   const int dim = p.H * 128;
-  const int j = threadIdx.x;
   const int h = grp * kNormHeads + (j >> 4);
   const bool active = h < p.H;
   const int col = active ? h * 128 + (j & 15) * 8 : 0;
@@ -99,7 +111,7 @@ __global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParam
   auto issue = [&](int tl) {
     if (tl < n && active) {
       const int64_t row = (int64_t)b * p.L + t0 + tl;
-      const uint32_t slot = ring + (tl % kNormRing) * slot_bytes + j * 16;
+      const uint32_t slot = ring + (tl % RING) * slot_bytes + j * 16;
       cp_async16_ca(slot, p.q_in + row * p.ld_in + col);
       cp_async16_ca(slot + kNormRow, p.k_in + row * p.ld_in + col);
       if (has_v) cp_async16_ca(slot + 2 * kNormRow, p.v_in + row * p.ld_in + col);
@@ -108,18 +120,20 @@ __global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParam
     cp_async_commit_grp();  // one group per token, empty past the block
   };
 #pragma unroll
-  for (int i = 0; i < kNormRing; ++i) issue(i);
+  for (int i = 0; i < RING; ++i) issue(i);
   if (NORM) {
     // rstd of every token of the block from the per-tile sums of squares
+    // (the barrier first: the previous item of this thread group may still read s_rstd)
+    named_bar_sync(bar_id);
     const int per = dim / p.ssq_tile;
-    for (int i = threadIdx.x; i < 2 * n; i += blockDim.x) {
+    for (int i = j; i < 2 * n; i += kNormThreads) {
       const int which = i / n, tl = i - which * n;
       const float* src = p.ssq + ((int64_t)b * p.L + t0 + tl) * p.ssq_ld + which * per;
       float s = 0.f;
       for (int k = 0; k < per; ++k) s += src[k];
       s_rstd[which * p.blk + tl] = rsqrtf(s * (1.0f / (float)dim) + p.eps);
     }
-    __syncthreads();
+    named_bar_sync(bar_id);
   }
   float wq[8], wk[8];
   if (NORM && active) {
@@ -135,17 +149,17 @@ __global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParam
 
 #pragma unroll 1
   for (int tl = 0; tl < n; ++tl) {
-    cp_async_wait_grp<kNormRing - 1>();  // this token's chunks have landed
+    cp_async_wait_grp<RING - 1>();  // this token's chunks have landed
     const int t = t0 + tl;
     const int64_t row = (int64_t)b * p.L + t;
-    const uint8_t* slot = nsm + (tl % kNormRing) * slot_bytes + j * 16;
+    const uint8_t* slot = nsm + (tl % RING) * slot_bytes + j * 16;
     float q[8], k[8], xv[8];
     unpack8(*reinterpret_cast<const uint4*>(slot), q);
     unpack8(*reinterpret_cast<const uint4*>(slot + kNormRow), k);
     uint4 vraw = make_uint4(0, 0, 0, 0);
     if (has_v) vraw = *reinterpret_cast<const uint4*>(slot + 2 * kNormRow);
     if (gate) unpack8(*reinterpret_cast<const uint4*>(slot + (2 + has_v) * kNormRow), xv);
-    issue(tl + kNormRing);  // refill the slot just read (own chunks only)
+    issue(tl + RING);  // refill the slot just read (own chunks only)
     if (!active) continue;
     if (has_v) *reinterpret_cast<uint4*>(chunk_dst(p.v_dst, p, b, t, col)) = vraw;
     if (NORM) {
@@ -189,7 +203,7 @@ __global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParam
 #pragma unroll
       for (int i = 0; i < 8; ++i) g = fmaf(xv[i], gw[i], g);
       // the 16 lanes of one head (the other half-warp may be an absent head)
-      const unsigned half = 0xffffu << (threadIdx.x & 16);
+      const unsigned half = 0xffffu << (j & 16);
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1) g += __shfl_xor_sync(half, g, o);
       if ((j & 15) == 0) {
@@ -204,8 +218,8 @@ __global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParam
   // after the block barrier orders every thread's rows before the kernel's
   // completion is signalled to the other ranks
   if (p.heads_per_chunk != p.H) {
-    __syncthreads();
-    if (threadIdx.x == 0) __threadfence_system();
+    named_bar_sync(bar_id);
+    if (j == 0) __threadfence_system();
   }
   if (POOL && active) {
     const float nx = (float)n;
@@ -217,6 +231,12 @@ __global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParam
     ko[0] = make_float4(ks[0], ks[1], ks[2], ks[3]);
     ko[1] = make_float4(ks[4], ks[5], ks[6], ks[7]);
   }
+}
+
+template <bool NORM, bool ROPE, bool POOL, int RING>
+__global__ void __launch_bounds__(kNormThreads) norm_stream_kernel(NormRopeParams p) {
+  extern __shared__ __align__(16) uint8_t nsm[];
+  norm_block<NORM, ROPE, POOL, RING>(p, blockIdx.x, blockIdx.y, blockIdx.z, nsm, threadIdx.x, 0);
 }
 
 // per-row sums of squares of q and k over tiles of 128 columns (q tiles, then k tiles)
@@ -250,19 +270,26 @@ int launch_row_ssq(const __nv_bfloat16* q, const __nv_bfloat16* k, int64_t ld, i
 int launch_norm_rope_pool(const NormRopeParams& p, bool norm, bool rope, bool pool, cudaStream_t s) {
   if (norm && (p.ssq == nullptr || p.ssq_tile <= 0 || (p.H * 128) % p.ssq_tile != 0)) return -1;
   const int nslots = 2 + (p.v_dst[0] != nullptr) + (p.x != nullptr && p.g_dst[0] != nullptr);
-  const int smem = kNormRing * nslots * kNormRow + (norm ? 2 * p.blk * (int)sizeof(float) : 0);
+  const int ring = p.compact ? kNormRingCompact : kNormRing;
+  const int smem = norm_smem_bytes(ring, nslots, p.blk, norm);
   if (smem > 227 * 1024) return -1;
   dim3 grid(p.NB, (p.H + kNormHeads - 1) / kNormHeads, p.B);
-#define ROLA_NORM(N, R, P)                                                                              \
-  do {                                                                                                  \
-    cudaFuncSetAttribute(norm_stream_kernel<N, R, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-    norm_stream_kernel<N, R, P><<<grid, kNormThreads, smem, s>>>(p);                                    \
+#define ROLA_NORM(N, R, P, RING)                                                                          \
+  do {                                                                                                    \
+    cudaFuncSetAttribute(norm_stream_kernel<N, R, P, RING>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+    cudaFuncSetAttribute(norm_stream_kernel<N, R, P, RING>, cudaFuncAttributePreferredSharedMemoryCarveout,   \
+                         cudaSharedmemCarveoutMaxShared);                                                 \
+    norm_stream_kernel<N, R, P, RING><<<grid, kNormThreads, smem, s>>>(p);                                \
   } while (0)
-  if (norm && rope && pool) ROLA_NORM(true, true, true);
-  else if (norm && rope) ROLA_NORM(true, true, false);
-  else if (norm) ROLA_NORM(true, false, false);
-  else if (rope && pool) ROLA_NORM(false, true, true);
-  else if (rope) ROLA_NORM(false, true, false);
+  if (p.compact) {
+    // the norm-only pass that runs beside the QKV GEMM of the next chunk
+    if (!norm || rope || pool) return -1;
+    ROLA_NORM(true, false, false, kNormRingCompact);
+  } else if (norm && rope && pool) ROLA_NORM(true, true, true, kNormRing);
+  else if (norm && rope) ROLA_NORM(true, true, false, kNormRing);
+  else if (norm) ROLA_NORM(true, false, false, kNormRing);
+  else if (rope && pool) ROLA_NORM(false, true, true, kNormRing);
+  else if (rope) ROLA_NORM(false, true, false, kNormRing);
   else return -1;
 #undef ROLA_NORM
   return (int)cudaGetLastError();

@@ -245,7 +245,6 @@ int launch_topk(const float* scores, int rows, int NBk, int k, int32_t* lut, cud
 // every score accumulated over d in order (the same FMA chain as
 // scores_kernel), then the warp picks each row's top-k exactly as topk_kernel.
 // ---------------------------------------------------------------------------
-constexpr int kSelRows = 64;          // query blocks per CTA (16 warps x 4 rows)
 constexpr int kSelWords = 65;         // smem row stride of pooled K, 32-bit words
 constexpr int kSelMaxNBk = 768;       // shared-memory bound of the fused kernel
 
@@ -286,15 +285,18 @@ __device__ __forceinline__ void warp_topk_emit(const float (&acc)[PER], int per,
   }
 }
 
-template <int PER>
+// RW query rows per warp, 16 * RW per CTA (fewer when B*H is small, so that
+// the grid still covers the SMs)
+template <int PER, int RW>
 __global__ void __launch_bounds__(512) select_fused_kernel(const __nv_bfloat16* __restrict__ pq,
                                                            const __nv_bfloat16* __restrict__ pk, int NBq, int NBk,
                                                            int k, int32_t* __restrict__ lut) {
+  constexpr int ROWS = 16 * RW;
   extern __shared__ uint32_t sel_smem[];
   uint32_t* sk = sel_smem;                                    // [NBk][65] words (bf16 pairs)
-  uint32_t* sq = sel_smem + ((NBk * kSelWords + 3) & ~3);     // [64][64] words, 16-byte aligned
+  uint32_t* sq = sel_smem + ((NBk * kSelWords + 3) & ~3);     // [ROWS][64] words, 16-byte aligned
   const int bh = blockIdx.y;
-  const int m0 = blockIdx.x * kSelRows;
+  const int m0 = blockIdx.x * ROWS;
   const uint4* kb = reinterpret_cast<const uint4*>(pk + (int64_t)bh * NBk * 128);
   // staging: eight 16-byte loads in flight per thread before their smem stores
   for (int i0 = threadIdx.x; i0 < NBk * 16; i0 += 8 * blockDim.x) {
@@ -317,7 +319,7 @@ __global__ void __launch_bounds__(512) select_fused_kernel(const __nv_bfloat16* 
     }
   }
   const uint4* qb = reinterpret_cast<const uint4*>(pq + (int64_t)bh * NBq * 128);
-  for (int i = threadIdx.x; i < kSelRows * 16; i += blockDim.x) {
+  for (int i = threadIdx.x; i < ROWS * 16; i += blockDim.x) {
     const int r = i >> 4;
     const uint4 u = (m0 + r < NBq) ? qb[(int64_t)m0 * 16 + i] : make_uint4(0, 0, 0, 0);
     reinterpret_cast<uint4*>(sq)[i] = u;
@@ -326,18 +328,18 @@ __global__ void __launch_bounds__(512) select_fused_kernel(const __nv_bfloat16* 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int per = (NBk + 31) / 32;
   {
-    const int rr0 = warp * 4;  // the 4 query rows of this warp
+    const int rr0 = warp * RW;  // the RW query rows of this warp
     if (m0 + rr0 >= NBq) return;
-    float acc[4][PER];
+    float acc[RW][PER];
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+    for (int a = 0; a < RW; ++a)
 #pragma unroll
       for (int i = 0; i < PER; ++i) acc[a][i] = 0.f;
 #pragma unroll 2
     for (int w = 0; w < 64; ++w) {
-      float q0[4], q1[4];
+      float q0[RW], q1[RW];
 #pragma unroll
-      for (int a = 0; a < 4; ++a) unpack_bf2(sq[(rr0 + a) * 64 + w], q0[a], q1[a]);
+      for (int a = 0; a < RW; ++a) unpack_bf2(sq[(rr0 + a) * 64 + w], q0[a], q1[a]);
 #pragma unroll
       for (int i = 0; i < PER; ++i) {
         const int j = lane + 32 * i;
@@ -345,7 +347,7 @@ __global__ void __launch_bounds__(512) select_fused_kernel(const __nv_bfloat16* 
           float k0, k1;
           unpack_bf2(sk[j * kSelWords + w], k0, k1);
 #pragma unroll
-          for (int a = 0; a < 4; ++a) {
+          for (int a = 0; a < RW; ++a) {
             acc[a][i] = __fmaf_rn(q0[a], k0, acc[a][i]);
             acc[a][i] = __fmaf_rn(q1[a], k1, acc[a][i]);
           }
@@ -353,7 +355,7 @@ __global__ void __launch_bounds__(512) select_fused_kernel(const __nv_bfloat16* 
       }
     }
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
+    for (int a = 0; a < RW; ++a) {
       const int m = m0 + rr0 + a;
       if (m < NBq) warp_topk_emit<PER>(acc[a], per, NBk, k, lane, lut + ((int64_t)bh * NBq + m) * k);
     }
@@ -363,19 +365,36 @@ __global__ void __launch_bounds__(512) select_fused_kernel(const __nv_bfloat16* 
 int launch_select_fused(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH, int NBq, int NBk, int k,
                         int32_t* lut, cudaStream_t s) {
   if (NBk > kSelMaxNBk || k < 1 || k > NBk) return -1;
-  const int smem = (((NBk * kSelWords + 3) & ~3) + kSelRows * 64) * 4;
-  dim3 grid((NBq + kSelRows - 1) / kSelRows, BH);
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  // rows per warp: 4 when the grid covers the SMs twice over, else fewer
+  int rw = 4;
+  while (rw > 1 && (int64_t)BH * ((NBq + 16 * rw - 1) / (16 * rw)) < 2 * sms) rw >>= 1;
+  const int smem = (((NBk * kSelWords + 3) & ~3) + 16 * rw * 64) * 4;
+  dim3 grid((NBq + 16 * rw - 1) / (16 * rw), BH);
   const int per = (NBk + 31) / 32;
-#define ROLA_SEL(P)                                                                                  \
-  do {                                                                                               \
-    cudaFuncSetAttribute(select_fused_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-    select_fused_kernel<P><<<grid, 512, smem, s>>>(pq, pk, NBq, NBk, k, lut);                        \
+#define ROLA_SEL(P, RW)                                                                                   \
+  do {                                                                                                    \
+    cudaFuncSetAttribute(select_fused_kernel<P, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);  \
+    select_fused_kernel<P, RW><<<grid, 512, smem, s>>>(pq, pk, NBq, NBk, k, lut);                         \
   } while (0)
-  if (per <= 4) ROLA_SEL(4);
-  else if (per <= 8) ROLA_SEL(8);
-  else if (per <= 16) ROLA_SEL(16);
-  else if (per <= 20) ROLA_SEL(20);
-  else ROLA_SEL(24);
+#define ROLA_SEL_RW(P)            \
+  do {                            \
+    if (rw == 4) ROLA_SEL(P, 4);  \
+    else if (rw == 2) ROLA_SEL(P, 2); \
+    else ROLA_SEL(P, 1);          \
+  } while (0)
+  if (per <= 4) ROLA_SEL_RW(4);
+  else if (per <= 8) ROLA_SEL_RW(8);
+  else if (per <= 16) ROLA_SEL_RW(16);
+  else if (per <= 20) ROLA_SEL_RW(20);
+  else ROLA_SEL_RW(24);
+#undef ROLA_SEL_RW
 #undef ROLA_SEL
   return (int)cudaGetLastError();
 }

@@ -70,10 +70,11 @@ def default_splits(B: int, H: int, L: int) -> int:
 # fused B200 path
 # ---------------------------------------------------------------------------
 def qkv_gemm(x2d: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
-             ssq: torch.Tensor | None = None) -> torch.Tensor:
+             ssq: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
     """out[M, N] = x[M, K] w[N, K]^T (+ bias) on tcgen05 (bf16 in/out, fp32 accumulate).
     ``ssq`` (fp32 ``[M, N/256]``) receives each row's sum of squares of its bf16
-    outputs per 256-column tile."""
+    outputs per 256-column tile.  ``out`` (contiguous bf16 ``[M, N]``) is
+    written in place when given."""
     _require_cuda(x2d, w, bias)
     if x2d.dtype != BF16 or w.dtype != BF16:
         raise ValueError("qkv_gemm: bf16 operands required")
@@ -83,7 +84,10 @@ def qkv_gemm(x2d: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = Non
     N = w.shape[0]
     if w.shape[1] != K:
         raise ValueError(f"qkv_gemm: weight {tuple(w.shape)} does not match x {tuple(x2d.shape)}")
-    out = torch.empty(M, N, device=x2d.device, dtype=BF16)
+    if out is None:
+        out = torch.empty(M, N, device=x2d.device, dtype=BF16)
+    elif out.shape != (M, N) or out.dtype != BF16 or not out.is_contiguous():
+        raise ValueError("qkv_gemm: out must be a contiguous bf16 [M, N] tensor")
     b = None if bias is None else bias.to(BF16).contiguous()
     if ssq is not None and (ssq.dtype != torch.float32 or ssq.shape != (M, N // 256) or not ssq.is_contiguous()):
         raise ValueError("qkv_gemm: ssq must be a contiguous fp32 [M, N/256] tensor")

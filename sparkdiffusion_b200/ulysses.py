@@ -37,6 +37,8 @@ CPU ranks in the tests); ``ulysses_rola_attention`` runs the CUDA kernels.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -74,17 +76,113 @@ def _peer_layout(B: int, Ls: int, H: int, p: int) -> dict:
 _out_slot: dict = {}
 
 
+def _scatter_args(qkv, ssq, xc, nwq, nwk, gw, gb, H, p, L, eps, buf, b, r0, t0, t1):
+    """rola_scatter_args of tokens [t0, t1) of batch b (rows r0.. of qkv) into
+    rows rank*Ls + t0.. of every rank's head buffers (buf)."""
+    dim = H * HEAD_DIM
+    Hl = H // p
+    a = _lib.ScatterArgs()
+    a.q_raw, a.k_raw, a.v_raw = _ptr(qkv[r0]), _ptr(qkv[r0, dim:]), _ptr(qkv[r0, 2 * dim:])
+    a.ld_raw = 3 * dim
+    a.ssq, a.ssq_ld = _ptr(ssq[r0]), ssq.shape[-1]
+    a.B, a.L, a.H, a.world, a.eps = 1, t1 - t0, H, p, eps
+    a.dst_rows, a.dst_row0 = L, t0
+    a.x = _ptr(xc[r0])
+    a.norm_wq, a.norm_wk, a.gate_w, a.gate_b = _ptr(nwq), _ptr(nwk), _ptr(gw), _ptr(gb)
+    boff = b * L * Hl * HEAD_DIM * 2
+    goff = b * L * Hl * 2
+    for name, field, off in (("q", "q_dst", boff), ("k", "k_dst", boff), ("v", "v_dst", boff),
+                             ("gate", "g_dst", goff)):
+        tab = getattr(a, field)
+        for r, ptr in enumerate(buf.region(name).table):
+            tab[r] = ptr + off
+    return a
+
+
+def chunk_plan(rows: int, n_tiles: int, sms: int, chunks: int | None = None) -> list[int]:
+    """Token-chunk sizes of the GEMM / scatter overlap.  ``chunks`` given: equal
+    chunks of whole 128-row tiles.  Otherwise a halving sequence (each chunk's
+    GEMM hides the previous chunk's scatter; the last, exposed one is small) of
+    sizes whose ``m_tiles * n_tiles`` output tiles fill the ``sms`` persistent
+    CTAs in whole waves where possible."""
+    m_tiles = -(-rows // 128)
+    if chunks is not None:
+        step = -(-m_tiles // max(1, chunks))
+        sizes = [step] * (m_tiles // step) + ([m_tiles % step] if m_tiles % step else [])
+    else:
+        def eff(s):
+            t = s * n_tiles
+            return t / (-(-t // sms) * sms)
+
+        sizes, left = [], m_tiles
+        while left > 8:
+            target = left // 2
+            s = max(range(max(1, (3 * target) // 4), target + 1), key=lambda c: (round(eff(c), 2), c))
+            sizes.append(s)
+            left -= s
+        if left:
+            sizes.append(left)
+    out, start = [], 0
+    for s in sizes:
+        n = min(rows - start, s * 128)
+        if n > 0:
+            out.append(n)
+            start += n
+    return out
+
+
+def _gemm_scatter_overlapped(x_local, w_qkv, b_qkv, nwq, nwk, gw, gb, xc, H, p, rank, eps, buf, chunks, events):
+    """QKV GEMM and the scattering norm pass in token chunks: the persistent
+    GEMM of chunk c carries the scatter of chunk c-1 on spare warps
+    (rola_b200_qkv_gemm_scatter), so the NVLink traffic hides under the
+    tensor-core work; the last chunk's scatter runs on its own."""
+    B, Ls, dim = x_local.shape
+    dev = x_local.device
+    st = _stream()
+    L = Ls * p
+    x2d = x_local.reshape(B * Ls, dim)
+    xc2 = xc.view(B * Ls, dim)
+    qkv = torch.empty(B * Ls, 3 * dim, device=dev, dtype=BF16)
+    ssq = torch.empty(B * Ls, 3 * dim // 256, device=dev, dtype=torch.float32)
+    bias = None if b_qkv is None else b_qkv.to(BF16).contiguous()
+    w = w_qkv.contiguous()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    plan = chunk_plan(Ls, 3 * dim // 256, sms, chunks)
+    if events is not None:
+        events["gemm"][0].record()
+    prev = None
+    for b in range(B):
+        t1 = 0
+        for n in plan:
+            t0, t1 = t1, t1 + n
+            r0, r1 = b * Ls + t0, b * Ls + t1
+            if prev is None:
+                _lib.call("rola_b200_qkv_gemm", _ptr(x2d[r0]), _ptr(w), _ptr(bias), _ptr(qkv[r0]), _ptr(ssq[r0]),
+                          r1 - r0, 3 * dim, dim, st)
+            else:
+                _lib.call("rola_b200_qkv_gemm_scatter", _ptr(x2d[r0]), _ptr(w), _ptr(bias), _ptr(qkv[r0]),
+                          _ptr(ssq[r0]), r1 - r0, 3 * dim, dim, ctypes.byref(prev), st)
+            prev = _scatter_args(qkv, ssq, xc2, nwq, nwk, gw, gb, H, p, L, eps, buf, b, r0, rank * Ls + t0,
+                                 rank * Ls + t1)
+    _lib.call("rola_b200_qk_norm_scatter", ctypes.byref(prev), 0, st)
+    if events is not None:
+        events["gemm"][1].record()
+
+
 def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk,
                                   proj_q, proj_k, gate_w, gate_b, num_heads: int, topk: int, group=None,
                                   eps: float = 1e-6, splits: int | None = None, events: dict | None = None,
-                                  transport: str = "peer"):
+                                  transport: str = "peer", chunks: int | None = None):
     """Sequence-sharded RoLa forward: ``x_local [B, Ls, H*D]`` on this rank ->
     ``[B, Ls, H*D]`` (excluding the output projection).  ``cos_sin`` and the
     low-rank tables cover the whole sequence (global positions).
 
     With ``transport="peer"`` the result is a view of one of two alternating
     peer-mapped output buffers: it stays valid until the second-next call with
-    the same shapes and group, and consumers must run on the current stream."""
+    the same shapes and group, and consumers must run on the current stream.
+    The peer transport overlaps the QKV GEMM with the scattering norm pass in
+    token chunks (``chunk_plan``; ``chunks`` forces that many equal chunks,
+    1 turns the overlap off)."""
     if transport not in ("peer", "nccl"):
         raise ValueError(f"unknown transport {transport!r}")
     p = dist.get_world_size(group)
@@ -98,12 +196,6 @@ def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin
         raise ValueError("cos_sin must cover the full (global) sequence")
     dev = x_local.device
     st = _stream()
-    ssq = torch.empty(B * Ls, 3 * dim // 256, device=dev, dtype=torch.float32)
-    if events is not None:
-        events["gemm"][0].record()
-    qkv = ops.qkv_gemm(x_local.reshape(B * Ls, dim), w_qkv, b_qkv, ssq)
-    if events is not None:
-        events["gemm"][1].record()
     gw = _bf16_vec(gate_w, HEAD_DIM, "gate_w")
     gb = _bf16_vec(gate_b, H, "gate_b")
     nwq = _bf16_vec(norm_wq, dim, "norm_wq")
@@ -114,12 +206,29 @@ def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin
         key = ("ulysses", B, Ls, H, str(dev))
         buf = peer.cached_buffer(key, _peer_layout(B, Ls, H, p), group)
         rq, rk, rv, rg = (buf.region(n) for n in ("q", "k", "v", "gate"))
-        _lib.call("rola_b200_qk_norm_scatter", _ptr(qkv), _ptr(qkv[:, dim:]), _ptr(qkv[:, 2 * dim:]), 3 * dim,
-                  _ptr(ssq), ssq.shape[-1], _ptr(xc), _ptr(nwq), _ptr(nwk), _ptr(gw), _ptr(gb), B, Ls, H, p, rank,
-                  eps, rq.table, rk.table, rv.table, rg.table, st)
+        if chunks is None or chunks > 1:
+            _gemm_scatter_overlapped(x_local, w_qkv, b_qkv, nwq, nwk, gw, gb, xc, H, p, rank, eps, buf, chunks,
+                                     events)
+        else:
+            ssq = torch.empty(B * Ls, 3 * dim // 256, device=dev, dtype=torch.float32)
+            if events is not None:
+                events["gemm"][0].record()
+            qkv = ops.qkv_gemm(x_local.reshape(B * Ls, dim), w_qkv, b_qkv, ssq)
+            if events is not None:
+                events["gemm"][1].record()
+            a = _scatter_args(qkv, ssq, xc.view(B * Ls, dim), nwq, nwk, gw, gb, H, p, L, eps, buf, 0, 0,
+                              rank * Ls, rank * Ls + Ls)
+            a.B = B
+            _lib.call("rola_b200_qk_norm_scatter", ctypes.byref(a), 0, st)
         peer.stream_barrier(group)
         q_n, k_n, v, gate = rq.tensor, rk.tensor, rv.tensor, rg.tensor
     else:
+        ssq = torch.empty(B * Ls, 3 * dim // 256, device=dev, dtype=torch.float32)
+        if events is not None:
+            events["gemm"][0].record()
+        qkv = ops.qkv_gemm(x_local.reshape(B * Ls, dim), w_qkv, b_qkv, ssq)
+        if events is not None:
+            events["gemm"][1].record()
         q_send = torch.empty(B, p, Ls, Hl * HEAD_DIM, device=dev, dtype=BF16)
         k_send = torch.empty_like(q_send)
         v_send = torch.empty_like(q_send)

@@ -5,7 +5,7 @@ shard of the hidden states; the result gathered from all ranks must match the
 single-GPU forward within the bf16 tolerance (the gate is summed in a different
 order on the two paths, so outputs may differ by bf16 rounding).  Both
 transports run: the exchanges fused into the kernels over peer memory, and the
-NCCL all-to-all.  With 8 ranks the shards (90 tokens) do not align with the
+NCCL all-to-all.  With 8 ranks the shards (360 tokens) do not align with the
 128-token blocks, so blocks straddle ranks in both exchanges.
 """
 
@@ -32,7 +32,7 @@ def _free_port():
 def _workload():
     from sparkdiffusion_b200.workloads import C3
 
-    wl = C3.scaled(H=8, grid=(3, 10, 24), B=1)  # L = 720 (NB = 6, ragged tail)
+    wl = C3.scaled(H=8, grid=(4, 16, 45), B=1)  # L = 2880 (NB = 23, ragged tail of 64)
     return wl.__class__(**{**wl.__dict__, "topk": 3})
 
 
@@ -50,7 +50,7 @@ def _inputs(wl, dev):
     return inp, common
 
 
-def _rank_main(rank, world, transport, port, out_path):
+def _rank_main(rank, world, transport, chunks, port, out_path):
     import datetime
 
     import torch.distributed as dist
@@ -71,7 +71,7 @@ def _rank_main(rank, world, transport, port, out_path):
     outs = []
     for _ in range(3):  # both alternating output buffers, then the first again
         out = ulysses_rola_attention_params(x_local, inp["w_qkv"], None, *common, wl.H, wl.topk,
-                                            transport=transport)
+                                            transport=transport, chunks=chunks)
         outs.append(out.clone())
     torch.cuda.synchronize()
     status = _lib.device_status()
@@ -86,17 +86,20 @@ def _rank_main(rank, world, transport, port, out_path):
     dist.destroy_process_group()
 
 
-CASES = [(2, "peer"), (2, "nccl"), (4, "peer"), (8, "peer")]
+# (ranks, transport, token chunks of the GEMM / scatter overlap: None = the
+# automatic plan, 1 = no overlap); with 8 ranks and 2 chunks the 360-token
+# shards split into 256 + 104 tokens
+CASES = [(2, "peer", None), (2, "peer", 1), (2, "nccl", 1), (4, "peer", None), (8, "peer", 2)]
 
 
-@pytest.mark.parametrize("world,transport", CASES, ids=[f"{w}gpu-{t}" for w, t in CASES])
-def test_ulysses_matches_single_gpu(tmp_path, world, transport):
+@pytest.mark.parametrize("world,transport,chunks", CASES, ids=[f"{w}gpu-{t}-c{c}" for w, t, c in CASES])
+def test_ulysses_matches_single_gpu(tmp_path, world, transport, chunks):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     from sparkdiffusion_b200 import ops
 
     out_path = str(tmp_path / "ulysses.pt")
-    mp.start_processes(_rank_main, args=(world, transport, _free_port(), out_path), nprocs=world,
+    mp.start_processes(_rank_main, args=(world, transport, chunks, _free_port(), out_path), nprocs=world,
                        start_method="spawn")
     got = torch.load(out_path)
     assert got["status"] == 0
