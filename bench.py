@@ -6,14 +6,16 @@ One step = one RoLa attention layer forward without the output projection
 (QKV GEMM + qk-RMSNorm + RoPE, block selection, low-rank branch, block-sparse
 attention with the fused epilogue) over one batch of synthetic inputs.  At N
 GPUs the same layer is split Ulysses-style (sequence shards for the prologue,
-head shards for attention, NCCL all-to-alls in between), so the total work is
-fixed (strong scaling).
+head shards for attention; the exchanges are fused into the norm pass and the
+attention epilogue as peer stores over NVLink), so the total work is fixed
+(strong scaling).
 
 ``value`` = selected-block attention FLOPs of the whole layer (4*D*sum rows*cols
 over valid tokens, from the actual LUT) / (max over ranks of the device time
-per step).  ``e2e`` is the same metric through the single C-ABI call (1 GPU) or
-the Ulysses entry (N GPUs) with the hidden states copied in from pinned host
-memory and the output copied back each step.
+per step).  ``e2e`` is the same metric through the C-ABI host-buffer pipeline
+(``rola_b200_pipeline_forward``, 1 GPU) or the Ulysses entry (N GPUs) with the
+hidden states copied in from pinned host memory and the output copied back
+every step; the copies of neighbouring steps overlap each step's kernels.
 
 ``--impl reference`` times the reference algorithm on the host CPU cores (the
 CPU oracle port, see ``oracle/``) on a bounded sample of the same workload.
@@ -326,36 +328,65 @@ def main():
     ms, t_gemm, t_attn = (float(v) for v in stats.tolist())
     status = _lib.device_status()
 
-    # end to end: pinned host -> device, forward, device -> pinned host, every step
+    # end to end: every step uploads its hidden states from pinned host memory
+    # and downloads its result into pinned host memory; consecutive steps
+    # overlap those copies with the neighbouring steps' kernels (double-buffered
+    # device copies, separate copy streams)
     e2e = None
     if not args.no_e2e:
         x_host = x.cpu().pin_memory()
-        x_dev = torch.empty_like(x)
         out_host = torch.empty(B, Ls, dim, dtype=torch.bfloat16).pin_memory()
         if world == 1:
-            ws_bytes = _lib.lib().rola_b200_forward_workspace_bytes(B, L, H, 128, wl.rank,
-                                                                     ops.default_splits(B, H, L))
-            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-            out_dev = torch.empty(B, L, dim, dtype=torch.bfloat16, device=dev)
+            pipe = ops.ForwardPipeline(x_host.numel() * 2, out_host.numel() * 2)
 
-            def e2e_step():
-                x_dev.copy_(x_host, non_blocking=True)
-                ops.rola_forward_capi(x_dev, w_qkv, None, *common, H, wl.topk, workspace=ws, out=out_dev)
-                out_host.copy_(out_dev, non_blocking=True)
+            def e2e_step(i):
+                pipe.forward(x_host, out_host, w_qkv, None, *common, H, wl.topk)
+
+            def e2e_flush():
+                pipe.wait()
         else:
-            def e2e_step():
-                x_dev.copy_(x_host, non_blocking=True)
-                o = step(x_dev)
-                out_host.copy_(o, non_blocking=True)
-        for _ in range(3):
-            e2e_step()
+            main = torch.cuda.current_stream()
+            h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+            x_devs = [torch.empty_like(x), torch.empty_like(x)]
+            ev = {"x_free": [None, None], "d2h": [None, None]}
+
+            def e2e_step(i):
+                s = i & 1
+                with torch.cuda.stream(h2d):
+                    if ev["x_free"][s] is not None:
+                        h2d.wait_event(ev["x_free"][s])
+                    x_devs[s].copy_(x_host, non_blocking=True)
+                x_ready = torch.cuda.Event()
+                x_ready.record(h2d)
+                main.wait_event(x_ready)
+                if ev["d2h"][s] is not None:  # step i-2's download read the output buffer this step reuses
+                    main.wait_event(ev["d2h"][s])
+                o = step(x_devs[s])
+                done = torch.cuda.Event()
+                done.record(main)
+                ev["x_free"][s] = done
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(done)
+                    out_host.copy_(o, non_blocking=True)
+                    e = torch.cuda.Event()
+                    e.record(d2h)
+                    ev["d2h"][s] = e
+
+            def e2e_flush():
+                for e in ev["d2h"]:
+                    if e is not None:
+                        main.wait_event(e)
+        for i in range(3):
+            e2e_step(i)
+        e2e_flush()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record()
-        for _ in range(K):
-            e2e_step()
+        for i in range(K):
+            e2e_step(3 + i)
+        e2e_flush()
         e2.record()
         torch.cuda.synchronize()
         t_e2e = torch.tensor([s2.elapsed_time(e2) / K], dtype=torch.float64, device=dev)
@@ -365,7 +396,11 @@ def main():
         e2e = {"value": flops_total / (t_e2e * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": t_e2e,
                "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
                "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
-               "api": "rola_b200_rola_forward (C ABI)" if world == 1 else "ulysses_rola_attention_params"}
+               "api": ("rola_b200_pipeline_forward (C ABI, host buffers)" if world == 1
+                       else "ulysses_rola_attention_params"),
+               "overlap": "uploads / downloads of neighbouring steps overlap each step's kernels"}
+        if world == 1:
+            pipe.close()
 
     cpu_base = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:

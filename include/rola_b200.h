@@ -265,6 +265,28 @@ int rola_b200_rola_forward(const void* x, const void* w_qkv, const void* b_qkv, 
                            void* workspace, size_t workspace_bytes, void* out, int32_t* lut_out,
                            rola_stream_t stream);
 
+/* Host-buffer pipeline (no counterpart in the reference, which takes device
+ * tensors): rola_b200_pipeline_forward uploads one step's hidden states from
+ * PINNED host memory x_host, runs rola_b200_rola_forward and downloads the
+ * result into pinned out_host, all asynchronously on the pipeline's own
+ * upload / compute / download streams with double-buffered device copies of
+ * x and out, so consecutive calls overlap step s+1's upload and step s-1's
+ * download with step s's kernels.  The step starts after the work already on
+ * `stream`; rola_b200_pipeline_wait makes `stream` wait for every submitted
+ * step (out_host of a step is complete then).  Host buffers must stay valid
+ * until that point.  x_bytes / out_bytes: the largest B*L*dim*2 to submit.
+ * Other arguments as rola_b200_rola_forward. */
+typedef struct rola_pipeline rola_pipeline;
+int rola_b200_pipeline_create(size_t x_bytes, size_t out_bytes, rola_pipeline** out);
+int rola_b200_pipeline_forward(rola_pipeline* pl, const void* x_host, const void* w_qkv, const void* b_qkv,
+                               const void* norm_wq, const void* norm_wk, const float* cos_sin, const void* lr_cos,
+                               const void* lr_sin, int rope_dim, const void* proj_q, const void* proj_k,
+                               const void* gate_w, const void* gate_b, int B, int L, int H, int blk, int topk, int R,
+                               int splits, float eps, void* workspace, size_t workspace_bytes, void* out_host,
+                               rola_stream_t stream);
+int rola_b200_pipeline_wait(rola_pipeline* pl, rola_stream_t stream);
+int rola_b200_pipeline_destroy(rola_pipeline* pl);
+
 #ifdef __cplusplus
 }
 #endif

@@ -66,6 +66,11 @@ SIGNATURES = {
     "rola_b200_lowrank_kv_noalloc": [_P, _L, _L, _L, _P, _L, _L, _L, _P, _P, _P, _I, _I, _I, _I, _I, _I,
                                      _P, _P, _P],
     "rola_b200_forward_workspace_bytes": [_I, _I, _I, _I, _I, _I],
+    "rola_b200_pipeline_create": [_Z, _Z, ctypes.POINTER(_P)],
+    "rola_b200_pipeline_forward": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I,
+                                   _I, _F, _P, _Z, _P, _P],
+    "rola_b200_pipeline_wait": [_P, _P],
+    "rola_b200_pipeline_destroy": [_P],
     "rola_b200_rola_forward": [_P, _P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I,
                                _I, _I, _F, _P, _Z, _P, _P, _P],
 }

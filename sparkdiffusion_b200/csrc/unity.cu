@@ -8,4 +8,5 @@
 #include "attn.cu"
 #include "capi.cu"
 #include "peer.cu"
+#include "pipeline.cu"
 #include "noalloc.cu"

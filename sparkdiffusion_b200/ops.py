@@ -18,6 +18,8 @@ there is no CPU or PyTorch fallback.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -269,6 +271,54 @@ def rola_forward_capi(x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm_w
               _ptr(_bf16_vec(gate_b, H, "gate_b")), B, L, H, 128, topk, R, splits, eps, _ptr(workspace), need,
               _ptr(out), None, _stream())
     return out
+
+
+class ForwardPipeline:
+    """Host-buffer forward through ``rola_b200_pipeline_forward``: every call
+    uploads pinned ``x_host [B, L, dim]``, runs the forward and downloads into
+    pinned ``out_host``; consecutive calls overlap uploads and downloads with
+    the previous / next step's kernels.  ``wait()`` orders the current stream
+    after every submitted step."""
+
+    def __init__(self, x_bytes: int, out_bytes: int):
+        self._lib = _lib.lib()
+        h = ctypes.c_void_p()
+        _lib.check(self._lib.rola_b200_pipeline_create(x_bytes, out_bytes, ctypes.byref(h)),
+                   "rola_b200_pipeline_create")
+        self._h = h
+        self._ws = None
+
+    def forward(self, x_host, out_host, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk, proj_q,
+                proj_k, gate_w, gate_b, num_heads: int, topk: int, eps: float = 1e-6, splits: int | None = None):
+        if not (x_host.is_pinned() and out_host.is_pinned()):
+            raise ValueError("ForwardPipeline: x_host and out_host must be pinned host tensors")
+        B, L, dim = x_host.shape
+        H = num_heads
+        R = proj_q.shape[0]
+        splits = splits or default_splits(B, H, L)
+        need = self._lib.rola_b200_forward_workspace_bytes(B, L, H, 128, R, splits)
+        dev = w_qkv.device
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, device=dev, dtype=torch.uint8)
+        _lib.call("rola_b200_pipeline_forward", self._h, _ptr(x_host), _ptr(w_qkv), _ptr(b_qkv),
+                  _ptr(_bf16_vec(norm_wq, dim, "norm_wq")), _ptr(_bf16_vec(norm_wk, dim, "norm_wk")), _ptr(cos_sin),
+                  _ptr(lr_cos), _ptr(lr_sin), rope_dim, _ptr(proj_q), _ptr(proj_k),
+                  _ptr(_bf16_vec(gate_w, HEAD_DIM, "gate_w")), _ptr(_bf16_vec(gate_b, H, "gate_b")), B, L, H, 128,
+                  topk, R, splits, eps, _ptr(self._ws), need, _ptr(out_host), _stream())
+
+    def wait(self) -> None:
+        _lib.call("rola_b200_pipeline_wait", self._h, _stream())
+
+    def close(self) -> None:
+        if self._h is not None:
+            _lib.call("rola_b200_pipeline_destroy", self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 # ---------------------------------------------------------------------------

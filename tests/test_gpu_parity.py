@@ -288,3 +288,27 @@ def test_reference_api_sparse_attn():
     assert_bf16_close(o.cpu(), ref, "fused_sparse_attn")
     with pytest.raises(ValueError):
         ops.fused_sparse_attn(q.cuda(), k.cuda(), v.cuda(), num_heads=3)
+
+
+def test_host_pipeline_matches_device_forward():
+    """rola_b200_pipeline_forward (pinned host in/out, overlapped steps) gives
+    exactly the device-buffer forward's output for every step."""
+    wl = C3.scaled(H=4, grid=(3, 10, 20))
+    wl = wl.__class__(**{**wl.__dict__, "topk": 3})
+    inp, cos_sin, lr_cos, lr_sin, rope_dim = _setup(wl)
+    g = _cuda(inp)
+    common = (cos_sin.cuda(), lr_cos.cuda(), lr_sin.cuda(), rope_dim, g["norm_wq"], g["norm_wk"], g["proj_q"],
+              g["proj_k"], g["gate_w"], g["gate_b"])
+    xs = [g["x"] * s for s in (1.0, 0.5, -1.0, 2.0)]
+    refs = [ops.rola_forward_capi(x, g["w_qkv"], None, *common, wl.H, wl.topk).cpu() for x in xs]
+    pipe = ops.ForwardPipeline(xs[0].numel() * 2, xs[0].numel() * 2)
+    hosts = [x.cpu().pin_memory() for x in xs]
+    outs = [torch.empty(x.shape, dtype=torch.bfloat16).pin_memory() for x in xs]
+    for xh, oh in zip(hosts, outs):
+        pipe.forward(xh, oh, g["w_qkv"], None, *common, wl.H, wl.topk)
+    pipe.wait()
+    torch.cuda.synchronize()
+    pipe.close()
+    assert _lib.device_status() == 0
+    for i, (o, r) in enumerate(zip(outs, refs)):
+        assert torch.equal(o, r), f"step {i} differs"
