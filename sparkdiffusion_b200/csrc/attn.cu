@@ -302,9 +302,14 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           for (int c = 0; c < 128; ++c)
             if (c >= valid) v[c] = __float_as_uint(-INFINITY);
         }
-        float mx = -INFINITY;
+        // row max as a tree of 8 independent chains
+        float mx8[8];
 #pragma unroll
-        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(v[c]));
+        for (int c = 0; c < 8; ++c) mx8[c] = __uint_as_float(v[c]);
+#pragma unroll
+        for (int c = 8; c < 128; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(v[c]));
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         const float m_new = fmaxf(m_run, mx * scale);
         float m_use = m_run, alpha = 1.f;
         bool rescale = false;
@@ -315,8 +320,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           alpha = ex2_approx(m_run - m_new);
           rescale = true;
         }
-        // P = exp2(s*scale - m), packed bf16 over the S columns (already in registers)
-        float rs = 0.f;
+        // P = exp2(s*scale - m), packed bf16 over the S columns (already in registers);
+        // the row sum in four independent partial sums (short dependency chains)
+        float rsum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t w[16];
@@ -324,7 +330,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           for (int e = 0; e < 16; ++e) {
             const float p0 = ex2_approx(fmaf(__uint_as_float(v[32 * c + 2 * e]), scale, -m_use));
             const float p1 = ex2_approx(fmaf(__uint_as_float(v[32 * c + 2 * e + 1]), scale, -m_use));
-            rs += p0 + p1;
+            rsum[e & 3] += p0 + p1;
             w[e] = pack_bf2(p0, p1);
           }
           tmem_st16(tS + c * 16, w);
@@ -341,6 +347,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           for (int c = 0; c < 4; ++c) tmem_st32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[c * 32]));
         }
         tmem_st_wait();
+        const float rs = (rsum[0] + rsum[1]) + (rsum[2] + rsum[3]);
         l_run = l_run * alpha + rs;
         m_run = m_use;
         tc_fence_before();

@@ -12,6 +12,12 @@
 #include "common.cuh"
 #include "kernels.h"
 
+// log2 growth of a row's running max that triggers the O rescale in the
+// attention kernel; 0 rescales on every growth (the reference's recurrence)
+#ifndef ROLA_RESCALE_THRESHOLD
+#define ROLA_RESCALE_THRESHOLD 0.0f
+#endif
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -529,7 +535,7 @@ static int sparse_attn_impl(const void* q, const void* k, int64_t qk_sB, int64_t
   p.has_lowrank = q_lr != nullptr;
   p.qk_scale = (float)(0.08838834764831845 * 1.4426950408889634);  // 128^-0.5 * log2(e)
   p.eps_lr = eps_lr;
-  p.rescale_threshold = 0.0f;
+  p.rescale_threshold = ROLA_RESCALE_THRESHOLD;
   if (peer) {
     p.peer_n = peer->world;
     p.peer_Ls = L / peer->world;

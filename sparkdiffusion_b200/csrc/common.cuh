@@ -276,6 +276,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(
