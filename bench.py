@@ -43,7 +43,11 @@ METRIC = "RoLa attn ms/layer & effective TFLOP/s (selected blocks), Wan14B 720P,
 UNIT = "TFLOP/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per launch from one ncu capture (profiles/); None until captured
-NCU_TRAFFIC_BYTES = {"gemm": None, "attn": None}
+# DRAM bytes (read + write) per launch of the two tensor-bound kernels, 1 GPU:
+# from one ncu capture at C3 (profiles/gemm_bf16_tcgen05_C3.md,
+# profiles/sparse_attn_tcgen05_C3.md) scaled to C4 by the rows processed
+# (75600 / 32760); C3 itself as captured.
+NCU_TRAFFIC_BYTES = {"C4": {"gemm": 8.9e9, "attn": 4.4e9}, "C3": {"gemm": 3.89e9, "attn": 1.92e9}}
 
 
 def parse_args():
@@ -417,7 +421,7 @@ def main():
     dominant = "gemm" if t_gemm >= t_attn else "attn"
 
     def roof(name, ach):
-        tr = NCU_TRAFFIC_BYTES.get(name)
+        tr = NCU_TRAFFIC_BYTES.get(args.workload, {}).get(name) if world == 1 else None
         return {"kernel": {"gemm": "gemm_bf16_tcgen05", "attn": "sparse_attn_tcgen05"}[name], "bound": "tensor",
                 "achieved": ach, "peak": peak_sust, "unit": "TFLOP/s", "frac": ach / peak_sust,
                 "peak_kind": f"{peak_kind} bf16 sustained", "traffic": tr,

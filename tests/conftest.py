@@ -31,7 +31,7 @@ def rel_err(got: torch.Tensor, ref: torch.Tensor):
     return (d.max() / rms).item(), (d.mean() / rms).item()
 
 
-# BASELINE.json tolerance for bf16 outputs: max-abs <= 2e-2 and mean-abs <= 2e-3 of the output RMS
+# The tolerance for bf16 outputs: max-abs <= 2e-2 and mean-abs <= 2e-3 of the output RMS
 BF16_MAX = 2e-2
 BF16_MEAN = 2e-3
 

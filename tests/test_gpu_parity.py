@@ -2,7 +2,7 @@
 
 Selection (pooled means, smooth-K centre, scores, LUT) is checked bit for bit
 against the oracle run on the bf16 q/k the GPU produced; floating-point
-outputs are checked against the BASELINE tolerance (max-abs <= 2e-2 and
+outputs are checked against the bf16 tolerance (max-abs <= 2e-2 and
 mean-abs <= 2e-3 of the output RMS).  Shapes are reduced (2-4 heads, a few
 hundred to ~1.2k tokens, ragged tail blocks) so the oracle runs in seconds.
 """
@@ -222,7 +222,7 @@ def test_full_layer_from_x():
                                       blkk=wl.blk, topk=wl.topk, lut=ex["lut"].cpu(), out_dtype=torch.float32)
     # end to end from x: the GEMM outputs already differ from the oracle's by bf16
     # rounding flips, which the rest of the layer propagates; the mean-abs bound
-    # is the BASELINE one, the max-abs bound allows those propagated flips.
+    # is the stated one, the max-abs bound allows those propagated flips.
     assert_bf16_close(out.cpu(), ref2["out"], "out (GPU LUT)", max_tol=6e-2)
 
 

@@ -16,7 +16,7 @@ from sparkdiffusion_b200 import rope as host_rope
 from sparkdiffusion_b200.workloads import C1, make_inputs
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-FP32_TOL = 1e-4  # BASELINE: fp32 on the CPU configuration within 1e-4 (relative to the RMS)
+FP32_TOL = 1e-4  # fp32 on the CPU configuration within 1e-4 (relative to the RMS)
 
 
 @pytest.fixture(scope="module")
