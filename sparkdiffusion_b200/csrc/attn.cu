@@ -302,12 +302,16 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           for (int c = 0; c < 128; ++c)
             if (c >= valid) v[c] = __float_as_uint(-INFINITY);
         }
-        // row max as a tree of 8 independent chains
+        // row max: 8 independent chains of three-input maxima
         float mx8[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) mx8[c] = __uint_as_float(v[c]);
+        for (int k = 0; k < 8; ++k) {
+          mx8[k] = __uint_as_float(v[k]);
 #pragma unroll
-        for (int c = 8; c < 128; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(v[c]));
+          for (int j = 0; j < 7; ++j)
+            mx8[k] = max3f(mx8[k], __uint_as_float(v[k + 8 + 16 * j]), __uint_as_float(v[k + 16 + 16 * j]));
+          mx8[k] = fmaxf(mx8[k], __uint_as_float(v[k + 120]));
+        }
         const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         const float m_new = fmaxf(m_run, mx * scale);
@@ -320,17 +324,23 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           alpha = ex2_approx(m_run - m_new);
           rescale = true;
         }
-        // P = exp2(s*scale - m), packed bf16 over the S columns (already in registers);
-        // the row sum in four independent partial sums (short dependency chains)
-        float rsum[4] = {0.f, 0.f, 0.f, 0.f};
+        // P = exp2(s*scale - m), packed bf16 over the S columns (already in registers).
+        // s*scale - m and the row sums run as packed fp32x2 operations (two
+        // columns per instruction), the row sum in two independent pairs.
+        const uint64_t sc2 = f2_pack(scale, scale), nm2 = f2_pack(-m_use, -m_use);
+        uint64_t rs2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t w[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const float p0 = ex2_approx(fmaf(__uint_as_float(v[32 * c + 2 * e]), scale, -m_use));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(v[32 * c + 2 * e + 1]), scale, -m_use));
-            rsum[e & 3] += p0 + p1;
+            float x0, x1;
+            f2_unpack(fma_f32x2(f2_pack(__uint_as_float(v[32 * c + 2 * e]), __uint_as_float(v[32 * c + 2 * e + 1])),
+                                sc2, nm2),
+                      x0, x1);
+            const float p0 = ex2_approx(x0);
+            const float p1 = ex2_approx(x1);
+            rs2[e & 1] = add_f32x2(rs2[e & 1], f2_pack(p0, p1));
             w[e] = pack_bf2(p0, p1);
           }
           tmem_st16(tS + c * 16, w);
@@ -341,13 +351,22 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
 #pragma unroll
           for (int c = 0; c < 4; ++c) tmem_ld32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[c * 32]));
           tmem_ld_wait();
+          const uint64_t a2 = f2_pack(alpha, alpha);
 #pragma unroll
-          for (int e = 0; e < 128; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          for (int e = 0; e < 64; ++e) {
+            float o0, o1;
+            f2_unpack(mul_f32x2(f2_pack(__uint_as_float(ov[2 * e]), __uint_as_float(ov[2 * e + 1])), a2), o0, o1);
+            ov[2 * e] = __float_as_uint(o0);
+            ov[2 * e + 1] = __float_as_uint(o1);
+          }
 #pragma unroll
           for (int c = 0; c < 4; ++c) tmem_st32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[c * 32]));
         }
         tmem_st_wait();
-        const float rs = (rsum[0] + rsum[1]) + (rsum[2] + rsum[3]);
+        float rsa, rsb, rsc, rsd;
+        f2_unpack(rs2[0], rsa, rsb);
+        f2_unpack(rs2[1], rsc, rsd);
+        const float rs = (rsa + rsc) + (rsb + rsd);
         l_run = l_run * alpha + rs;
         m_run = m_use;
         tc_fence_before();
@@ -370,9 +389,12 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       if (ok) {
         const int tok = (m0 + t) * 128 + row;
         const float inv_l = 1.0f / l_run;
-        // pass 1: row statistics of o_sparse (bf16 chain) and of o_lr (16-column chunks)
+        // one pass over TMEM: the row's o_sparse and o_lr values, rounded to
+        // bf16 as the reference materialises them, stay in registers as packed
+        // pairs (64 + 64) for the statistics and the fused output
+        uint32_t osp[64], lrp[64];
         float ss_os = 0.f, ss_lr = 0.f;
-#pragma unroll 1
+#pragma unroll
         for (int c = 0; c < 8; ++c) {
           uint32_t ov[16];
           tmem_ld16(tO + c * 16, ov);
@@ -380,12 +402,23 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           if (lowrank) tmem_ld16(tS + c * 16, lv);
           tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float os = rbf(__uint_as_float(ov[e]) * inv_l);
-            ss_os += rbf(os * os);
+          for (int e = 0; e < 8; ++e) {
+            // each bf16 rounding of a column pair is one packed conversion
+            const uint32_t op = pack_bf2(__uint_as_float(ov[2 * e]) * inv_l, __uint_as_float(ov[2 * e + 1]) * inv_l);
+            osp[8 * c + e] = op;
+            float o0, o1;
+            unpack_bf2(op, o0, o1);
+            float q0 = o0 * o0, q1 = o1 * o1;
+            rbf2(q0, q1);
+            ss_os += q0;
+            ss_os += q1;
             if (lowrank) {
-              const float lr = rbf(__uint_as_float(lv[e]));
-              ss_lr = fmaf(lr, lr, ss_lr);
+              const uint32_t lp = pack_bf2(__uint_as_float(lv[2 * e]), __uint_as_float(lv[2 * e + 1]));
+              lrp[8 * c + e] = lp;
+              float l0, l1;
+              unpack_bf2(lp, l0, l1);
+              ss_lr = fmaf(l0, l0, ss_lr);
+              ss_lr = fmaf(l1, l1, ss_lr);
             }
           }
         }
@@ -426,29 +459,28 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             gate = bf2f(p.gate[((int64_t)b * p.L + tok) * p.H + h]);
           }
         }
-        // pass 2: fuse (TMEM loads by the whole warp).  The fused row goes to
-        // the staging tile (stored out coalesced below); o_sparse directly.
+        // fuse from registers (os / os_rms as a product with the row's
+        // reciprocal: one division per row instead of one per element); the
+        // fused row goes to the staging tile (stored out coalesced below),
+        // o_sparse directly
+        const float inv_rms = 1.0f / os_rms;
         const bool store = tok < p.L;
         const int64_t orow = (int64_t)b * p.o_sB + (int64_t)h * p.o_sH + (int64_t)tok * p.o_sT;
-#pragma unroll 1
+#pragma unroll
         for (int c = 0; c < 8; ++c) {
-          uint32_t ov[16];
-          tmem_ld16(tO + c * 16, ov);
-          uint32_t lv[16];
-          if (lowrank) tmem_ld16(tS + c * 16, lv);
-          tmem_ld_wait();
-          uint32_t wo[8], ws[8];
+          uint32_t wo[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            float os0 = rbf(__uint_as_float(ov[2 * e]) * inv_l);
-            float os1 = rbf(__uint_as_float(ov[2 * e + 1]) * inv_l);
-            ws[e] = pack_bf2(os0, os1);
             if (lowrank) {
-              const float l0 = rbf(rbf(__uint_as_float(lv[2 * e])) * lr_scale);
-              const float l1 = rbf(rbf(__uint_as_float(lv[2 * e + 1])) * lr_scale);
-              wo[e] = pack_bf2((os0 / os_rms + gate * l0) * os_rms, (os1 / os_rms + gate * l1) * os_rms);
+              float os0, os1, l0, l1;
+              unpack_bf2(osp[8 * c + e], os0, os1);
+              unpack_bf2(lrp[8 * c + e], l0, l1);
+              l0 *= lr_scale;
+              l1 *= lr_scale;
+              rbf2(l0, l1);
+              wo[e] = pack_bf2((os0 * inv_rms + gate * l0) * os_rms, (os1 * inv_rms + gate * l1) * os_rms);
             } else {
-              wo[e] = ws[e];
+              wo[e] = osp[8 * c + e];
             }
           }
           if (staged) {
@@ -459,8 +491,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           }
           if (p.o_sparse && store) {
             uint4* dst = reinterpret_cast<uint4*>(p.o_sparse + orow + c * 16);
-            dst[0] = make_uint4(ws[0], ws[1], ws[2], ws[3]);
-            dst[1] = make_uint4(ws[4], ws[5], ws[6], ws[7]);
+            dst[0] = make_uint4(osp[8 * c + 0], osp[8 * c + 1], osp[8 * c + 2], osp[8 * c + 3]);
+            dst[1] = make_uint4(osp[8 * c + 4], osp[8 * c + 5], osp[8 * c + 6], osp[8 * c + 7]);
           }
         }
       }

@@ -195,6 +195,7 @@ int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw,
   ROLA_CHECK(ld_raw % 8 == 0 && aligned16(q_raw) && aligned16(k_raw), "qk_norm_rope: 16-byte aligned rows required");
   ROLA_CHECK((pooled_q == nullptr) == (ksum == nullptr), "qk_norm_rope: pooled_q and ksum go together");
   ROLA_CHECK(x == nullptr || (gate_w && gate_b && gate_out), "qk_norm_rope: the gate needs gate_w, gate_b, gate_out");
+  ROLA_CHECK(x == nullptr || (aligned16(x) && aligned16(gate_w)), "qk_norm_rope: x and gate_w must be 16-byte aligned");
   ROLA_CHECK(ssq == nullptr || (H % 2 == 0 && ssq_ld >= H),
              "qk_norm_rope: sums of squares need an even head count and ssq_ld >= H");
   NormRopeParams p{};
@@ -237,6 +238,7 @@ int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_r
              "qk_norm_pack: bad sizes (at most 8 head chunks)");
   ROLA_CHECK(ld_raw % 8 == 0, "qk_norm_pack: 16-byte aligned rows required");
   ROLA_CHECK(x == nullptr || (gate_w && gate_b && gate_out), "qk_norm_pack: the gate needs gate_w, gate_b, gate_out");
+  ROLA_CHECK(x == nullptr || (aligned16(x) && aligned16(gate_w)), "qk_norm_pack: x and gate_w must be 16-byte aligned");
   ROLA_CHECK(ssq == nullptr || (H % 2 == 0 && ssq_ld >= H), "qk_norm_pack: sums of squares need an even head count");
   NormRopeParams p{};
   p.q_in = BF(q_raw);
@@ -278,7 +280,7 @@ static int scatter_params(const rola_scatter_args* a, bool compact, NormRopePara
   ROLA_CHECK(a->dst_row0 >= 0 && a->dst_row0 + a->L <= a->dst_rows && a->dst_rows < (1ll << 31),
              "%s: rows [dst_row0, dst_row0 + L) outside the destination", what);
   ROLA_CHECK(a->ld_raw % 8 == 0 && aligned16(a->q_raw) && aligned16(a->k_raw) && aligned16(a->v_raw) &&
-                 aligned16(a->x),
+                 aligned16(a->x) && aligned16(a->gate_w),
              "%s: 16-byte aligned rows required", what);
   ROLA_CHECK(a->ssq == nullptr || (a->H % 2 == 0 && a->ssq_ld >= a->H),
              "%s: sums of squares need an even head count", what);
@@ -637,9 +639,9 @@ int rola_b200_rola_forward(const void* x, const void* w_qkv, const void* b_qkv, 
   float* ssq = reinterpret_cast<float*>(ws + f.ssq);
   const int ssq_ld = (int)(3 * dim / 256);
   ROLA_TRY(rola_b200_qkv_gemm(x, w_qkv, b_qkv, qkv, ssq, M, 3 * dim, dim, stream));
-  ROLA_TRY(rola_b200_qk_norm_rope(qkv, qkv + dim, 3 * dim, ssq, ssq_ld, nullptr, norm_wq, norm_wk, cos_sin, nullptr,
-                                  nullptr, B, L, H, blk, eps, ws + f.q_rope, ws + f.k_rope, ws + f.q_normed,
-                                  ws + f.k_normed, nullptr, ws + f.pooled_q, reinterpret_cast<float*>(ws + f.ksum),
+  ROLA_TRY(rola_b200_qk_norm_rope(qkv, qkv + dim, 3 * dim, ssq, ssq_ld, x, norm_wq, norm_wk, cos_sin, gate_w,
+                                  gate_b, B, L, H, blk, eps, ws + f.q_rope, ws + f.k_rope, ws + f.q_normed,
+                                  ws + f.k_normed, ws + f.gate, ws + f.pooled_q, reinterpret_cast<float*>(ws + f.ksum),
                                   stream));
   ROLA_TRY(rola_b200_center_from_sums(reinterpret_cast<float*>(ws + f.ksum), B, NB, (int)dim, L, ws + f.center,
                                       stream));
@@ -654,8 +656,8 @@ int rola_b200_rola_forward(const void* x, const void* w_qkv, const void* b_qkv, 
   ROLA_TRY(rola_b200_lowrank_q(ws + f.q_normed, Ld, 128, dim, proj_q, lr_cos, lr_sin, rope_dim, B, L, H, R,
                                ws + f.q_lr, stream));
   return rola_b200_sparse_attn(ws + f.q_rope, ws + f.k_rope, Ld, 128, dim, qkv + 2 * dim, 3 * Ld, 128, 3 * dim, lut,
-                               B, L, H, blk, topk, ws + f.q_lr, ws + f.ct, nullptr, x, Ld, 128, dim, gate_w, gate_b,
-                               0.0078125f, out, nullptr, Ld, 128, dim, stream);
+                               B, L, H, blk, topk, ws + f.q_lr, ws + f.ct, ws + f.gate, nullptr, 0, 0, 0, nullptr,
+                               nullptr, 0.0078125f, out, nullptr, Ld, 128, dim, stream);
 }
 
 }  // extern "C"

@@ -51,6 +51,9 @@ __device__ __forceinline__ void unpack_bf2(uint32_t u, float& lo, float& hi) {
   lo = __uint_as_float(u << 16);
   hi = __uint_as_float(u & 0xffff0000u);
 }
+// rbf of two values with one conversion instruction (the conversions run on
+// the MUFU/XU pipe, a quarter of the FMA pipe's rate; pairing halves them)
+__device__ __forceinline__ void rbf2(float& a, float& b) { unpack_bf2(pack_bf2(a, b), a, b); }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -276,6 +279,37 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+
+// Packed fp32x2 arithmetic of sm_100 (one instruction for two IEEE fp32
+// operations, each rounded to nearest) and the three-input fp32 max.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;

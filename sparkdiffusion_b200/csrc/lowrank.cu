@@ -96,12 +96,17 @@ __device__ __forceinline__ float2 rope_cs(const LowrankParams& p, int t, int pai
 
 // SiLU + rank-RoPE on one (even, odd) rank pair; returns packed bf16x2
 __device__ __forceinline__ uint32_t silu_rope_pair(float l0, float l1, float2 cs, bool rotate) {
-  float e = rbf(l0), o = rbf(l1);                       // bf16 linear output (fused_lowrank.py:97)
-  e = rbf(e * __fdividef(1.0f, 1.0f + __expf(-e)));     // silu in fp32, then bf16 (:99-102)
-  o = rbf(o * __fdividef(1.0f, 1.0f + __expf(-o)));
+  // every bf16 rounding of the pair is one packed conversion (rbf2)
+  float e = l0, o = l1;
+  rbf2(e, o);                                           // bf16 linear output (fused_lowrank.py:97)
+  e = e * __fdividef(1.0f, 1.0f + __expf(-e));          // silu in fp32, then bf16 (:99-102)
+  o = o * __fdividef(1.0f, 1.0f + __expf(-o));
   if (rotate) {                                         // rotated pairs (:104-135)
+    rbf2(e, o);
     const float c = cs.x, s = cs.y;
-    const float ec = rbf(e * c), os = rbf(o * s), es = rbf(e * s), oc = rbf(o * c);
+    float ec = e * c, os = o * s, es = e * s, oc = o * c;
+    rbf2(ec, os);
+    rbf2(es, oc);
     return pack_bf2(ec - os, es + oc);
   }
   return pack_bf2(e, o);

@@ -164,32 +164,47 @@ __device__ __forceinline__ void norm_block(const NormRopeParams& p, int m, int g
     if (has_v) *reinterpret_cast<uint4*>(chunk_dst(p.v_dst, p, b, t, col)) = vraw;
     if (NORM) {
       const float rq = s_rstd[tl], rk = s_rstd[p.blk + tl];
+      // unit in bf16, then x weight in bf16; every bf16 rounding of a column
+      // pair is one packed conversion, and the packed words are what is stored
+      uint4 qn, kn;
+      uint32_t* qw = reinterpret_cast<uint32_t*>(&qn);
+      uint32_t* kw = reinterpret_cast<uint32_t*>(&kn);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        q[i] = rbf(rbf(q[i] * rq) * wq[i]);  // unit in bf16, then x weight in bf16
-        k[i] = rbf(rbf(k[i] * rk) * wk[i]);
+      for (int i = 0; i < 4; ++i) {
+        float a0 = q[2 * i] * rq, a1 = q[2 * i + 1] * rq;
+        float b0 = k[2 * i] * rk, b1 = k[2 * i + 1] * rk;
+        rbf2(a0, a1);
+        rbf2(b0, b1);
+        qw[i] = pack_bf2(a0 * wq[2 * i], a1 * wq[2 * i + 1]);
+        kw[i] = pack_bf2(b0 * wk[2 * i], b1 * wk[2 * i + 1]);
+        unpack_bf2(qw[i], q[2 * i], q[2 * i + 1]);
+        unpack_bf2(kw[i], k[2 * i], k[2 * i + 1]);
       }
-      if (p.qn_dst[0]) store8(chunk_dst(p.qn_dst, p, b, t, col), q);
-      if (p.kn_dst[0]) store8(chunk_dst(p.kn_dst, p, b, t, col), k);
+      if (p.qn_dst[0]) *reinterpret_cast<uint4*>(chunk_dst(p.qn_dst, p, b, t, col)) = qn;
+      if (p.kn_dst[0]) *reinterpret_cast<uint4*>(chunk_dst(p.kn_dst, p, b, t, col)) = kn;
     }
     if (ROPE) {
       const float4* cs = reinterpret_cast<const float4*>(p.cos_sin + (int64_t)t * 128 + d0);
       float qr[8], kr[8];
+      uint4 qrp, krp;
+      uint32_t* qrw = reinterpret_cast<uint32_t*>(&qrp);
+      uint32_t* krw = reinterpret_cast<uint32_t*>(&krp);
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         float4 c = cs[i];  // cos_a, sin_a, cos_b, sin_b
         const int e0 = 4 * i, e1 = 4 * i + 2;
-        qr[e0] = rbf(q[e0] * c.x - q[e0 + 1] * c.y);
-        qr[e0 + 1] = rbf(q[e0] * c.y + q[e0 + 1] * c.x);
-        qr[e1] = rbf(q[e1] * c.z - q[e1 + 1] * c.w);
-        qr[e1 + 1] = rbf(q[e1] * c.w + q[e1 + 1] * c.z);
-        kr[e0] = rbf(k[e0] * c.x - k[e0 + 1] * c.y);
-        kr[e0 + 1] = rbf(k[e0] * c.y + k[e0 + 1] * c.x);
-        kr[e1] = rbf(k[e1] * c.z - k[e1 + 1] * c.w);
-        kr[e1 + 1] = rbf(k[e1] * c.w + k[e1 + 1] * c.z);
+        qrw[2 * i] = pack_bf2(q[e0] * c.x - q[e0 + 1] * c.y, q[e0] * c.y + q[e0 + 1] * c.x);
+        qrw[2 * i + 1] = pack_bf2(q[e1] * c.z - q[e1 + 1] * c.w, q[e1] * c.w + q[e1 + 1] * c.z);
+        krw[2 * i] = pack_bf2(k[e0] * c.x - k[e0 + 1] * c.y, k[e0] * c.y + k[e0 + 1] * c.x);
+        krw[2 * i + 1] = pack_bf2(k[e1] * c.z - k[e1 + 1] * c.w, k[e1] * c.w + k[e1 + 1] * c.z);
       }
-      if (p.q_rope) store8(p.q_rope + row * dim + col, qr);
-      if (p.k_rope) store8(p.k_rope + row * dim + col, kr);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        unpack_bf2(qrw[i], qr[2 * i], qr[2 * i + 1]);
+        unpack_bf2(krw[i], kr[2 * i], kr[2 * i + 1]);
+      }
+      if (p.q_rope) *reinterpret_cast<uint4*>(p.q_rope + row * dim + col) = qrp;
+      if (p.k_rope) *reinterpret_cast<uint4*>(p.k_rope + row * dim + col) = krp;
       if (POOL) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {

@@ -214,17 +214,19 @@ def rola_attention_from_qkv(q_raw, k_raw, v_raw, x, cos_sin, lr_cos, lr_sin, rop
     cos_sin = cos_sin.to(torch.float32).contiguous()
     xc = x.contiguous()
     ssq_ld = 0 if ssq is None else ssq.shape[-1]
-    _lib.call("rola_b200_qk_norm_rope", _ptr(q_raw), _ptr(k_raw), q_raw.stride(1), _ptr(ssq), ssq_ld, None,
-              _ptr(nwq), _ptr(nwk), _ptr(cos_sin), None, None, B, L, H, blk, eps, _ptr(q_rope),
-              _ptr(k_rope), _ptr(q_normed), _ptr(k_normed), None, _ptr(pooled_q), _ptr(ksum), st)
-    res = head_local_attention(q_rope, k_rope, q_normed, k_normed, v_raw, None, pooled_q, ksum, lr_cos, lr_sin,
-                               rope_dim, proj_q, proj_k, H, blk, topk, splits, keep, lut, events, x=xc,
-                               gate_w=gate_w, gate_b=gate_b)
+    # the gate values come out of the same streaming pass (it reads x beside q and k)
+    gate = e(B, L, H)
+    _lib.call("rola_b200_qk_norm_rope", _ptr(q_raw), _ptr(k_raw), q_raw.stride(1), _ptr(ssq), ssq_ld, _ptr(xc),
+              _ptr(nwq), _ptr(nwk), _ptr(cos_sin), _ptr(_bf16_vec(gate_w, HEAD_DIM, "gate_w")),
+              _ptr(_bf16_vec(gate_b, H, "gate_b")), B, L, H, blk, eps, _ptr(q_rope), _ptr(k_rope), _ptr(q_normed),
+              _ptr(k_normed), _ptr(gate), _ptr(pooled_q), _ptr(ksum), st)
+    res = head_local_attention(q_rope, k_rope, q_normed, k_normed, v_raw, gate, pooled_q, ksum, lr_cos, lr_sin,
+                               rope_dim, proj_q, proj_k, H, blk, topk, splits, keep, lut, events)
     if not keep:
         return res
     out, extra = res
     extra.update(q_rope=q_rope, k_rope=k_rope, q_normed=q_normed, k_normed=k_normed, pooled_q=pooled_q, ksum=ksum,
-                 v=v_raw)
+                 v=v_raw, gate=gate)
     return out, extra
 
 
