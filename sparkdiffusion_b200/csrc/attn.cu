@@ -11,24 +11,27 @@
 //
 // One CTA per (pair of query blocks, batch*head): the two 128-row tiles A and
 // B have their own LUT rows and run ping-pong, so the tensor core executes one
-// tile's MMAs while the other tile's softmax runs.  Three warpgroups with
-// registers rebalanced by setmaxnreg (launch: 384 threads x 168):
+// tile's MMAs while the other tile's softmax runs.  Four warpgroups with
+// registers rebalanced by setmaxnreg (launch: 512 threads x 128):
 //   WG0 (56 regs)   warp 0 lane 0: TMA producer.  Q of both tiles once, then
 //                   the K and V blocks of both LUTs through one 5-slot ring in
 //                   exactly the order the MMAs consume them (K_A0 K_B0 | V_A0
 //                   K_A1 V_B0 K_B1 | ...), then the epilogue operands (q_lr
-//                   tiles and C^T, and the hidden-state tiles from which the
-//                   epilogue computes the gate).  No multicast.
+//                   tiles and C^T, and the hidden-state tiles when the gate is
+//                   computed from x).  No multicast.
 //                   warp 1: TMEM owner and MMA issuer (one elected thread):
 //                   S = Q K^T (smem x smem) and O += P V with P read from TMEM
 //                   (tcgen05.mma with the A operand in tensor memory).
-//   WG1, WG2 (224)  softmax of tile A / tile B: thread = query row = TMEM lane.
+//   WG1, WG2 (176)  softmax of tile A / tile B: thread = query row = TMEM lane.
 //                   Per KV block the whole S row is loaded at once, the row max
-//                   taken, P = exp2(s*scale - m) written back over the S
-//                   columns as packed bf16, and O rescaled in TMEM when the
-//                   running max grew by more than `rescale_threshold` (0 = every
-//                   growth: the reference's recurrence exactly); then the
-//                   fused epilogue.
+//                   taken, the row's O rescale factor published, and
+//                   P = exp2(s*scale - m) written back over the S columns as
+//                   packed bf16; then the fused epilogue.
+//   WG3 (96)        correction: rescales O in TMEM by the published factors
+//                   while the softmax computes P (every growth of the running
+//                   max when `rescale_threshold` is 0: the reference's
+//                   recurrence exactly); the MMA issuer waits for P and the
+//                   corrected O before P V.
 // TMEM columns: S/P of tile t at [128 t, 128 t + 128), O of tile t at
 // [256 + 128 t, ...); the epilogue's o_lr reuses the S columns.
 #include "common.cuh"
@@ -37,17 +40,19 @@
 namespace rola {
 
 namespace attn {
-constexpr int THREADS = 384;
-constexpr int LAUNCH_REGS = 168;            // 65536 / 384, rounded down to 8
-constexpr int REGS_LOAD = 56, REGS_SOFTMAX = 224;
-static_assert(128 * REGS_LOAD + 2 * 128 * REGS_SOFTMAX <= THREADS * LAUNCH_REGS, "register split exceeds the pool");
+constexpr int THREADS = 512;
+constexpr int LAUNCH_REGS = 128;            // 65536 / 512
+constexpr int REGS_LOAD = 56, REGS_CORR = 96, REGS_SOFTMAX = 176;
+static_assert(128 * REGS_LOAD + 128 * REGS_CORR + 2 * 128 * REGS_SOFTMAX <= THREADS * LAUNCH_REGS,
+              "register split exceeds the pool");
 constexpr int TILE = 16384;                 // one [128 rows x 64 bf16] box, 128B swizzle
 constexpr int SLOT = 2 * TILE;              // one 128x128 K or V block
 constexpr int NSLOTS = 5;
 constexpr int OFF_Q = 0;                    // 2 tiles x 2 boxes
 constexpr int OFF_RING = 4 * TILE;          // 5 slots
 constexpr int OFF_BAR = OFF_RING + NSLOTS * SLOT;  // 224 KB
-constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr int OFF_ALPHA = OFF_BAR + 256;    // per-row O rescale factors of both tiles [2][128] fp32
+constexpr int SMEM_BYTES = OFF_ALPHA + 1024 + 1024;
 }  // namespace attn
 
 // barrier slots
@@ -59,6 +64,8 @@ enum : int {
   B_PF0, B_PF1,                  // P of tile t in TMEM and O rescaled (softmax -> MMA), 4 arrivals
   B_OF0, B_OF1,                  // last P V of tile t complete
   B_LR0, B_LR1,                  // o_lr of tile t in TMEM
+  B_AR0, B_AR1,                  // rescale factors of tile t published (softmax -> correction), 4 arrivals
+  B_OC0, B_OC1,                  // O of tile t rescaled (correction -> MMA), 4 arrivals
   B_DRAIN,
   B_COUNT
 };
@@ -105,6 +112,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       mbar_init(bar(B_PF0 + t), 4);
       mbar_init(bar(B_OF0 + t), 1);
       mbar_init(bar(B_LR0 + t), 1);
+      mbar_init(bar(B_AR0 + t), 4);
+      mbar_init(bar(B_OC0 + t), 4);
     }
     mbar_init(bar(B_DRAIN), 1);
     *abort_flag = 0;
@@ -230,7 +239,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       for (int t = 0; t < nt && ok; ++t) issue_s(t);
       for (int i = 0; i < topk && ok; ++i) {
         for (int t = 0; t < nt && ok; ++t) {
-          if (!mbar_wait(bar(B_PF0 + t), i & 1, abort_flag, kDevTimeoutSoftmax)) {
+          if (!mbar_wait(bar(B_PF0 + t), i & 1, abort_flag, kDevTimeoutSoftmax) ||
+              !mbar_wait(bar(B_OC0 + t), i & 1, abort_flag, kDevTimeoutSoftmax)) {
             ok = false;
             break;
           }
@@ -270,6 +280,51 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       mbar_wait(bar(B_DRAIN), 0, abort_flag, kDevTimeoutMma);
     }
   }
+  } else if (warp >= 12) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_CORR));
+    // ------------------------------------------------------------ correction
+    // O rescale of both tiles, off the softmax's critical path: once a tile's
+    // softmax has published the row factors of block i (right after the row
+    // max), scale its O in TMEM while that softmax computes P.  O is stable:
+    // the last P V of the tile completed before its S of block i.
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const float* s_alpha = reinterpret_cast<const float*>(gbase + OFF_ALPHA);
+    bool ok = true;
+    for (int i = 0; i < topk && ok; ++i) {
+      for (int t = 0; t < nt && ok; ++t) {
+        if (!__all_sync(0xffffffffu, mbar_wait(bar(B_AR0 + t), i & 1, abort_flag, kDevTimeoutSoftmax))) {
+          ok = false;
+          break;
+        }
+        const float alpha = s_alpha[t * 128 + row];
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+          tc_fence_after();
+          const uint32_t tO = tmem + 256 + 128 * t + ((uint32_t)(q * 32) << 16);
+          const uint64_t a2 = f2_pack(alpha, alpha);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            uint32_t ov[64];
+            tmem_ld32(tO + h2 * 64, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
+            tmem_ld32(tO + h2 * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              float o0, o1;
+              f2_unpack(mul_f32x2(f2_pack(__uint_as_float(ov[2 * e]), __uint_as_float(ov[2 * e + 1])), a2), o0, o1);
+              ov[2 * e] = __float_as_uint(o0);
+              ov[2 * e + 1] = __float_as_uint(o1);
+            }
+            tmem_st32(tO + h2 * 64, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
+            tmem_st32(tO + h2 * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
+          }
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_OC0 + t));
+      }
+    }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_SOFTMAX));
     // -------------------------------------------------------------- softmax
@@ -324,6 +379,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           alpha = ex2_approx(m_run - m_new);
           rescale = true;
         }
+        // publish this row's O rescale factor to the correction warpgroup
+        reinterpret_cast<float*>(gbase + OFF_ALPHA)[t * 128 + row] = rescale ? alpha : 1.0f;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(B_AR0 + t));
         // P = exp2(s*scale - m), packed bf16 over the S columns (already in registers).
         // s*scale - m and the row sums run as packed fp32x2 operations (two
         // columns per instruction), the row sum in two independent pairs.
@@ -344,23 +403,6 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             w[e] = pack_bf2(p0, p1);
           }
           tmem_st16(tS + c * 16, w);
-        }
-        // O of this tile is stable: its last P V completed before this S (in-order MMAs)
-        if (__any_sync(0xffffffffu, rescale)) {
-          uint32_t ov[128];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) tmem_ld32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[c * 32]));
-          tmem_ld_wait();
-          const uint64_t a2 = f2_pack(alpha, alpha);
-#pragma unroll
-          for (int e = 0; e < 64; ++e) {
-            float o0, o1;
-            f2_unpack(mul_f32x2(f2_pack(__uint_as_float(ov[2 * e]), __uint_as_float(ov[2 * e + 1])), a2), o0, o1);
-            ov[2 * e] = __float_as_uint(o0);
-            ov[2 * e + 1] = __float_as_uint(o1);
-          }
-#pragma unroll
-          for (int c = 0; c < 4; ++c) tmem_st32(tO + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[c * 32]));
         }
         tmem_st_wait();
         float rsa, rsb, rsc, rsd;
