@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/rola_b200.h"
@@ -105,6 +106,33 @@ int make_token_map(CUtensorMap* m, const void* ptr, int64_t cols, int64_t ld, in
 }
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Two side streams per device for the forward's independent branches (the
+// low-rank C^T and q_lr run beside the selection chain), with fork/join events.
+struct ForkJoin {
+  cudaStream_t side[2] = {nullptr, nullptr};
+  cudaEvent_t fork = nullptr, join[2] = {nullptr, nullptr};
+  std::mutex mu;
+};
+ForkJoin g_forkjoin[64];
+
+int forkjoin_get(ForkJoin** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) return fail(ROLA_ERR_CUDA, "rola_forward: no current device");
+  ForkJoin& f = g_forkjoin[dev];
+  std::lock_guard<std::mutex> lock(f.mu);
+  if (f.fork == nullptr) {
+    for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
+      e = cudaStreamCreateWithFlags(&f.side[i], cudaStreamNonBlocking);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&f.join[i], cudaEventDisableTiming);
+    }
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&f.fork, cudaEventDisableTiming);
+    if (e != cudaSuccess) return fail(ROLA_ERR_CUDA, "rola_forward: %s", cudaGetErrorString(e));
+  }
+  *out = &f;
+  return ROLA_OK;
+}
 
 }  // namespace
 
@@ -643,18 +671,31 @@ int rola_b200_rola_forward(const void* x, const void* w_qkv, const void* b_qkv, 
                                   gate_b, B, L, H, blk, eps, ws + f.q_rope, ws + f.k_rope, ws + f.q_normed,
                                   ws + f.k_normed, ws + f.gate, ws + f.pooled_q, reinterpret_cast<float*>(ws + f.ksum),
                                   stream));
+  // fork: the low-rank branches on two side streams, selection on `stream`
+  ForkJoin* fj = nullptr;
+  ROLA_TRY(forkjoin_get(&fj));
+  std::lock_guard<std::mutex> lock(fj->mu);
+  cudaError_t ce = cudaEventRecord(fj->fork, S(stream));
+  for (int i = 0; i < 2 && ce == cudaSuccess; ++i) ce = cudaStreamWaitEvent(fj->side[i], fj->fork, 0);
+  if (ce != cudaSuccess) return fail(ROLA_ERR_CUDA, "rola_forward: %s", cudaGetErrorString(ce));
+  const int64_t Ld = (int64_t)L * dim;
+  ROLA_TRY(rola_b200_lowrank_kv(ws + f.k_normed, Ld, 128, dim, qkv + 2 * dim, 3 * Ld, 128, 3 * dim, proj_k, lr_cos,
+                                lr_sin, rope_dim, B, L, H, R, splits, reinterpret_cast<float*>(ws + f.c_partial),
+                                nullptr, ws + f.ct, fj->side[0]));
+  ROLA_TRY(rola_b200_lowrank_q(ws + f.q_normed, Ld, 128, dim, proj_q, lr_cos, lr_sin, rope_dim, B, L, H, R,
+                               ws + f.q_lr, fj->side[1]));
   ROLA_TRY(rola_b200_center_from_sums(reinterpret_cast<float*>(ws + f.ksum), B, NB, (int)dim, L, ws + f.center,
                                       stream));
   ROLA_TRY(rola_b200_mean_pool(ws + f.k_rope, (int64_t)L * dim, 128, dim, B, H, L, blk, ws + f.center,
                                ws + f.pooled_k, stream));
   ROLA_TRY(rola_b200_block_select(ws + f.pooled_q, ws + f.pooled_k, B * H, NB, NB, topk,
                                   reinterpret_cast<float*>(ws + f.scores), lut, stream));
-  const int64_t Ld = (int64_t)L * dim;
-  ROLA_TRY(rola_b200_lowrank_kv(ws + f.k_normed, Ld, 128, dim, qkv + 2 * dim, 3 * Ld, 128, 3 * dim, proj_k, lr_cos,
-                                lr_sin, rope_dim, B, L, H, R, splits, reinterpret_cast<float*>(ws + f.c_partial),
-                                nullptr, ws + f.ct, stream));
-  ROLA_TRY(rola_b200_lowrank_q(ws + f.q_normed, Ld, 128, dim, proj_q, lr_cos, lr_sin, rope_dim, B, L, H, R,
-                               ws + f.q_lr, stream));
+  // join before the attention
+  for (int i = 0; i < 2 && ce == cudaSuccess; ++i) {
+    ce = cudaEventRecord(fj->join[i], fj->side[i]);
+    if (ce == cudaSuccess) ce = cudaStreamWaitEvent(S(stream), fj->join[i], 0);
+  }
+  if (ce != cudaSuccess) return fail(ROLA_ERR_CUDA, "rola_forward: %s", cudaGetErrorString(ce));
   return rola_b200_sparse_attn(ws + f.q_rope, ws + f.k_rope, Ld, 128, dim, qkv + 2 * dim, 3 * Ld, 128, 3 * dim, lut,
                                B, L, H, blk, topk, ws + f.q_lr, ws + f.ct, ws + f.gate, nullptr, 0, 0, 0, nullptr,
                                nullptr, 0.0078125f, out, nullptr, Ld, 128, dim, stream);

@@ -8,8 +8,8 @@
 // `_gate_fusion_kernel` (ops/fused_kernel/fused_gate.py:97-114), in one pass
 // over the projected rows so that q and k are read from HBM once.
 //
-// Layout: one CTA per (128-token block m, batch b); thread j owns the 8 hidden
-// columns [8j, 8j+8) of every token of the block (16 threads per head), so
+// Layout: one CTA per (token block m, group of 8 heads, batch b); thread j
+// owns 8 hidden columns of every token of the block (16 threads per head), so
 // every global access is a coalesced 16-byte vector.  Rows are walked in
 // order, which fixes the fp32 summation order of the block sums (row 0 first).
 #include "common.cuh"
@@ -53,14 +53,14 @@ __device__ __forceinline__ void store8(__nv_bfloat16* dst, const float (&v)[8]) 
 // Streaming pass.  One CTA per (token block m, group of 8 heads, batch b):
 // thread j owns hidden columns [8 j, 8 j + 8) of the group (16 threads per
 // head) for every token of the block.  The token rows of q, k (and v / x when
-// needed) are streamed through an 8-token cp.async ring in shared memory;
+// needed) are streamed through a 4-token cp.async ring in shared memory;
 // each thread reads back exactly the 16-byte chunks it copied, so the loop
 // needs no block-wide barrier.  The full-width RMS statistics come from the
 // per-tile sums of squares (QKV GEMM epilogue or row_ssq_kernel).
 // ---------------------------------------------------------------------------
 constexpr int kNormHeads = 8;                   // heads per CTA
 constexpr int kNormThreads = kNormHeads * 16;   // 128
-constexpr int kNormRing = 8;                    // tokens in flight
+constexpr int kNormRing = 4;                    // tokens in flight (more, smaller CTAs beat a deeper ring)
 constexpr int kNormRingCompact = 3;             // co-resident variant (fits beside a GEMM CTA)
 constexpr int kNormRow = kNormHeads * 128 * 2;  // bytes of one tensor row segment (2 KB)
 

@@ -30,6 +30,18 @@ HEAD_DIM = 128
 FUSED_SELECT_MAX_NB = 768  # up to this many key blocks the scores stay on chip (no scores buffer)
 
 
+_SIDE: dict = {}
+
+
+def _side_streams(dev) -> tuple:
+    """Two side streams per device for the concurrent head-local branches."""
+    key = torch.device(dev).index if torch.device(dev).index is not None else torch.cuda.current_device()
+    s = _SIDE.get(key)
+    if s is None:
+        s = _SIDE[key] = (torch.cuda.Stream(device=key), torch.cuda.Stream(device=key))
+    return s
+
+
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
@@ -128,6 +140,13 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
     out = e(B, L, dim) if scatter is None else None
     o_sparse = e(B, L, dim) if keep else None
     scores = None
+    # three independent branches run concurrently (each under-fills the GPU on
+    # its own): selection on this stream, the low-rank C^T and q_lr on two side
+    # streams; the attention waits for all three
+    main = torch.cuda.current_stream(dev)
+    s_kv, s_q = _side_streams(dev)
+    s_kv.wait_stream(main)
+    s_q.wait_stream(main)
     _lib.call("rola_b200_center_from_sums", _ptr(ksum), B, NB, dim, L, _ptr(center), st)
     _lib.call("rola_b200_mean_pool", _ptr(k_rope), L * dim, HEAD_DIM, dim, B, H, L, blk, _ptr(center),
               _ptr(pooled_k), st)
@@ -145,10 +164,21 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
     vs = v.stride()
     ks = k_normed.stride()
     qs = q_normed.stride()
+    for t in (pq_, pk_, lc, ls):
+        if t is not None:
+            t.record_stream(s_kv)
+            t.record_stream(s_q)
+    for t in (c_part, C, Ct):
+        if t is not None:
+            t.record_stream(s_kv)
+    q_lr.record_stream(s_q)
     _lib.call("rola_b200_lowrank_kv", _ptr(k_normed), ks[0], HEAD_DIM, ks[1], _ptr(v), vs[0], HEAD_DIM, vs[1],
-              _ptr(pk_), _ptr(lc), _ptr(ls), rope_dim, B, L, H, R, splits, _ptr(c_part), _ptr(C), _ptr(Ct), st)
+              _ptr(pk_), _ptr(lc), _ptr(ls), rope_dim, B, L, H, R, splits, _ptr(c_part), _ptr(C), _ptr(Ct),
+              s_kv.cuda_stream)
     _lib.call("rola_b200_lowrank_q", _ptr(q_normed), qs[0], HEAD_DIM, qs[1], _ptr(pq_), _ptr(lc), _ptr(ls),
-              rope_dim, B, L, H, R, _ptr(q_lr), st)
+              rope_dim, B, L, H, R, _ptr(q_lr), s_q.cuda_stream)
+    main.wait_stream(s_kv)
+    main.wait_stream(s_q)
     eps_lr = float(torch.finfo(BF16).eps)
     if events is not None:
         events["attn"][0].record()
