@@ -98,8 +98,8 @@ int rola_b200_qk_norm_pack(const void* q_raw, const void* k_raw, const void* v_r
  * dst_row0 + L), and the gate into g_dst[r] [B, dst_rows, Hl].  A whole
  * sequence shard of rank rk is L = Ls, dst_rows = world*Ls, dst_row0 = rk*Ls;
  * a chunk of it (B = 1) shifts dst_row0.  The destinations are peer mappings
- * (rola_b200_peer_open); the kernels end with a system-scope fence, so a
- * stream-ordered barrier of all ranks after them makes the rows visible.
+ * (rola_b200_peer_open); the rows are complete when the kernel completes, so a
+ * stream-ordered barrier of all ranks after it makes them visible.
  * world <= ROLA_MAX_RANKS.  No counterpart in the reference, whose context
  * parallelism (sparkdiffusion/utils/a2a_cp.py:146-186) exchanges with NCCL
  * all-to-all. */

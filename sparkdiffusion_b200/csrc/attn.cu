@@ -569,10 +569,6 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
-  // rows stored into peers' memory: one system-scope fence per CTA after the
-  // block barrier orders every thread's rows before the kernel's completion is
-  // signalled to the other ranks
-  if (p.peer_n > 0 && threadIdx.x == 0) __threadfence_system();
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();

@@ -229,13 +229,6 @@ __device__ __forceinline__ void norm_block(const NormRopeParams& p, int m, int g
     }
   }
   cp_async_wait_grp<0>();
-  // chunked outputs may live in peers' memory: one system-scope fence per CTA
-  // after the block barrier orders every thread's rows before the kernel's
-  // completion is signalled to the other ranks
-  if (p.heads_per_chunk != p.H) {
-    named_bar_sync(bar_id);
-    if (j == 0) __threadfence_system();
-  }
   if (POOL && active) {
     const float nx = (float)n;
     float pq[8];

@@ -79,6 +79,7 @@ class WanSelfAttentionRoLaB200(nn.Module):
         self._use_fused_inference = True
         self._pg = None
         self._qkv_cache = None
+        self._o_cache = None
 
     def init_weights(self):
         """Re-apply the RoLa-specific init after WanModel's xavier pass
@@ -138,7 +139,21 @@ class WanSelfAttentionRoLaB200(nn.Module):
                                        self.proj_q.weight, self.proj_k.weight, self.gate_proj.weight,
                                        self.gate_bias, self.num_heads, 128, topk, self.eps)
 
+    def _o_weight(self):
+        """bf16 copy of the output projection for the tcgen05 GEMM (cached like the QKV weight)."""
+        key = (self.o.weight.data_ptr(), self.o.weight._version, self.o.bias.data_ptr(), self.o.bias._version)
+        if self._o_cache is None or self._o_cache[0] != key:
+            self._o_cache = (key, self.o.weight.to(torch.bfloat16).contiguous(),
+                             self.o.bias.to(torch.bfloat16).contiguous())
+        return self._o_cache[1], self._o_cache[2]
+
     def forward(self, x: torch.Tensor, seq_lens: torch.Tensor, freqs: torch.Tensor, rope_cache=None) -> torch.Tensor:
         del seq_lens
         out = self.attention_core(x, freqs, rope_cache)
+        B, L, dim = out.shape
+        if dim % 256 == 0:
+            # self.o (wan_rola_attention.py:447) on the same persistent tcgen05 GEMM as the QKV projection
+            w, b = self._o_weight()
+            y = ops.qkv_gemm(out.reshape(B * L, dim), w, b).view(B, L, dim)
+            return y.to(self.o.weight.dtype)
         return F.linear(out.to(self.o.weight.dtype), self.o.weight, self.o.bias)

@@ -145,25 +145,16 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
     # streams; the attention waits for all three
     main = torch.cuda.current_stream(dev)
     s_kv, s_q = _side_streams(dev)
-    s_kv.wait_stream(main)
-    s_q.wait_stream(main)
-    _lib.call("rola_b200_center_from_sums", _ptr(ksum), B, NB, dim, L, _ptr(center), st)
-    _lib.call("rola_b200_mean_pool", _ptr(k_rope), L * dim, HEAD_DIM, dim, B, H, L, blk, _ptr(center),
-              _ptr(pooled_k), st)
-    if lut is None:
-        scores = e(B * H, NB, NB, dt=torch.float32) if NB > FUSED_SELECT_MAX_NB else None
-        lut = e(B * H, NB, topk, dt=torch.int32)
-        _lib.call("rola_b200_block_select", _ptr(pooled_q), _ptr(pooled_k), B * H, NB, NB, topk, _ptr(scores),
-                  _ptr(lut), st)
-    else:
-        lut = lut.to(device=dev, dtype=torch.int32).reshape(B * H, NB, -1).contiguous()
-        topk = lut.shape[-1]
     pq_, pk_ = proj_q.to(BF16).contiguous(), proj_k.to(BF16).contiguous()
     lc = None if lr_cos is None else lr_cos.to(BF16).contiguous()
     ls = None if lr_sin is None else lr_sin.to(BF16).contiguous()
     vs = v.stride()
     ks = k_normed.stride()
     qs = q_normed.stride()
+    # fork once every input of the side branches (the conversions just queued
+    # included) is on this stream
+    s_kv.wait_stream(main)
+    s_q.wait_stream(main)
     for t in (pq_, pk_, lc, ls):
         if t is not None:
             t.record_stream(s_kv)
@@ -177,6 +168,17 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
               s_kv.cuda_stream)
     _lib.call("rola_b200_lowrank_q", _ptr(q_normed), qs[0], HEAD_DIM, qs[1], _ptr(pq_), _ptr(lc), _ptr(ls),
               rope_dim, B, L, H, R, _ptr(q_lr), s_q.cuda_stream)
+    _lib.call("rola_b200_center_from_sums", _ptr(ksum), B, NB, dim, L, _ptr(center), st)
+    _lib.call("rola_b200_mean_pool", _ptr(k_rope), L * dim, HEAD_DIM, dim, B, H, L, blk, _ptr(center),
+              _ptr(pooled_k), st)
+    if lut is None:
+        scores = e(B * H, NB, NB, dt=torch.float32) if NB > FUSED_SELECT_MAX_NB else None
+        lut = e(B * H, NB, topk, dt=torch.int32)
+        _lib.call("rola_b200_block_select", _ptr(pooled_q), _ptr(pooled_k), B * H, NB, NB, topk, _ptr(scores),
+                  _ptr(lut), st)
+    else:
+        lut = lut.to(device=dev, dtype=torch.int32).reshape(B * H, NB, -1).contiguous()
+        topk = lut.shape[-1]
     main.wait_stream(s_kv)
     main.wait_stream(s_q)
     eps_lr = float(torch.finfo(BF16).eps)

@@ -10,9 +10,12 @@ A buffer is carved into named regions (``PeerBuffer.region``), each a dense
 tensor view of this rank's copy plus the table of all ranks' addresses of the
 same region, as the ``void* const*`` arrays the scatter entry points take.
 
-Ordering: the writer kernels end with a system-scope fence; ``stream_barrier``
-(a one-element NCCL all-reduce on the current stream) after them makes every
-rank's rows visible before the next kernel on any rank reads them.
+Ordering: a kernel's peer stores are complete when the kernel completes;
+``stream_barrier`` (a one-element NCCL all-reduce queued on the current stream
+after the writer kernel) completes on a rank only after every rank's writer
+kernel completed, so the next kernel on any rank sees every rank's rows.  (A
+system-scope fence at the end of each writer CTA was measured to cost 50 us
+per layer at 8 GPUs by draining the CTA's NVLink stores before it exits.)
 """
 
 from __future__ import annotations

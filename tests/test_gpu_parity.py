@@ -312,3 +312,24 @@ def test_host_pipeline_matches_device_forward():
     assert _lib.device_status() == 0
     for i, (o, r) in enumerate(zip(outs, refs)):
         assert torch.equal(o, r), f"step {i} differs"
+
+
+def test_layer_forward_with_output_projection():
+    """The drop-in layer: attention core followed by self.o on the tcgen05 GEMM
+    equals the core output projected in fp32 (bf16 tolerance)."""
+    from sparkdiffusion_b200.layer import WanSelfAttentionRoLaB200
+
+    torch.manual_seed(0)
+    grid = (3, 10, 20)
+    L = grid[0] * grid[1] * grid[2]
+    layer = WanSelfAttentionRoLaB200(512, 4, True, 1e-6, rola_topk_ratio=2.5 / 5, rola_rank=64).cuda().eval()
+    x = torch.randn(1, L, 512, device="cuda").to(torch.bfloat16)
+    freqs = wan_rope_freqs(*grid).cuda()
+    with torch.no_grad():
+        y = layer(x, torch.tensor([L]), freqs)
+        core = layer.attention_core(x, freqs)
+        ref = torch.nn.functional.linear(core.float(), layer.o.weight.float(), layer.o.bias.float())
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert y.shape == (1, L, 512) and y.dtype == layer.o.weight.dtype
+    assert_bf16_close(y.float().cpu(), ref.cpu(), "layer output projection")
