@@ -427,8 +427,20 @@ def main():
                 "peak_kind": f"{peak_kind} bf16 sustained", "traffic": tr,
                 "ms_per_launch": t_gemm if name == "gemm" else t_attn}
 
-    # gemm, norm(+pack), [rope_pool], centre, pooled k, select, lowrank_kv (+ reduce), lowrank_q, attention
-    launches_per_step = 9 if world == 1 else 10
+    # library kernels per step.  1 GPU: gemm, norm, centre, pooled k, select, lowrank_kv, reduce,
+    # lowrank_q, attention.  N GPUs (peer transport): one GEMM per token chunk (each but the first
+    # carrying the previous chunk's scatter), the last chunk's scatter, then rope_pool and the seven
+    # head-local kernels; (NCCL transport: gemm, norm_pack, rope_pool + seven)
+    if world == 1:
+        launches_per_step = 9
+    elif args.transport == "peer":
+        from sparkdiffusion_b200.ulysses import chunk_plan
+
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        n_chunks = len(chunk_plan(Ls, 3 * dim // 256, sms, args.chunks)) if args.chunks != 1 else 1
+        launches_per_step = n_chunks + 1 + 8
+    else:
+        launches_per_step = 10
     line = {
         "metric": METRIC, "value": flops_total / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": ms, "ms_per_layer": ms, "higher_is_better": True,
