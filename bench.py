@@ -47,7 +47,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # from one ncu capture at C3 (profiles/gemm_bf16_tcgen05_C3.md,
 # profiles/sparse_attn_tcgen05_C3.md) scaled to C4 by the rows processed
 # (75600 / 32760); C3 itself as captured.
-NCU_TRAFFIC_BYTES = {"C4": {"gemm": 8.9e9, "attn": 4.4e9}, "C3": {"gemm": 3.89e9, "attn": 1.92e9}}
+NCU_TRAFFIC_BYTES = {"C4": {"gemm": 8.9e9, "attn": 3.6e9}, "C3": {"gemm": 3.89e9, "attn": 1.57e9}}
 
 
 def parse_args():
