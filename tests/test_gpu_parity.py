@@ -333,3 +333,20 @@ def test_layer_forward_with_output_projection():
     assert _lib.device_status() == 0
     assert y.shape == (1, L, 512) and y.dtype == layer.o.weight.dtype
     assert_bf16_close(y.float().cpu(), ref.cpu(), "layer output projection")
+
+
+def test_gate_from_hidden_states_in_epilogue(qkv_case):
+    """The attention epilogue's other gate source: the gate computed from the
+    hidden-state tile x (rola_b200_sparse_attn with x) instead of precomputed
+    gate values; same output within the bf16 tolerance (the gate's dot product
+    is summed in another order)."""
+    wl, inp, *_, out, ex = qkv_case
+    g = _cuda(inp)
+    lr_cos, lr_sin, rope_dim = qkv_case[3], qkv_case[4], qkv_case[5]
+    got = ops.head_local_attention(ex["q_rope"], ex["k_rope"], ex["q_normed"], ex["k_normed"], ex["v"], None,
+                                   ex["pooled_q"], ex["ksum"], lr_cos.cuda(), lr_sin.cuda(), rope_dim, g["proj_q"],
+                                   g["proj_k"], wl.H, wl.blk, wl.topk, lut=ex["lut"], x=g["x"].contiguous(),
+                                   gate_w=g["gate_w"], gate_b=g["gate_b"])
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert_bf16_close(got.float().cpu(), out.float().cpu(), "gate from x vs gate values")
