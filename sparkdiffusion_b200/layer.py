@@ -157,3 +157,82 @@ class WanSelfAttentionRoLaB200(nn.Module):
             y = ops.qkv_gemm(out.reshape(B * L, dim), w, b).view(B, L, dim)
             return y.to(self.o.weight.dtype)
         return F.linear(out.to(self.o.weight.dtype), self.o.weight, self.o.bias)
+
+
+class WanSelfAttentionB200(nn.Module):
+    """Dense self-attention of the Wan DiT on the B200 kernels: the fused
+    inference path of ``WanSelfAttention.forward`` (wan2pt1.py:221-324) — one
+    QKV GEMM, the streaming qk-RMSNorm + RoPE pass, dense attention (the
+    block-sparse kernel with every key block selected) and the output
+    projection on the same GEMM.  Same parameter names and shapes (q, k, v, o,
+    norm_q, norm_k) as the reference layer, so its checkpoints load unchanged.
+    Inference only."""
+
+    def __init__(self, dim: int, num_heads: int, qk_norm: bool = True, eps: float = 1e-6):
+        super().__init__()
+        assert dim % num_heads == 0
+        self.dim = dim
+        self.num_heads = num_heads
+        self.head_dim = dim // num_heads
+        self.qk_norm = qk_norm
+        self.eps = eps
+        self.q = nn.Linear(dim, dim)
+        self.k = nn.Linear(dim, dim)
+        self.v = nn.Linear(dim, dim)
+        self.o = nn.Linear(dim, dim)
+        self.norm_q = RMSNormWeight(dim, eps=eps) if qk_norm else nn.Identity()
+        self.norm_k = RMSNormWeight(dim, eps=eps) if qk_norm else nn.Identity()
+        self._layer_name = "DenseB200"
+        self._qkv_cache = None
+        self._o_cache = None
+        self.init_weights()
+
+    def init_weights(self):
+        """Same init as the reference layer (wan2pt1.py:247-262)."""
+        std = 1.0 / math.sqrt(self.dim)
+        for lin in (self.q, self.k, self.v, self.o):
+            torch.nn.init.trunc_normal_(lin.weight, std=std)
+            lin.bias.data.zero_()
+        if self.qk_norm:
+            self.norm_q.reset_parameters()
+            self.norm_k.reset_parameters()
+
+    _fused_qkv = WanSelfAttentionRoLaB200._fused_qkv
+    _o_weight = WanSelfAttentionRoLaB200._o_weight
+
+    def forward(self, x: torch.Tensor, seq_lens: torch.Tensor, freqs: torch.Tensor, rope_cache=None) -> torch.Tensor:
+        del seq_lens
+        if torch.is_grad_enabled() and self.training:
+            raise RuntimeError("WanSelfAttentionB200 is inference-only (no backward kernels)")
+        if not x.is_cuda:
+            raise RuntimeError("WanSelfAttentionB200 runs on CUDA tensors only")
+        if self.head_dim != 128 or self.dim % 256 != 0:
+            raise ValueError("the B200 path needs head_dim 128 and an even head count")
+        B, L, dim = x.shape
+        H = self.num_heads
+        x = x.to(torch.bfloat16).contiguous()
+        if rope_cache is not None and rope_cache[0] is not None:
+            cos_sin = rope_cache[0].to(torch.float32).contiguous()
+        else:
+            cos_sin = prepare_cos_sin(freqs, freqs.shape[0], self.head_dim).to(torch.float32).contiguous()
+        w_qkv, b_qkv = self._fused_qkv()
+        ssq = torch.empty(B * L, 3 * dim // 256, device=x.device, dtype=torch.float32)
+        qkv = ops.qkv_gemm(x.reshape(B * L, dim), w_qkv, b_qkv, ssq).view(B, L, 3 * dim)
+        bf = torch.bfloat16
+        q_rope = torch.empty(B, L, dim, device=x.device, dtype=bf)
+        k_rope = torch.empty_like(q_rope)
+        nwq = ops._bf16_vec(self.norm_q.weight, dim, "norm_q") if self.qk_norm else None
+        nwk = ops._bf16_vec(self.norm_k.weight, dim, "norm_k") if self.qk_norm else None
+        from . import _lib
+
+        _lib.call("rola_b200_qk_norm_rope", ops._ptr(qkv), ops._ptr(qkv[..., dim:]), 3 * dim,
+                  ops._ptr(ssq if self.qk_norm else None), ssq.shape[-1] if self.qk_norm else 0, None,
+                  ops._ptr(nwq), ops._ptr(nwk), ops._ptr(cos_sin), None, None, B, L, H, 128, self.eps,
+                  ops._ptr(q_rope), ops._ptr(k_rope), None, None, None, None, None, ops._stream())
+        out = torch.empty(B, L, dim, device=x.device, dtype=bf)
+        tok = (L * dim, 128, dim)  # (b, h, t) strides of the token-major [B, L, H*D] tensors
+        ops.dense_attention_strided(q_rope, k_rope, qkv[..., 2 * dim:], B, L, H, tok, (L * 3 * dim, 128, 3 * dim),
+                                    out, tok)
+        w, b = self._o_weight()
+        y = ops.qkv_gemm(out.reshape(B * L, dim), w, b).view(B, L, dim)
+        return y.to(self.o.weight.dtype)

@@ -441,6 +441,50 @@ def fused_sparse_attn(q, k, v, topk_ratio: float = 0.1, blkq: int = 64, blkk: in
     return o
 
 
+_FULL_LUT: dict = {}
+
+
+def _full_lut(BH: int, NB: int, dev) -> torch.Tensor:
+    """LUT that keeps every key block of every query block, ascending (dense attention)."""
+    key = (BH, NB, str(dev))
+    lut = _FULL_LUT.get(key)
+    if lut is None:
+        lut = torch.arange(NB, device=dev, dtype=torch.int32).expand(BH, NB, NB).contiguous()
+        _FULL_LUT[key] = lut
+    return lut
+
+
+def dense_attention_strided(q, k, v, B: int, L: int, H: int, qk_strides, v_strides, out, o_strides) -> None:
+    """Dense softmax attention through the block-sparse kernel with every key
+    block selected (the reference's dense path runs SDPA / flash attention after
+    the same prologue, sparkdiffusion/networks/wan2pt1.py:282-320).  Element
+    (b, h, t, d) of each tensor at ``base + sB*b + sH*h + sT*t + d``."""
+    NB = (L + 127) // 128
+    lut = _full_lut(B * H, NB, q.device)
+    _lib.call("rola_b200_sparse_attn", _ptr(q), _ptr(k), *qk_strides, _ptr(v), *v_strides, _ptr(lut), B, L, H, 128,
+              NB, None, None, None, None, 0, 0, 0, None, None, 0.0, None, _ptr(out), *o_strides, _stream())
+
+
+def dense_attention(q, k, v, num_heads: int):
+    """Dense attention over ``q, k, v [B*H, L, D]`` (normed and roped, the
+    layouts ``fused_qkv_gemm_rope`` returns) -> ``[B, H, L, D]``; the reference
+    computes it with its attention op after the fused prologue
+    (sparkdiffusion/networks/wan2pt1.py:282-320)."""
+    BH, L, D = q.shape
+    if num_heads <= 0 or BH % num_heads != 0:
+        raise ValueError(f"invalid num_heads={num_heads} for leading dimension {BH}")
+    if D != HEAD_DIM:
+        raise ValueError("head dim must be 128")
+    _require_cuda(q, k, v)
+    H = num_heads
+    B = BH // H
+    q4, k4, v4 = (t.view(B, H, L, D).contiguous() for t in (q, k, v))
+    o = torch.empty_like(v4)
+    s, vs = q4.stride(), v4.stride()
+    dense_attention_strided(q4, k4, v4, B, L, H, (s[0], s[1], s[2]), (vs[0], vs[1], vs[2]), o, (s[0], s[1], s[2]))
+    return o
+
+
 def fused_qkv_gemm_rope(x, q_proj, k_proj, v_proj, freqs, norm_q_weight, norm_k_weight, num_heads, head_dim,
                         eps: float = 1e-6, return_normed: bool = False, fp8_weights=None, cos_sin=None):
     """QKV projection + full-width qk-RMSNorm + interleaved RoPE

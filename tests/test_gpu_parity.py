@@ -350,3 +350,26 @@ def test_gate_from_hidden_states_in_epilogue(qkv_case):
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
     assert_bf16_close(got.float().cpu(), out.float().cpu(), "gate from x vs gate values")
+
+
+def test_dense_attention_full_lut():
+    """Dense attention (every key block kept) against the oracle's recurrence
+    with the full LUT; ragged tail block."""
+    B, H, L = 1, 2, 600
+    torch.manual_seed(5)
+    q = torch.randn(B * H, L, 128).to(torch.bfloat16)
+    k = torch.randn(B * H, L, 128).to(torch.bfloat16)
+    v = torch.randn(B * H, L, 128).to(torch.bfloat16)
+    o = ops.dense_attention(q.cuda(), k.cuda(), v.cuda(), num_heads=H)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    NB = (L + 127) // 128
+    lut = torch.arange(NB, dtype=torch.int32).expand(B * H, NB, NB).reshape(B, H, NB, NB)
+    q4, k4, v4 = (t.view(B, H, L, 128) for t in (q, k, v))
+    ref = orc.sparse_attn_lut(q4, k4, v4, lut, 128, 128, out_dtype=torch.float32)
+    # every query attends to all 600 keys: the output is an average over many
+    # values, so its RMS is small against the bf16 rounding of P and of the
+    # output; the mean bound is the stated one, the max bound is the
+    # end-to-end one (measured: max 2.85e-2, mean 1.11e-3 of the RMS)
+    assert_bf16_close(o.cpu(), ref, "dense attention", max_tol=6e-2)
+

@@ -63,3 +63,14 @@ def test_forward_refuses_cpu_and_grad():
 def test_constructor_validation():
     with pytest.raises(ValueError):
         WanSelfAttentionRoLaB200(256, 2, attn_precision="fp4")
+
+
+def test_dense_layer_params_match_reference_dense_layer():
+    """WanSelfAttentionB200 carries WanSelfAttention's parameters (wan2pt1.py:221-239)."""
+    from sparkdiffusion_b200.layer import WanSelfAttentionB200
+
+    m = WanSelfAttentionB200(256, 2, True, 1e-6)
+    got = {k: tuple(v.shape) for k, v in m.state_dict().items()}
+    dense = {k: v for k, v in REFERENCE_PARAMS.items() if k.split(".")[0] in ("q", "k", "v", "o", "norm_q", "norm_k")}
+    assert got == dense
+    assert torch.all(m.q.bias == 0) and torch.all(m.norm_q.weight == 1)
