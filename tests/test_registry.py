@@ -74,3 +74,19 @@ def test_dense_layer_params_match_reference_dense_layer():
     dense = {k: v for k, v in REFERENCE_PARAMS.items() if k.split(".")[0] in ("q", "k", "v", "o", "norm_q", "norm_k")}
     assert got == dense
     assert torch.all(m.q.bias == 0) and torch.all(m.norm_q.weight == 1)
+
+
+def test_dense_path_validates_on_the_host():
+    from sparkdiffusion_b200 import ops
+    from sparkdiffusion_b200.layer import WanSelfAttentionB200
+
+    q = torch.zeros(4, 256, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        ops.dense_attention(q, q, q, num_heads=3)  # 4 is not a multiple of 3
+    with pytest.raises(ValueError):
+        ops.dense_attention(q[..., :64], q[..., :64], q[..., :64], num_heads=2)  # head dim 64
+    with pytest.raises((RuntimeError, ValueError)):
+        ops.dense_attention(q, q, q, num_heads=2)  # CPU tensors: no fallback
+    m = WanSelfAttentionB200(256, 2).eval()
+    with torch.no_grad(), pytest.raises(RuntimeError):
+        m(torch.zeros(1, 256, 256), torch.tensor([256]), torch.zeros(256, 64))
