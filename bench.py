@@ -42,11 +42,9 @@ import torch.distributed as dist  # noqa: E402
 METRIC = "RoLa attn ms/layer & effective TFLOP/s (selected blocks), Wan14B 720P, 1/2/4/8 B200"
 UNIT = "TFLOP/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes (read + write) per launch from one ncu capture (profiles/); None until captured
-# DRAM bytes (read + write) per launch of the two tensor-bound kernels, 1 GPU:
-# from one ncu capture at C3 (profiles/gemm_bf16_tcgen05_C3.md,
-# profiles/sparse_attn_tcgen05_C3.md) scaled to C4 by the rows processed
-# (75600 / 32760); C3 itself as captured.
+# DRAM bytes (read + write) per launch of the two tensor-bound kernels, 1 GPU,
+# from one ncu capture at C3 scaled to C4 by the rows processed (75600 / 32760);
+# C3 itself as captured.
 NCU_TRAFFIC_BYTES = {"C4": {"gemm": 8.9e9, "attn": 3.6e9}, "C3": {"gemm": 3.89e9, "attn": 1.57e9}}
 
 
@@ -59,6 +57,8 @@ def parse_args():
     ap.add_argument("--workload", default="C4")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-gpu-reference", action="store_true",
+                    help="skip timing the reference's own Triton path on this GPU (N=1)")
     ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
                     help="N>1: sequence<->head exchanges fused into the kernels over peer memory, or NCCL all-to-all")
     ap.add_argument("--chunks", type=int, default=None,
@@ -213,11 +213,164 @@ def run_reference(args, wl, rank):
 
 
 # ---------------------------------------------------------------------------
+# The reference's own GPU path on the same box (a reported comparison point)
+# ---------------------------------------------------------------------------
+def reference_package_dir() -> str | None:
+    """``pip install --target`` of the SparkDiffusion checkout (git-ignored), if present."""
+    d = os.environ.get("SPARKDIFFUSION_REF", os.path.join(ROOT, "baseline", "_ref"))
+    return d if os.path.isdir(os.path.join(d, "sparkdiffusion", "ops", "fused_kernel")) else None
+
+
+def gpu_reference_timing(wl, inp, dev, steps: int, warmup: int) -> dict:
+    """Time the reference's fused RoLa path (Triton + cuBLAS, autotuned, with its
+    ``IS_BLACKWELL`` attention tuning) on this GPU, called as
+    ``WanSelfAttentionRoLa.fused_forward`` calls it
+    (sparkdiffusion/networks/wan_rola_attention.py:414-446) without ``self.o``,
+    with ``topk_ratio=(k+0.5)/NB``; per stage and for ``_rola_fwd_kernel``
+    alone (fused_sparse_attn.py:55-144, launched as :204-213 launches it)."""
+    import importlib
+    import types
+
+    from sparkdiffusion_b200.rope import prepare_cos_sin, wan_rope_freqs
+    from sparkdiffusion_b200.workloads import attn_flops_lut
+
+    ref = reference_package_dir()
+    if ref is None:
+        return {"unavailable": "reference package not installed under baseline/_ref"}
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    fq = importlib.import_module("sparkdiffusion.ops.fused_kernel.fused_qkv_rope")
+    fs = importlib.import_module("sparkdiffusion.ops.fused_kernel.fused_sparse_attn")
+    fl = importlib.import_module("sparkdiffusion.ops.fused_kernel.fused_lowrank")
+    fg = importlib.import_module("sparkdiffusion.ops.fused_kernel.fused_gate")
+    B, L, H, dim = wl.B, wl.L, wl.H, wl.dim
+    freqs = wan_rope_freqs(*wl.grid)
+    cos_sin = prepare_cos_sin(freqs, L, 128).to(dev)
+    lr_tables = tuple(t.to(dev) if isinstance(t, torch.Tensor) else t
+                      for t in fl.prepare_lowrank_cos_sin(freqs, L, wl.rank, torch.bfloat16))
+    w = inp["w_qkv"]
+    lin = lambda wt: types.SimpleNamespace(weight=wt, bias=None)  # noqa: E731
+    projs = (lin(w[:dim]), lin(w[dim:2 * dim]), lin(w[2 * dim:]))
+    gate_b = inp["gate_b"].reshape(H).to(torch.bfloat16)
+    rec = {}
+
+    def layer(ev=None):
+        mark = (lambda i: ev[i].record()) if ev is not None else (lambda i: None)
+        mark(0)
+        q, k, v, qn, kn = fq.fused_qkv_gemm_rope(inp["x"], *projs, freqs.to(dev), inp["norm_wq"], inp["norm_wk"],
+                                                 H, 128, eps=1e-6, return_normed=True, cos_sin=cos_sin)
+        mark(1)
+        orig = torch.topk
+
+        def topk(x, kk, *a, **kw):
+            r = orig(x, kk, *a, **kw)
+            rec["lut"] = r.indices
+            return r
+
+        torch.topk = topk
+        try:
+            o_sparse = fs.fused_sparse_attn(q, k, v, topk_ratio=wl.reference_topk_ratio, blkq=wl.blk, blkk=wl.blk,
+                                            num_heads=H)
+        finally:
+            torch.topk = orig
+        mark(2)
+        o_lr = fl.fused_lowrank(qn, kn, v, None, proj_q_weight=inp["proj_q"], proj_k_weight=inp["proj_k"],
+                                rola_rank=wl.rank, eps=1e-6, rope_tables=lr_tables)
+        mark(3)
+        out = fg.fused_gate(o_lr, o_sparse, inp["x"], gate_proj_weight=inp["gate_w"], gate_bias=gate_b)
+        mark(4)
+        rec["qkv"] = (q, k, v)
+        return out
+
+    with torch.no_grad():
+        for _ in range(warmup):  # the first call autotunes every Triton kernel
+            layer()
+        torch.cuda.synchronize()
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(steps)]
+        for i in range(steps):
+            layer(evs[i])
+        torch.cuda.synchronize()
+        stage = [statistics.median(e[j].elapsed_time(e[j + 1]) for e in evs) for j in range(4)]
+        total = statistics.median(e[0].elapsed_time(e[4]) for e in evs)
+        # _rola_fwd_kernel alone on the last layer's q/k/v and LUT, launched as fused_sparse_attn does
+        q, k, v = rec["qkv"]
+        lut = rec["lut"]
+        NB = wl.NB
+        q4, k4, v4 = (t.view(B, H, L, 128) for t in (q, k, v))
+        o = torch.empty_like(v4)
+        kt = lut.shape[-1]
+
+        def kernel():
+            fs._rola_fwd_kernel[(NB, B * H)](q4, k4, v4, lut.reshape(B * H, NB, kt), o, 128 ** -0.5 * 1.4426950408889634,
+                                             kt, L, NB, 128, wl.blk, wl.blk, IS_BLACKWELL=fs.is_blackwell(q.device))
+
+        for _ in range(warmup):
+            kernel()
+        torch.cuda.synchronize()
+        ke = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for a, b in ke:
+            a.record()
+            kernel()
+            b.record()
+        torch.cuda.synchronize()
+        t_kernel = statistics.median(a.elapsed_time(b) for a, b in ke)
+        flops = attn_flops_lut(lut, L, wl.blk)
+    rec.clear()
+    torch.cuda.empty_cache()
+    return {"ms_per_layer": total, "value": flops / (total * 1e-3) / 1e12, "unit": UNIT,
+            "stages_ms": {"fused_qkv_gemm_rope": stage[0], "fused_sparse_attn": stage[1],
+                          "fused_lowrank": stage[2], "fused_gate": stage[3]},
+            "rola_fwd_kernel": {"ms": t_kernel, "tflops": flops / (t_kernel * 1e-3) / 1e12,
+                                "flops": flops},
+            "what": "reference fused path (Triton 3.6 + cuBLAS, autotuned) from baseline/_ref on this GPU, "
+                    "same seeded inputs, topk_ratio=(k+0.5)/NB, median of the timed steps; self.o excluded"}
+
+
+# ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
 def workload_desc(wl) -> str:
     return (f"{wl.name}: B={wl.B} H={wl.H} D=128 latent grid {wl.grid[0]}x{wl.grid[1]}x{wl.grid[2]} L={wl.L}, "
             f"block {wl.blk} ({wl.NB} blocks), top-{wl.topk}, low-rank {wl.rank}, fused QKV from hidden states")
+
+
+def check_parity(args, wl, out1, lut1, step, x, rank, world, dev) -> dict:
+    """Parity of the benchmarked forward, reported in the JSON line.
+
+    * Against the reference: the 1-GPU forward of this layer (``out1``, ``lut1``)
+      against the recorded output of the reference's own fused path on a B200
+      for the same seeded inputs (``tests/golden/ref_b200_<workload>.pt``, heads
+      0-3 on sampled token rows): per-row LUT set agreement with every mismatch
+      classified, and the output error on the agreeing rows.
+    * At N > 1: this rank's Ulysses output rows and LUT (its head group) against
+      the 1-GPU forward's, max over ranks.
+    Bounds: LUT mismatches all explained (bf16 ties or boundary rounding of the
+    reference's scores), output max-abs <= 2e-2 and mean-abs <= 2e-3 of the RMS."""
+    from sparkdiffusion_b200 import refcheck
+
+    B, L, H = wl.B, wl.L, wl.H
+    res: dict = {}
+    fx = refcheck.load_fixture(args.workload.lower())
+    if fx is not None:
+        r = refcheck.output_parity(out1, lut1, fx, B, L, H, wl.blk)
+        r["ok"] = r["lut_unexplained"] == 0 and r["out_max_rel"] <= 2e-2 and r["out_mean_rel"] <= 2e-3
+        res["vs_reference_b200"] = r
+    else:
+        res["vs_reference_b200"] = {"unavailable": f"no reference fixture for {args.workload}"}
+    if world > 1:
+        Ls, Hl = L // world, H // world
+        rec: dict = {}
+        o = step(x, record=rec)
+        torch.cuda.synchronize()
+        ref_rows = out1[:, rank * Ls:(rank + 1) * Ls]
+        mine = lut1.view(B, H, -1, lut1.shape[-1])[:, rank * Hl:(rank + 1) * Hl].reshape(rec["lut"].shape)
+        mx, mn = refcheck.rel_err(o, ref_rows)
+        st = torch.tensor([float(not torch.equal(rec["lut"], mine)), mx, mn], dtype=torch.float64, device=dev)
+        dist.all_reduce(st, op=dist.ReduceOp.MAX)
+        bad, mx, mn = st.tolist()
+        res["vs_1gpu"] = {"lut_exact": bad == 0.0, "max_rel": mx, "mean_rel": mn,
+                          "ok": bad == 0.0 and mx <= 2e-2 and mn <= 2e-3}
+    return res
 
 
 def gpu_index(local_rank: int) -> int:
@@ -267,7 +420,8 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     _lib.load_library()
     peaks, peak_kind = load_peaks()
-    inp = make_inputs(wl, device=dev)
+    # seeded on the CPU (the same tensors as the committed reference fixtures), then moved
+    inp = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in make_inputs(wl, device="cpu").items()}
     freqs = wan_rope_freqs(*wl.grid, device=dev)
     cos_sin = prepare_cos_sin(freqs, wl.L, 128)
     lr_cos, lr_sin, rope_dim = prepare_lowrank_cos_sin(freqs, wl.L, wl.rank, torch.bfloat16)
@@ -280,24 +434,28 @@ def main():
               inp["gate_w"].reshape(-1).contiguous(), inp["gate_b"].reshape(-1).to(torch.bfloat16))
 
     if world == 1:
-        def step(xin, events=None):
+        def step(xin, events=None, record=None):
             return ops.rola_attention_core(xin, w_qkv, None, *common, H, 128, wl.topk, events=events)
     else:
         from sparkdiffusion_b200.ulysses import ulysses_rola_attention_params
 
-        def step(xin, events=None):
+        def step(xin, events=None, record=None):
             return ulysses_rola_attention_params(xin, w_qkv, None, *common, H, wl.topk, group, events=events,
-                                                 transport=args.transport, chunks=args.chunks)
+                                                 transport=args.transport, chunks=args.chunks, record=record)
 
     # exact selected-block FLOPs from this layer's LUT.  Every rank runs the
     # 1-GPU pipeline once on the full hidden states (selection is bit-exact and
     # identical to the head-sharded one), so no collective is needed here.
-    _, ex = ops.rola_attention_core(inp["x"], w_qkv, None, *common, H, 128, wl.topk, keep=True)
+    out1, ex = ops.rola_attention_core(inp["x"], w_qkv, None, *common, H, 128, wl.topk, keep=True)
     flops_total = attn_flops_lut(ex["lut"], L, wl.blk)
+    lut1 = ex["lut"]
     del ex
     torch.cuda.synchronize()
     if _lib.device_status() != 0:
         raise SystemExit("device-side error flag set during the LUT pass")
+    torch.cuda.empty_cache()
+    parity = check_parity(args, wl, out1, lut1, step, x, rank, world, dev)
+    del out1, lut1
     torch.cuda.empty_cache()
 
     for _ in range(args.warmup):
@@ -414,6 +572,13 @@ def main():
         cpu_base = {"value": flops_total / secs / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
                     "sample": sample, "ms_per_layer": secs * 1e3}
 
+    gpu_ref = None
+    if world == 1 and not args.no_gpu_reference:
+        gpu_ref = gpu_reference_timing(wl, inp, dev, steps=min(K, 10), warmup=3)
+
+    # the timed region is well under a second of back-to-back layers, so the
+    # burst bf16 figure is the denominator; the sustained one is given beside it
+    peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
     peak_sust = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
     gemm_flops_local = 6.0 * B * Ls * dim * dim
     gemm_ach = gemm_flops_local / (t_gemm * 1e-3) / 1e12
@@ -423,8 +588,8 @@ def main():
     def roof(name, ach):
         tr = NCU_TRAFFIC_BYTES.get(args.workload, {}).get(name) if world == 1 else None
         return {"kernel": {"gemm": "gemm_bf16_tcgen05", "attn": "sparse_attn_tcgen05"}[name], "bound": "tensor",
-                "achieved": ach, "peak": peak_sust, "unit": "TFLOP/s", "frac": ach / peak_sust,
-                "peak_kind": f"{peak_kind} bf16 sustained", "traffic": tr,
+                "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                "peak_kind": f"{peak_kind} bf16 burst", "frac_of_sustained": ach / peak_sust, "traffic": tr,
                 "ms_per_launch": t_gemm if name == "gemm" else t_attn}
 
     # library kernels per step.  1 GPU: gemm, norm, centre, pooled k, select, lowrank_kv, reduce,
@@ -458,6 +623,8 @@ def main():
         "roofline_gemm": roof("gemm", gemm_ach),
         "e2e": e2e,
         "cpu_baseline": cpu_base,
+        "gpu_reference": gpu_ref,
+        "parity": parity,
         "clocks": clk,
         "gpu_launches": launches_per_step * K,
         "device_status": status,

@@ -71,7 +71,7 @@ int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out
  * k_normed token-major [B*L, dim]; gate_out [B*L, H]; pooled_q [B, H, NB, D]
  * bf16; ksum [B, NB, dim] fp32 block sums of k_rope.
  * Replaces _epilogue_kernel (fused_qkv_rope.py:53-225, layout [B*H, L, D] there),
- * mean_pool(q) (utils.py:272-297 via fused_sparse_attn.py:179) and the gate
+ * mean_pool(q) (utils.py:57-82 via fused_sparse_attn.py:179) and the gate
  * logits of _gate_fusion_kernel (fused_gate.py:97-114). */
 int rola_b200_qk_norm_rope(const void* q_raw, const void* k_raw, int64_t ld_raw, const float* ssq, int ssq_ld,
                            const void* x, const void* norm_wq, const void* norm_wk, const float* cos_sin,
@@ -147,7 +147,7 @@ int rola_b200_rope_pool(const void* q_normed, const void* k_normed, int64_t ld, 
                         int H, int blk, void* q_rope, void* k_rope, void* pooled_q, float* ksum,
                         rola_stream_t stream);
 
-/* (a5) block mean pooling, mean_pool (sparkdiffusion/ops/fused_kernel/utils.py:272-297).
+/* (a5) block mean pooling, mean_pool (sparkdiffusion/ops/fused_kernel/utils.py:57-82).
  * Element (b, h, t, d) of x sits at x + b*sB + h*sH + t*sT + d (elements).
  * center: [B, H, D] or NULL; out: [B, H, NB, D] bf16.  Rows are summed in order. */
 int rola_b200_mean_pool(const void* x, int64_t sB, int64_t sH, int64_t sT, int B, int H, int L, int blk,

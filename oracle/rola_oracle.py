@@ -176,7 +176,7 @@ def fused_qkv_gemm_rope(x, wq, bq, wk, bk, wv, bv, cos_sin, norm_wq, norm_wk, nu
 def block_sums(x4: torch.Tensor, blk: int) -> torch.Tensor:
     """fp32 per-block column sums ``[B, H, NB, D]``, rows added sequentially.
 
-    Tail rows beyond L contribute nothing (utils.py:250-254 masks them to 0).
+    Tail rows beyond L contribute nothing (utils.py:46-50 masks them to 0 after the subtraction).
     """
     B, H, L, D = x4.shape
     NB = (L + blk - 1) // blk
@@ -192,7 +192,7 @@ def block_sums(x4: torch.Tensor, blk: int) -> torch.Tensor:
 
 
 def block_counts(L: int, blk: int) -> torch.Tensor:
-    """Valid rows per block ``nx = min(blk, L - m*blk)`` (utils.py:267)."""
+    """Valid rows per block ``nx = min(blk, L - m*blk)`` (utils.py:52)."""
     NB = (L + blk - 1) // blk
     return torch.tensor([min(blk, L - m * blk) for m in range(NB)], dtype=F32)
 
@@ -200,9 +200,9 @@ def block_counts(L: int, blk: int) -> torch.Tensor:
 def mean_pool(x4: torch.Tensor, blk: int, center: torch.Tensor | None = None) -> torch.Tensor:
     """Block mean in the data dtype (utils.py:19-82, ``compress_kernel``).
 
-    Without a centre: bf16(sum_fp32(x) / nx) (:250-268).  With a centre:
+    Without a centre: bf16(sum_fp32(x) / nx) (:52-54).  With a centre:
     each row is first materialised as bf16(x - c) and tail rows are zeroed
-    after the subtraction (:255-265).
+    after the subtraction (:40-50).
     """
     dt = x4.dtype
     B, H, L, D = x4.shape

@@ -200,10 +200,13 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           ++r;
         }
       }
-      // drain: no TMA may still target shared memory when the CTA exits
-      mbar_wait(bar(B_Q), 0, abort_flag, kDevTimeoutLoad);
-      for (int n = max(0, r - NSLOTS); n < r; ++n)
-        mbar_wait(bar(B_FULL0 + n % NSLOTS), (n / NSLOTS) & 1, abort_flag, kDevTimeoutLoad);
+      // drain: no TMA may still target shared memory when the CTA exits.  The
+      // waits ignore the abort flag (on the abort path the copies already
+      // issued must still land) and share one wall-time limit.
+      const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+      bool drained = mbar_wait_until(bar(B_Q), 0, deadline);
+      for (int n = max(0, r - NSLOTS); n < r && drained; ++n)
+        drained = mbar_wait_until(bar(B_FULL0 + n % NSLOTS), (n / NSLOTS) & 1, deadline);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA
@@ -496,6 +499,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
               }
               const float logit = rbf(rbf(acc) + bf2f(p.gate_b[h]));
               gate = rbf(1.0f / (1.0f + expf(-logit)));
+            } else {
+              ok = false;  // no gate for these rows: store nothing (the error flag is set)
             }
           } else if (p.gate != nullptr && tok < p.L) {
             gate = bf2f(p.gate[((int64_t)b * p.L + tok) * p.H + h]);
@@ -506,7 +511,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         // fused row goes to the staging tile (stored out coalesced below),
         // o_sparse directly
         const float inv_rms = 1.0f / os_rms;
-        const bool store = tok < p.L;
+        const bool store = ok && tok < p.L;
         const int64_t orow = (int64_t)b * p.o_sB + (int64_t)h * p.o_sH + (int64_t)tok * p.o_sT;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
@@ -525,7 +530,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
               wo[e] = osp[8 * c + e];
             }
           }
-          if (staged) {
+          if (staged && ok) {
             *reinterpret_cast<uint4*>(stage + row * 256 + (((2 * c) ^ (row & 7)) << 4)) =
                 make_uint4(wo[0], wo[1], wo[2], wo[3]);
             *reinterpret_cast<uint4*>(stage + row * 256 + (((2 * c + 1) ^ (row & 7)) << 4)) =

@@ -116,6 +116,20 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Wait for a phase regardless of the CTA abort flag, until the globaltimer
+// passes `deadline`.  Used to drain bulk copies still in flight into shared
+// memory before a CTA exits (also on the abort path, where mbar_wait would
+// return at once): returns false when the deadline passed first.
+__device__ __forceinline__ bool mbar_wait_until(uint32_t bar, uint32_t parity, uint64_t deadline) {
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 255u && globaltimer_ns() > deadline) {
+      set_device_error(kDevTimeoutLoad);
+      return false;
+    }
+  }
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

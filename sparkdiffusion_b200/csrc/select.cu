@@ -53,7 +53,7 @@ __global__ void block_pool_kernel(const __nv_bfloat16* __restrict__ x, int64_t s
     unpack_bf2(u.w, v[6], v[7]);
     if (center) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = rbf(v[i] - c[i]);  // bf16(k - c), utils.py:261-265
+      for (int i = 0; i < 8; ++i) v[i] = rbf(v[i] - c[i]);  // bf16(k - c), utils.py:46-50
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] += v[i];

@@ -360,7 +360,7 @@ class ForwardPipeline:
 # ---------------------------------------------------------------------------
 def mean_pool(x: torch.Tensor, BLK: int, *, center: torch.Tensor | None = None) -> torch.Tensor:
     """Block mean pooling of ``x [B, H, L, D]`` -> ``[B, H, NB, D]``
-    (sparkdiffusion/ops/fused_kernel/utils.py:272-297)."""
+    (sparkdiffusion/ops/fused_kernel/utils.py:57-82)."""
     _require_cuda(x, center)
     B, H, L, D = x.shape
     if D != HEAD_DIM:

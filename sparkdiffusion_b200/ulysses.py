@@ -172,7 +172,7 @@ def _gemm_scatter_overlapped(x_local, w_qkv, b_qkv, nwq, nwk, gw, gb, xc, H, p, 
 def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk,
                                   proj_q, proj_k, gate_w, gate_b, num_heads: int, topk: int, group=None,
                                   eps: float = 1e-6, splits: int | None = None, events: dict | None = None,
-                                  transport: str = "peer", chunks: int | None = None):
+                                  transport: str = "peer", chunks: int | None = None, record: dict | None = None):
     """Sequence-sharded RoLa forward: ``x_local [B, Ls, H*D]`` on this rank ->
     ``[B, Ls, H*D]`` (excluding the output projection).  ``cos_sin`` and the
     low-rank tables cover the whole sequence (global positions).
@@ -182,7 +182,8 @@ def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin
     the same shapes and group, and consumers must run on the current stream.
     The peer transport overlaps the QKV GEMM with the scattering norm pass in
     token chunks (``chunk_plan``; ``chunks`` forces that many equal chunks,
-    1 turns the overlap off)."""
+    1 turns the overlap off).  ``record`` (a dict) receives this rank's LUT
+    (``lut``, int32 ``[B*Hl, NB, k]`` of heads ``rank*Hl ...``)."""
     if transport not in ("peer", "nccl"):
         raise ValueError(f"unknown transport {transport!r}")
     p = dist.get_world_size(group)
@@ -259,14 +260,21 @@ def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin
         slot = _out_slot.get(key, 0)
         _out_slot[key] = slot ^ 1
         rout = buf.region(f"out{slot}")
-        ops.head_local_attention(q_rope, k_rope, q_n, k_n, v, gate, pooled_q, ksum, lr_cos, lr_sin, rope_dim,
-                                 proj_q, proj_k, Hl, blk, topk, splits, events=events,
-                                 scatter=dict(dst=rout.table, world=p, head_offset=rank * Hl, H_total=H))
+        res = ops.head_local_attention(q_rope, k_rope, q_n, k_n, v, gate, pooled_q, ksum, lr_cos, lr_sin, rope_dim,
+                                       proj_q, proj_k, Hl, blk, topk, splits, keep=record is not None,
+                                       events=events,
+                                       scatter=dict(dst=rout.table, world=p, head_offset=rank * Hl, H_total=H))
+        if record is not None:
+            record["lut"] = res[1]["lut"]
         peer.stream_barrier(group)
         return rout.tensor
-    out_heads = ops.head_local_attention(q_rope, k_rope, q_n, k_n, v, gate, pooled_q, ksum, lr_cos, lr_sin,
-                                         rope_dim, proj_q, proj_k, Hl, blk, topk, splits, events=events)
-    return head_to_seq(out_heads, p, group)
+    res = ops.head_local_attention(q_rope, k_rope, q_n, k_n, v, gate, pooled_q, ksum, lr_cos, lr_sin,
+                                   rope_dim, proj_q, proj_k, Hl, blk, topk, splits, keep=record is not None,
+                                   events=events)
+    if record is not None:
+        res, extra = res
+        record["lut"] = extra["lut"]
+    return head_to_seq(res, p, group)
 
 
 def ulysses_rola_attention(layer, x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, nwq, nwk):

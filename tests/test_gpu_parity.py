@@ -207,23 +207,22 @@ def test_full_layer_from_x():
                                      gate_w=inp["gate_w"], gate_b=inp["gate_b"], num_heads=wl.H, blkq=wl.blk,
                                      blkk=wl.blk, topk=wl.topk)
     qkv = ex["qkv"].cpu()
+    # the GEMM: every q/k/v element within the bf16 rounding of the oracle's fp32-accumulated product
     assert_ulp_close(qkv[..., :dim], ref["q_raw"], "q_raw")
+    assert_ulp_close(qkv[..., dim:2 * dim], ref["k_raw"], "k_raw")
+    assert_ulp_close(qkv[..., 2 * dim:], ref["v_raw"], "v_raw")
     # selection from the GPU's own q/k is bit exact
     lut, *_ = orc.block_select(_heads(ex["q_rope"], wl), _heads(ex["k_rope"], wl), wl.blk, wl.blk, wl.topk)
     assert torch.equal(ex["lut"].cpu(), lut.reshape_as(ex["lut"].cpu()))
-    agree = (ex["lut"].cpu() == ref["lut"].reshape_as(ex["lut"].cpu())).all(-1).float().mean().item()
-    if agree == 1.0:
-        assert_bf16_close(out.cpu(), ref["out"].float(), "out", max_tol=6e-2)
-    # and the output is in tolerance against the oracle run with the GPU's LUT
-    ref2 = orc.rola_attention_forward(inp["x"], wq, None, wk, None, wv, None, cos_sin=cos_sin, lr_cos=lr_cos,
-                                      lr_sin=lr_sin, rope_dim=rope_dim, norm_wq=inp["norm_wq"],
-                                      norm_wk=inp["norm_wk"], proj_q=inp["proj_q"], proj_k=inp["proj_k"],
-                                      gate_w=inp["gate_w"], gate_b=inp["gate_b"], num_heads=wl.H, blkq=wl.blk,
-                                      blkk=wl.blk, topk=wl.topk, lut=ex["lut"].cpu(), out_dtype=torch.float32)
-    # end to end from x: the GEMM outputs already differ from the oracle's by bf16
-    # rounding flips, which the rest of the layer propagates; the mean-abs bound
-    # is the stated one, the max-abs bound allows those propagated flips.
-    assert_bf16_close(out.cpu(), ref2["out"], "out (GPU LUT)", max_tol=6e-2)
+    # everything after the GEMM, from the GPU's own projections (GEMM outputs that
+    # differ from the oracle's by one bf16 rounding step would otherwise propagate
+    # through the norm, the attention and the gate): the stated bound
+    ref2 = orc.rola_attention_core(qkv[..., :dim], qkv[..., dim:2 * dim], qkv[..., 2 * dim:], inp["x"], cos_sin,
+                                   lr_cos, lr_sin, rope_dim, inp["norm_wq"], inp["norm_wk"], inp["proj_q"],
+                                   inp["proj_k"], inp["gate_w"], inp["gate_b"], wl.H, wl.blk, wl.blk, wl.topk,
+                                   out_dtype=torch.float32)
+    assert torch.equal(ex["lut"].cpu(), ref2["lut"].reshape_as(ex["lut"].cpu()))
+    assert_bf16_close(out.cpu(), ref2["out"], "out (from the GPU's projections)")
 
 
 def test_topk_ties_lower_index():
@@ -367,9 +366,11 @@ def test_dense_attention_full_lut():
     lut = torch.arange(NB, dtype=torch.int32).expand(B * H, NB, NB).reshape(B, H, NB, NB)
     q4, k4, v4 = (t.view(B, H, L, 128) for t in (q, k, v))
     ref = orc.sparse_attn_lut(q4, k4, v4, lut, 128, 128, out_dtype=torch.float32)
-    # every query attends to all 600 keys: the output is an average over many
-    # values, so its RMS is small against the bf16 rounding of P and of the
-    # output; the mean bound is the stated one, the max bound is the
-    # end-to-end one (measured: max 2.85e-2, mean 1.11e-3 of the RMS)
-    assert_bf16_close(o.cpu(), ref, "dense attention", max_tol=6e-2)
+    # Every query averages all 600 values, so the output's largest elements sit
+    # ~4.5x above its RMS and one bf16 rounding step of them is already ~2e-2 of
+    # the RMS: the bound allows one step per element (ulp_floor), and element by
+    # element against the oracle rounded like the kernel's output at most 0.1 %
+    # of the elements may differ by more than one step.
+    assert_ulp_close(o.cpu(), ref.to(torch.bfloat16), "dense attention", ulps=1, max_frac=1e-3)
+    assert_bf16_close(o.cpu(), ref, "dense attention", ulp_floor=True)
 

@@ -1,0 +1,137 @@
+"""Parity against the reference's own bf16 fused path run on a B200.
+
+The fixtures ``tests/golden/ref_b200_{c2,c4}.pt`` hold what the unmodified
+SparkDiffusion fused inference path (``fused_qkv_gemm_rope`` or its epilogue
+kernel, ``fused_sparse_attn``, ``fused_lowrank``, ``fused_gate``, as
+``WanSelfAttentionRoLa.fused_forward`` chains them, wan_rola_attention.py:414-446)
+produced on a B200 for the seeded C2 and C4 inputs (``make_golden_b200.py``).
+Checked here, at the full BASELINE shapes:
+
+(i)   selection: per-row set agreement of this build's LUT with the reference's;
+      the reference scores in bf16 (fused_sparse_attn.py:181) where this build
+      scores in fp32, so a row may keep another block where the reference's bf16
+      scores cannot tell the two apart.  Every mismatch must be such a case: the
+      swapped blocks' reference bf16 scores lie within ``BOUNDARY_ULPS`` bf16
+      ulps of the reference's k-th score (0 ulps: an exact bf16 tie);
+(ii)  attention with the reference's LUT injected: o_sparse within the bf16
+      tolerance of the reference's o_sparse;
+(iii) the gated output with the reference's LUT injected, and with this build's
+      own LUT on the query blocks whose kept sets agree, within the bf16
+      tolerance of the reference's output.
+
+Outputs are compared on the fixture's seeded sample of token rows (all heads of
+C2, heads 0-3 of C4).  Tolerance: max-abs <= 2e-2 and mean-abs <= 2e-3 of the
+RMS of the reference's sampled output.
+"""
+
+import pytest
+import torch
+
+from conftest import BF16_MAX, BF16_MEAN, assert_bf16_close, assert_ulp_close
+from sparkdiffusion_b200 import _lib, ops, refcheck
+from sparkdiffusion_b200.rope import prepare_cos_sin, prepare_lowrank_cos_sin, wan_rope_freqs
+from sparkdiffusion_b200.workloads import C2, C4, make_inputs
+
+pytestmark = pytest.mark.gpu
+
+BOUNDARY_ULPS = 2
+
+
+def _load(name):
+    fx = refcheck.load_fixture(name)
+    assert fx is not None, f"fixture ref_b200_{name}.pt missing"
+    return fx
+
+
+def _checksum(t):
+    f = t.double()
+    return [float(f.sum()), float(f.abs().sum())]
+
+
+def _inputs(wl, fx):
+    inp = make_inputs(wl, device="cpu")
+    for k, v in fx["input_checksums"].items():
+        assert _checksum(inp[k]) == v, f"seeded input {k} differs from the one the fixture was made from"
+    freqs = wan_rope_freqs(*wl.grid)
+    cos_sin = prepare_cos_sin(freqs, wl.L, 128)
+    lr_cos, lr_sin, rope_dim = prepare_lowrank_cos_sin(freqs, wl.L, wl.rank, torch.bfloat16)
+    g = {k: (v.cuda() if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
+    return g, (cos_sin.cuda(), lr_cos.cuda(), lr_sin.cuda(), rope_dim)
+
+
+def _masked_close(got, ref, mask, name):
+    mx, mn = refcheck.rel_err(got, ref, mask)
+    assert mx <= BF16_MAX and mn <= BF16_MEAN, f"{name}: max-abs/rms={mx:.3e} mean-abs/rms={mn:.3e}"
+
+
+_sample_heads = refcheck.sample_heads
+_sample_out = refcheck.sample_out
+_agree_mask = refcheck.agree_mask
+
+
+def selection_report(lut, fx, heads):
+    return refcheck.selection_report(lut, fx, heads, BOUNDARY_ULPS)
+
+
+def test_c2_against_reference_b200():
+    wl = C2
+    fx = _load("c2")
+    B, L, H = wl.B, wl.L, wl.H
+    g, (cos_sin, lr_cos, lr_sin, rope_dim) = _inputs(wl, fx)
+    args = (g["q_raw"], g["k_raw"], g["v_raw"], g["x"], cos_sin, lr_cos, lr_sin, rope_dim, g["norm_wq"],
+            g["norm_wk"], g["proj_q"], g["proj_k"], g["gate_w"], g["gate_b"], H, wl.blk, wl.topk)
+    out, ex = ops.rola_attention_from_qkv(*args, keep=True)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    # the prologue agrees with the reference's epilogue kernel to the bf16 ulp
+    assert_ulp_close(_sample_heads(ex["q_rope"], fx, B, L, H, H), fx["q_rope"].float(), "q_rope vs reference")
+    # (i) selection
+    rep, agree = selection_report(ex["lut"], fx, H)
+    print(f"C2 selection vs reference: {rep}")
+    assert rep["unexplained"] == 0, rep
+    # (ii) attention and (iii) gated output with the reference's LUT injected
+    out_r, ex_r = ops.rola_attention_from_qkv(*args, keep=True, lut=fx["lut"].to(torch.int32).cuda())
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert_bf16_close(_sample_heads(ex_r["o_sparse"], fx, B, L, H, H), fx["o_sparse"].float(),
+                      "o_sparse (reference LUT) vs reference")
+    assert_bf16_close(_sample_out(out_r, fx, B, L, H), fx["out"].float(), "out (reference LUT) vs reference")
+    # (iii) own LUT, on the query blocks whose kept sets agree
+    _masked_close(_sample_out(out, fx, B, L, H), fx["out"].float(), _agree_mask(agree, fx, H, wl.blk),
+                  "out (own LUT, agreeing blocks) vs reference")
+
+
+def test_c4_against_reference_b200():
+    """C4 from the hidden states (all 40 heads through the prologue, whose norm
+    spans every head); heads 0-3 compared with the reference."""
+    wl = C4
+    fx = _load("c4")
+    hs = fx["config"]["H"]
+    B, L, H = wl.B, wl.L, wl.H
+    g, (cos_sin, lr_cos, lr_sin, rope_dim) = _inputs(wl, fx)
+    out, ex = ops.rola_attention_core(g["x"], g["w_qkv"], None, cos_sin, lr_cos, lr_sin, rope_dim, g["norm_wq"],
+                                      g["norm_wk"], g["proj_q"], g["proj_k"], g["gate_w"], g["gate_b"], H, wl.blk,
+                                      wl.topk, keep=True)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert_ulp_close(_sample_heads(ex["q_rope"], fx, B, L, H, hs), fx["q_rope"].float(), "q_rope vs reference",
+                     ulps=2, max_frac=2e-2)
+    rep, agree = selection_report(ex["lut"], fx, hs)
+    print(f"C4 selection vs reference (heads 0-{hs - 1}): {rep}")
+    assert rep["unexplained"] == 0, rep
+    # reference LUT injected for heads 0-3 (the other heads keep this build's)
+    lut = ex["lut"].clone().view(B * H, wl.NB, wl.topk)
+    lut[:hs] = fx["lut"].to(torch.int32).cuda()
+    qkv = ex["qkv"]
+    dim = wl.dim
+    out_r, ex_r = ops.rola_attention_from_qkv(qkv[..., :dim], qkv[..., dim:2 * dim], qkv[..., 2 * dim:], g["x"],
+                                              cos_sin, lr_cos, lr_sin, rope_dim, g["norm_wq"], g["norm_wk"],
+                                              g["proj_q"], g["proj_k"], g["gate_w"], g["gate_b"], H, wl.blk, wl.topk,
+                                              keep=True, lut=lut)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert_bf16_close(_sample_heads(ex_r["o_sparse"], fx, B, L, H, hs), fx["o_sparse"].float(),
+                      "o_sparse (reference LUT) vs reference")
+    assert_bf16_close(_sample_out(out_r, fx, B, L, hs), fx["out"].float(), "out (reference LUT) vs reference")
+    _masked_close(_sample_out(out, fx, B, L, hs), fx["out"].float(), _agree_mask(agree, fx, hs, wl.blk),
+                  "out (own LUT, agreeing blocks) vs reference")
