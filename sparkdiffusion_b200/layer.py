@@ -10,7 +10,10 @@ registered as ``"rola_b200"``.
 
 Inference only (the reference's fused path has the same gating,
 wan_rola_attention.py:467-477): the forward raises under autograd or on CPU
-tensors instead of falling back.
+tensors instead of falling back.  The kernels are reached through the custom
+operators ``torch.ops.rola_b200.*`` (``torch_ops``), so ``torch.compile`` of a
+model holding these layers captures each as one opaque node (meta tensors run
+the operators' shape functions only).
 """
 
 from __future__ import annotations
@@ -21,7 +24,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import ops
+from . import ops, torch_ops  # noqa: F401  (torch_ops registers torch.ops.rola_b200.*)
 from .registry import register_sparse_attn
 from .rope import prepare_cos_sin, prepare_lowrank_cos_sin
 
@@ -96,6 +99,9 @@ class WanSelfAttentionRoLaB200(nn.Module):
         self._pg = process_group
 
     def _fused_qkv(self):
+        if torch.compiler.is_compiling():  # traced: no data pointers, the concatenation is part of the graph
+            return (torch.cat([self.q.weight, self.k.weight, self.v.weight], 0).to(torch.bfloat16),
+                    torch.cat([self.q.bias, self.k.bias, self.v.bias], 0).to(torch.bfloat16))
         key = tuple((p.data_ptr(), p._version) for p in (self.q.weight, self.k.weight, self.v.weight,
                                                          self.q.bias, self.k.bias, self.v.bias))
         if self._qkv_cache is None or self._qkv_cache[0] != key:
@@ -108,7 +114,7 @@ class WanSelfAttentionRoLaB200(nn.Module):
         """Everything of the forward except the output projection."""
         if torch.is_grad_enabled() and self.training:
             raise RuntimeError("WanSelfAttentionRoLaB200 is inference-only (no backward kernels)")
-        if not x.is_cuda:
+        if x.device.type == "cpu":
             raise RuntimeError("WanSelfAttentionRoLaB200 runs on CUDA tensors only")
         if self.attn_precision != "bf16":
             raise ValueError("the B200 path implements attn_precision='bf16'")
@@ -135,12 +141,14 @@ class WanSelfAttentionRoLaB200(nn.Module):
             return ulysses_rola_attention(self, x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, nwq, nwk)
         NB = (L + 127) // 128
         topk = ops.topk_count(self.rola_topk_ratio, NB)
-        return ops.rola_attention_core(x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, nwq, nwk,
-                                       self.proj_q.weight, self.proj_k.weight, self.gate_proj.weight,
-                                       self.gate_bias, self.num_heads, 128, topk, self.eps)
+        return torch.ops.rola_b200.attention_core(x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, nwq, nwk,
+                                                  self.proj_q.weight, self.proj_k.weight, self.gate_proj.weight,
+                                                  self.gate_bias, self.num_heads, topk, self.eps)
 
     def _o_weight(self):
         """bf16 copy of the output projection for the tcgen05 GEMM (cached like the QKV weight)."""
+        if torch.compiler.is_compiling():
+            return self.o.weight.to(torch.bfloat16), self.o.bias.to(torch.bfloat16)
         key = (self.o.weight.data_ptr(), self.o.weight._version, self.o.bias.data_ptr(), self.o.bias._version)
         if self._o_cache is None or self._o_cache[0] != key:
             self._o_cache = (key, self.o.weight.to(torch.bfloat16).contiguous(),
@@ -154,7 +162,7 @@ class WanSelfAttentionRoLaB200(nn.Module):
         if dim % 256 == 0:
             # self.o (wan_rola_attention.py:447) on the same persistent tcgen05 GEMM as the QKV projection
             w, b = self._o_weight()
-            y = ops.qkv_gemm(out.reshape(B * L, dim), w, b).view(B, L, dim)
+            y = torch.ops.rola_b200.qkv_gemm(out.reshape(B * L, dim), w, b).view(B, L, dim)
             return y.to(self.o.weight.dtype)
         return F.linear(out.to(self.o.weight.dtype), self.o.weight, self.o.bias)
 
