@@ -340,6 +340,12 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       const uint32_t tO = tmem + 256 + 128 * t + lane_off;
       const int32_t* lut_row = p.lut + ((int64_t)bh * p.NBq + m0 + t) * topk;
       const float scale = p.qk_scale;
+      // the row's gate value (computed by the norm pass), loaded before the main
+      // loop so that its latency is hidden behind it
+      const int tok_row = (m0 + t) * 128 + row;
+      const float gate_pref = (p.has_lowrank && !p.has_x && p.gate != nullptr && tok_row < p.L)
+                                  ? bf2f(p.gate[((int64_t)b * p.L + tok_row) * p.H + h])
+                                  : 0.f;
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true;
       for (int i = 0; i < topk; ++i) {
@@ -502,8 +508,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             } else {
               ok = false;  // no gate for these rows: store nothing (the error flag is set)
             }
-          } else if (p.gate != nullptr && tok < p.L) {
-            gate = bf2f(p.gate[((int64_t)b * p.L + tok) * p.H + h]);
+          } else {
+            gate = gate_pref;
           }
         }
         // fuse from registers (os / os_rms as a product with the row's

@@ -107,11 +107,14 @@ int make_token_map(CUtensorMap* m, const void* ptr, int64_t cols, int64_t ld, in
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-// Two side streams per device for the forward's independent branches (the
-// low-rank C^T and q_lr run beside the selection chain), with fork/join events.
+// Side streams per device for the forward's three independent branches, with
+// fork/join events: the selection chain (centre, pooled k, scores + top-k) on a
+// stream of the device's greatest priority, so that the hardware dispatches its
+// few, latency-bound CTAs ahead of the many queued CTAs of the low-rank C^T and
+// q_lr kernels, which run on the other two.
 struct ForkJoin {
-  cudaStream_t side[2] = {nullptr, nullptr};
-  cudaEvent_t fork = nullptr, join[2] = {nullptr, nullptr};
+  cudaStream_t side[3] = {nullptr, nullptr, nullptr};  // low-rank kv, low-rank q, selection
+  cudaEvent_t fork = nullptr, join[3] = {nullptr, nullptr, nullptr};
   std::mutex mu;
 };
 ForkJoin g_forkjoin[64];
@@ -123,8 +126,10 @@ int forkjoin_get(ForkJoin** out) {
   ForkJoin& f = g_forkjoin[dev];
   std::lock_guard<std::mutex> lock(f.mu);
   if (f.fork == nullptr) {
-    for (int i = 0; i < 2 && e == cudaSuccess; ++i) {
-      e = cudaStreamCreateWithFlags(&f.side[i], cudaStreamNonBlocking);
+    int least = 0, greatest = 0;
+    e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+    for (int i = 0; i < 3 && e == cudaSuccess; ++i) {
+      e = cudaStreamCreateWithPriority(&f.side[i], cudaStreamNonBlocking, i == 2 ? greatest : least);
       if (e == cudaSuccess) e = cudaEventCreateWithFlags(&f.join[i], cudaEventDisableTiming);
     }
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&f.fork, cudaEventDisableTiming);
@@ -671,27 +676,28 @@ int rola_b200_rola_forward(const void* x, const void* w_qkv, const void* b_qkv, 
                                   gate_b, B, L, H, blk, eps, ws + f.q_rope, ws + f.k_rope, ws + f.q_normed,
                                   ws + f.k_normed, ws + f.gate, ws + f.pooled_q, reinterpret_cast<float*>(ws + f.ksum),
                                   stream));
-  // fork: the low-rank branches on two side streams, selection on `stream`
+  // fork: selection on the high-priority side stream (queued first), the
+  // low-rank branches on the other two
   ForkJoin* fj = nullptr;
   ROLA_TRY(forkjoin_get(&fj));
   std::lock_guard<std::mutex> lock(fj->mu);
   cudaError_t ce = cudaEventRecord(fj->fork, S(stream));
-  for (int i = 0; i < 2 && ce == cudaSuccess; ++i) ce = cudaStreamWaitEvent(fj->side[i], fj->fork, 0);
+  for (int i = 0; i < 3 && ce == cudaSuccess; ++i) ce = cudaStreamWaitEvent(fj->side[i], fj->fork, 0);
   if (ce != cudaSuccess) return fail(ROLA_ERR_CUDA, "rola_forward: %s", cudaGetErrorString(ce));
   const int64_t Ld = (int64_t)L * dim;
+  ROLA_TRY(rola_b200_center_from_sums(reinterpret_cast<float*>(ws + f.ksum), B, NB, (int)dim, L, ws + f.center,
+                                      fj->side[2]));
+  ROLA_TRY(rola_b200_mean_pool(ws + f.k_rope, (int64_t)L * dim, 128, dim, B, H, L, blk, ws + f.center,
+                               ws + f.pooled_k, fj->side[2]));
+  ROLA_TRY(rola_b200_block_select(ws + f.pooled_q, ws + f.pooled_k, B * H, NB, NB, topk,
+                                  reinterpret_cast<float*>(ws + f.scores), lut, fj->side[2]));
   ROLA_TRY(rola_b200_lowrank_kv(ws + f.k_normed, Ld, 128, dim, qkv + 2 * dim, 3 * Ld, 128, 3 * dim, proj_k, lr_cos,
                                 lr_sin, rope_dim, B, L, H, R, splits, reinterpret_cast<float*>(ws + f.c_partial),
                                 nullptr, ws + f.ct, fj->side[0]));
   ROLA_TRY(rola_b200_lowrank_q(ws + f.q_normed, Ld, 128, dim, proj_q, lr_cos, lr_sin, rope_dim, B, L, H, R,
                                ws + f.q_lr, fj->side[1]));
-  ROLA_TRY(rola_b200_center_from_sums(reinterpret_cast<float*>(ws + f.ksum), B, NB, (int)dim, L, ws + f.center,
-                                      stream));
-  ROLA_TRY(rola_b200_mean_pool(ws + f.k_rope, (int64_t)L * dim, 128, dim, B, H, L, blk, ws + f.center,
-                               ws + f.pooled_k, stream));
-  ROLA_TRY(rola_b200_block_select(ws + f.pooled_q, ws + f.pooled_k, B * H, NB, NB, topk,
-                                  reinterpret_cast<float*>(ws + f.scores), lut, stream));
   // join before the attention
-  for (int i = 0; i < 2 && ce == cudaSuccess; ++i) {
+  for (int i = 0; i < 3 && ce == cudaSuccess; ++i) {
     ce = cudaEventRecord(fj->join[i], fj->side[i]);
     if (ce == cudaSuccess) ce = cudaStreamWaitEvent(S(stream), fj->join[i], 0);
   }

@@ -34,11 +34,16 @@ _SIDE: dict = {}
 
 
 def _side_streams(dev) -> tuple:
-    """Two side streams per device for the concurrent head-local branches."""
+    """Three side streams per device for the concurrent head-local branches: the
+    low-rank C^T and q_lr at the lowest priority, the selection chain at the
+    device's greatest priority (the hardware then dispatches its few,
+    latency-bound CTAs ahead of the low-rank kernels' many queued ones)."""
     key = torch.device(dev).index if torch.device(dev).index is not None else torch.cuda.current_device()
     s = _SIDE.get(key)
     if s is None:
-        s = _SIDE[key] = (torch.cuda.Stream(device=key), torch.cuda.Stream(device=key))
+        least, greatest = torch.cuda.Stream.priority_range()
+        s = _SIDE[key] = (torch.cuda.Stream(device=key, priority=least), torch.cuda.Stream(device=key, priority=least),
+                          torch.cuda.Stream(device=key, priority=greatest))
     return s
 
 
@@ -140,11 +145,11 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
     out = e(B, L, dim) if scatter is None else None
     o_sparse = e(B, L, dim) if keep else None
     scores = None
-    # three independent branches run concurrently (each under-fills the GPU on
-    # its own): selection on this stream, the low-rank C^T and q_lr on two side
-    # streams; the attention waits for all three
+    # three independent branches run concurrently on side streams (each
+    # under-fills the GPU on its own): the selection chain (queued first, high
+    # priority), the low-rank C^T and q_lr; the attention waits for all three
     main = torch.cuda.current_stream(dev)
-    s_kv, s_q = _side_streams(dev)
+    s_kv, s_q, s_sel = _side_streams(dev)
     pq_, pk_ = proj_q.to(BF16).contiguous(), proj_k.to(BF16).contiguous()
     lc = None if lr_cos is None else lr_cos.to(BF16).contiguous()
     ls = None if lr_sin is None else lr_sin.to(BF16).contiguous()
@@ -155,6 +160,25 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
     # included) is on this stream
     s_kv.wait_stream(main)
     s_q.wait_stream(main)
+    s_sel.wait_stream(main)
+    for t in (center, pooled_k):
+        t.record_stream(s_sel)
+    lut_in = lut
+    if lut is None:
+        scores = e(B * H, NB, NB, dt=torch.float32) if NB > FUSED_SELECT_MAX_NB else None
+        lut = e(B * H, NB, topk, dt=torch.int32)
+        for t in (scores, lut):
+            if t is not None:
+                t.record_stream(s_sel)
+    else:
+        lut = lut.to(device=dev, dtype=torch.int32).reshape(B * H, NB, -1).contiguous()
+        topk = lut.shape[-1]
+    _lib.call("rola_b200_center_from_sums", _ptr(ksum), B, NB, dim, L, _ptr(center), s_sel.cuda_stream)
+    _lib.call("rola_b200_mean_pool", _ptr(k_rope), L * dim, HEAD_DIM, dim, B, H, L, blk, _ptr(center),
+              _ptr(pooled_k), s_sel.cuda_stream)
+    if lut_in is None:
+        _lib.call("rola_b200_block_select", _ptr(pooled_q), _ptr(pooled_k), B * H, NB, NB, topk, _ptr(scores),
+                  _ptr(lut), s_sel.cuda_stream)
     for t in (pq_, pk_, lc, ls):
         if t is not None:
             t.record_stream(s_kv)
@@ -168,17 +192,7 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
               s_kv.cuda_stream)
     _lib.call("rola_b200_lowrank_q", _ptr(q_normed), qs[0], HEAD_DIM, qs[1], _ptr(pq_), _ptr(lc), _ptr(ls),
               rope_dim, B, L, H, R, _ptr(q_lr), s_q.cuda_stream)
-    _lib.call("rola_b200_center_from_sums", _ptr(ksum), B, NB, dim, L, _ptr(center), st)
-    _lib.call("rola_b200_mean_pool", _ptr(k_rope), L * dim, HEAD_DIM, dim, B, H, L, blk, _ptr(center),
-              _ptr(pooled_k), st)
-    if lut is None:
-        scores = e(B * H, NB, NB, dt=torch.float32) if NB > FUSED_SELECT_MAX_NB else None
-        lut = e(B * H, NB, topk, dt=torch.int32)
-        _lib.call("rola_b200_block_select", _ptr(pooled_q), _ptr(pooled_k), B * H, NB, NB, topk, _ptr(scores),
-                  _ptr(lut), st)
-    else:
-        lut = lut.to(device=dev, dtype=torch.int32).reshape(B * H, NB, -1).contiguous()
-        topk = lut.shape[-1]
+    main.wait_stream(s_sel)
     main.wait_stream(s_kv)
     main.wait_stream(s_q)
     eps_lr = float(torch.finfo(BF16).eps)
