@@ -331,7 +331,9 @@ def gpu_reference_timing(wl, inp, dev, steps: int, warmup: int) -> dict:
 # ---------------------------------------------------------------------------
 def workload_desc(wl) -> str:
     return (f"{wl.name}: B={wl.B} H={wl.H} D=128 latent grid {wl.grid[0]}x{wl.grid[1]}x{wl.grid[2]} L={wl.L}, "
-            f"block {wl.blk} ({wl.NB} blocks), top-{wl.topk}, low-rank {wl.rank}, fused QKV from hidden states")
+            f"block {wl.blk} ({wl.NB} blocks), top-{wl.topk}, low-rank {wl.rank}, fused QKV from hidden states"
+            + (f"; a stack of {wl.layers} attention layers with distinct N(0,0.02) QKV weights per step, cond and "
+               f"uncond batched as B={wl.B} (the reference runs them as two B=1 calls)" if wl.layers > 1 else ""))
 
 
 def check_parity(args, wl, out1, lut1, step, x, rank, world, dev) -> dict:
@@ -343,7 +345,7 @@ def check_parity(args, wl, out1, lut1, step, x, rank, world, dev) -> dict:
       0-3 on sampled token rows): per-row LUT set agreement with every mismatch
       classified, and the output error on the agreeing rows.
     * At N > 1: this rank's Ulysses output rows and LUT (its head group) against
-      the 1-GPU forward's, max over ranks.
+      the 1-GPU forward's (bit for bit: ``lut_exact``, ``out_exact``), max over ranks.
     Bounds: LUT mismatches all explained (bf16 ties or boundary rounding of the
     reference's scores), output max-abs <= 2e-2 and mean-abs <= 2e-3 of the RMS."""
     from sparkdiffusion_b200 import refcheck
@@ -365,11 +367,12 @@ def check_parity(args, wl, out1, lut1, step, x, rank, world, dev) -> dict:
         ref_rows = out1[:, rank * Ls:(rank + 1) * Ls]
         mine = lut1.view(B, H, -1, lut1.shape[-1])[:, rank * Hl:(rank + 1) * Hl].reshape(rec["lut"].shape)
         mx, mn = refcheck.rel_err(o, ref_rows)
-        st = torch.tensor([float(not torch.equal(rec["lut"], mine)), mx, mn], dtype=torch.float64, device=dev)
+        st = torch.tensor([float(not torch.equal(rec["lut"], mine)), float(not torch.equal(o, ref_rows)), mx, mn],
+                          dtype=torch.float64, device=dev)
         dist.all_reduce(st, op=dist.ReduceOp.MAX)
-        bad, mx, mn = st.tolist()
-        res["vs_1gpu"] = {"lut_exact": bad == 0.0, "max_rel": mx, "mean_rel": mn,
-                          "ok": bad == 0.0 and mx <= 2e-2 and mn <= 2e-3}
+        bad_lut, bad_out, mx, mn = st.tolist()
+        res["vs_1gpu"] = {"lut_exact": bad_lut == 0.0, "out_exact": bad_out == 0.0, "max_rel": mx, "mean_rel": mn,
+                          "ok": bad_lut == 0.0 and mx <= 2e-2 and mn <= 2e-3}
     return res
 
 
@@ -433,28 +436,46 @@ def main():
     common = (cos_sin, lr_cos, lr_sin, rope_dim, inp["norm_wq"], inp["norm_wk"], inp["proj_q"], inp["proj_k"],
               inp["gate_w"].reshape(-1).contiguous(), inp["gate_b"].reshape(-1).to(torch.bfloat16))
 
+    # a stack of `layers` attention layers (C5: 40) with distinct random QKV
+    # weights ~ N(0, 0.02); every layer runs on the step's hidden states
+    layers = wl.layers
+    w_layers = [w_qkv]
+    for li in range(1, layers):
+        gl = torch.Generator(device=dev).manual_seed(1000 + li)
+        w_layers.append((torch.randn(3 * dim, dim, generator=gl, device=dev) * 0.02).to(torch.bfloat16))
+
     if world == 1:
-        def step(xin, events=None, record=None):
-            return ops.rola_attention_core(xin, w_qkv, None, *common, H, 128, wl.topk, events=events)
+        def layer_step(xin, li, events=None, record=None):
+            return ops.rola_attention_core(xin, w_layers[li], None, *common, H, 128, wl.topk, events=events)
     else:
         from sparkdiffusion_b200.ulysses import ulysses_rola_attention_params
 
-        def step(xin, events=None, record=None):
-            return ulysses_rola_attention_params(xin, w_qkv, None, *common, H, wl.topk, group, events=events,
+        def layer_step(xin, li, events=None, record=None):
+            return ulysses_rola_attention_params(xin, w_layers[li], None, *common, H, wl.topk, group, events=events,
                                                  transport=args.transport, chunks=args.chunks, record=record)
 
-    # exact selected-block FLOPs from this layer's LUT.  Every rank runs the
-    # 1-GPU pipeline once on the full hidden states (selection is bit-exact and
-    # identical to the head-sharded one), so no collective is needed here.
-    out1, ex = ops.rola_attention_core(inp["x"], w_qkv, None, *common, H, 128, wl.topk, keep=True)
-    flops_total = attn_flops_lut(ex["lut"], L, wl.blk)
-    lut1 = ex["lut"]
-    del ex
+    def step(xin, events=None):
+        for li in range(layers):
+            o = layer_step(xin, li, events=events if li == 0 else None)
+        return o
+
+    # exact selected-block FLOPs from each layer's LUT.  Every rank runs the
+    # 1-GPU pipeline once per layer on the full hidden states (selection is
+    # bit-exact and identical to the head-sharded one), so no collective is needed.
+    flops_layers = []
+    for li in range(layers):
+        o1, ex = ops.rola_attention_core(inp["x"], w_layers[li], None, *common, H, 128, wl.topk, keep=True)
+        flops_layers.append(attn_flops_lut(ex["lut"], L, wl.blk))
+        if li == 0:
+            out1, lut1 = o1, ex["lut"]
+        del o1, ex
+    flops_total = sum(flops_layers)
     torch.cuda.synchronize()
     if _lib.device_status() != 0:
         raise SystemExit("device-side error flag set during the LUT pass")
     torch.cuda.empty_cache()
-    parity = check_parity(args, wl, out1, lut1, step, x, rank, world, dev)
+    parity = check_parity(args, wl, out1, lut1, lambda xin, record: layer_step(xin, 0, record=record), x, rank,
+                          world, dev)
     del out1, lut1
     torch.cuda.empty_cache()
 
@@ -498,7 +519,7 @@ def main():
     if not args.no_e2e:
         x_host = x.cpu().pin_memory()
         out_host = torch.empty(B, Ls, dim, dtype=torch.bfloat16).pin_memory()
-        if world == 1:
+        if world == 1 and layers == 1:
             pipe = ops.ForwardPipeline(x_host.numel() * 2, out_host.numel() * 2)
 
             def e2e_step(i):
@@ -558,10 +579,10 @@ def main():
         e2e = {"value": flops_total / (t_e2e * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": t_e2e,
                "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
                "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
-               "api": ("rola_b200_pipeline_forward (C ABI, host buffers)" if world == 1
-                       else "ulysses_rola_attention_params"),
+               "api": ("rola_b200_pipeline_forward (C ABI, host buffers)" if world == 1 and layers == 1
+                       else "ops.rola_attention_core" if world == 1 else "ulysses_rola_attention_params"),
                "overlap": "uploads / downloads of neighbouring steps overlap each step's kernels"}
-        if world == 1:
+        if world == 1 and layers == 1:
             pipe.close()
 
     cpu_base = None
@@ -580,9 +601,9 @@ def main():
     # burst bf16 figure is the denominator; the sustained one is given beside it
     peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
     peak_sust = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
-    gemm_flops_local = 6.0 * B * Ls * dim * dim
+    gemm_flops_local = 6.0 * B * Ls * dim * dim  # t_gemm, t_attn: the first layer of each step
     gemm_ach = gemm_flops_local / (t_gemm * 1e-3) / 1e12
-    attn_ach = (flops_total / world) / (t_attn * 1e-3) / 1e12
+    attn_ach = (flops_layers[0] / world) / (t_attn * 1e-3) / 1e12
     dominant = "gemm" if t_gemm >= t_attn else "attn"
 
     def roof(name, ach):
@@ -608,16 +629,16 @@ def main():
         launches_per_step = 10
     line = {
         "metric": METRIC, "value": flops_total / (ms * 1e-3) / 1e12, "unit": UNIT, "n_gpus": world, "steps": K,
-        "warmup": args.warmup, "ms_per_step": ms, "ms_per_layer": ms, "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": ms, "ms_per_layer": ms / layers, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) hidden states, N(0,0.02) QKV weights, random low-rank/gate factors)",
-        "config": {"workload": workload_desc(wl), "global_batch": B, "seq_len": L,
+        "config": {"workload": workload_desc(wl), "global_batch": B, "seq_len": L, "layers": layers,
                    "parallelism": f"ulysses{world}" if world > 1 else "single",
                    "exchange": (f"fused into the norm pass and attention epilogue (peer stores), "
                                 f"GEMM/scatter overlap in {args.chunks or 'auto'} chunks"
                                 if args.transport == "peer" else "NCCL all_to_all_single") if world > 1 else None,
                    "l2": "inputs larger than L2 (hidden states 774 MB, QKV 2.3 GB per layer); no flush"},
-        "flops_per_layer": flops_total,
+        "flops_per_layer": flops_total / layers,
         "roofline": roof(dominant, gemm_ach if dominant == "gemm" else attn_ach),
         "roofline_attention": roof("attn", attn_ach),
         "roofline_gemm": roof("gemm", gemm_ach),
@@ -626,7 +647,7 @@ def main():
         "gpu_reference": gpu_ref,
         "parity": parity,
         "clocks": clk,
-        "gpu_launches": launches_per_step * K,
+        "gpu_launches": launches_per_step * layers * K,
         "device_status": status,
     }
     if rank == 0:

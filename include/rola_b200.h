@@ -181,7 +181,9 @@ int rola_b200_lowrank_q(const void* q_normed, int64_t sB, int64_t sH, int64_t sT
 /* (a9) C = k_lr^T v per (b, h).  k_normed and v are strided views as in
  * rola_b200_lowrank_q (k_s* and v_s* strides) -> C [B*H, R, D] and
  * Ct [B*H, D, R] bf16 (either may be NULL).  c_partial_ws: fp32 scratch of
- * splits*B*H*R*D floats.  R == 64.
+ * chunks*B*H*R*D floats, chunks = ceil(ceil(L/64)/16): one partial sum per
+ * 1024 tokens, added in order, so C is the same for any `splits` (the number
+ * of CTA columns of the reduction, a parallelism knob).  R == 64.
  * Replaces fused_lowrank.py:331-358 (k_lr projection + cuBLAS k_lr^T v). */
 int rola_b200_lowrank_kv(const void* k_normed, int64_t k_sB, int64_t k_sH, int64_t k_sT, const void* v, int64_t v_sB,
                          int64_t v_sH, int64_t v_sT, const void* proj_k, const void* lr_cos, const void* lr_sin,
@@ -236,8 +238,10 @@ int rola_b200_peer_free(void* ptr);
  * cudaFree (which may synchronise the device) is not acceptable, or a binding
  * with no CUDA allocator at hand.  The partials live in a fixed 16 MiB
  * (4 Mi fp32) array compiled into the library, held by every GPU that loads
- * the library until the process exits; splits*B*H*R*D must not exceed 4 Mi
- * (larger requests return ROLA_ERR_INVALID; C4 fits with splits <= 12).  The
+ * the library until the process exits; chunks*B*H*R*D (chunks as in
+ * rola_b200_lowrank_kv) must not exceed 4 Mi, i.e. at most 512 (chunk, batch,
+ * head) partials: C4 with 5 heads per GPU fits, all 40 heads do not (larger
+ * requests return ROLA_ERR_INVALID before any work).  The
  * first call on a device looks up the array's device address (issue it before
  * any stream capture on that device).  All calls share the array, so calls that
  * overlap on the GPU race; the array needs no clearing (every partial is

@@ -497,7 +497,7 @@ int rola_b200_lowrank_kv(const void* k_normed, int64_t k_sB, int64_t k_sH, int64
   p.rope_dim = rope_dim;
   p.splits = splits;
   ROLA_TRY(cuda_status(launch_lowrank_kv(p, S(stream)), "lowrank_kv"));
-  return cuda_status(launch_lowrank_reduce(c_partial_ws, splits, B * H, R, BFm(C), BFm(Ct), S(stream)),
+  return cuda_status(launch_lowrank_reduce(c_partial_ws, lowrank_chunks(L), B * H, R, BFm(C), BFm(Ct), S(stream)),
                      "lowrank_kv/reduce");
 }
 
@@ -637,7 +637,7 @@ static FwdLayout fwd_layout(int B, int L, int H, int blk, int R, int splits, int
   f.scores = take((size_t)B * H * NB * NB * 4);
   f.lut = take((size_t)B * H * NB * (size_t)topk * 4);
   f.q_lr = take(BL * H * R * 2);
-  f.c_partial = take((size_t)splits * B * H * R * 128 * 4);
+  f.c_partial = take((size_t)lowrank_chunks(L) * B * H * R * 128 * 4);
   f.ct = take((size_t)B * H * 128 * R * 2);
   f.total = off;
   return f;

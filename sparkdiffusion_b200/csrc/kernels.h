@@ -81,12 +81,15 @@ struct LowrankParams {
   const __nv_bfloat16* v;     // element (b,h,t,d) at v + b*v_sB + h*v_sH + t*v_sT + d
   int64_t v_sB, v_sH, v_sT;
   __nv_bfloat16* lr_out;      // q_lr: element (b,t,h,r) at lr_out + (b*L+t)*H*R + h*R + r
-  float* c_partial;           // [splits, B*H, R, D]
-  int B, L, H, R, rope_dim, splits;
+  float* c_partial;           // [lowrank_chunks(L), B*H, R, D]
+  int B, L, H, R, rope_dim, splits;  // splits: CTA columns of the C reduction
 };
+// C partials: one per chunk of kKvChunk 64-token tiles, [lowrank_chunks(L), B*H, R, D] fp32
+constexpr int kKvChunk = 16;
+inline int lowrank_chunks(int L) { return ((L + 63) / 64 + kKvChunk - 1) / kKvChunk; }
 int launch_lowrank_q(const LowrankParams& p, cudaStream_t s);
 int launch_lowrank_kv(const LowrankParams& p, cudaStream_t s);
-// C[bh, r, d] and Ct[bh, d, r] (bf16) from the fp32 partials (sequential over splits)
+// C[bh, r, d] and Ct[bh, d, r] (bf16) from the fp32 partials (sequential over the chunks)
 int launch_lowrank_reduce(const float* c_partial, int splits, int BH, int R, __nv_bfloat16* C, __nv_bfloat16* Ct,
                           cudaStream_t s);
 

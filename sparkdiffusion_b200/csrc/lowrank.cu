@@ -9,8 +9,9 @@
 //
 // These contractions are small (K = 128 or the 128-token block, N = rank), so
 // they use warp-level mma.sync m16n8k16 with ldmatrix fragments.  C is summed
-// over the sequence in `splits` fp32 partials (one per CTA column) that a
-// second kernel adds in a fixed order, so C is deterministic.
+// over the sequence in fp32 partials, one per fixed chunk of kKvChunk 64-token
+// tiles, that a second kernel adds in chunk order: C is deterministic and the
+// same for any number of CTA columns, so for any number of GPUs.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -215,14 +216,24 @@ __global__ void __launch_bounds__(256, 2) lowrank_kv_kernel(LowrankParams p) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) cacc[nt][e] = 0.f;
 
+  // This CTA column owns the chunks split, split + splits, ... of kKvChunk
+  // consecutive tiles; each chunk's sum goes to its own partial, so C's
+  // summation order depends only on L (not on the number of CTA columns, which
+  // follows the heads per GPU).
   const int ntiles = (p.L + kKvT - 1) / kKvT;
-  int tile = split;
+  const int nchunks = (ntiles + kKvChunk - 1) / kKvChunk;
+  auto next_tile = [&](int t) {  // the tile this CTA processes after tile t (ntiles when done)
+    if ((t + 1) % kKvChunk != 0 && t + 1 < ntiles) return t + 1;
+    const int c = t / kKvChunk + p.splits;
+    return c < nchunks ? c * kKvChunk : ntiles;
+  };
+  int tile = split < nchunks ? split * kKvChunk : ntiles;
   int buf = 0;
   if (tile < ntiles) kv_issue_tile(sX, sV, p, b, h, tile * kKvT);
   cp_async_commit();
   const int pm = warp & 3, pn = warp >> 2;  // projection: m-tile, rank half
-  for (; tile < ntiles; tile += p.splits, buf ^= 1) {
-    const int next = tile + p.splits;
+  for (; tile < ntiles; tile = next_tile(tile), buf ^= 1) {
+    const int next = next_tile(tile);
     if (next < ntiles) kv_issue_tile(sX + (buf ^ 1) * kKvTile, sV + (buf ^ 1) * kKvTile, p, b, h, next * kKvT);
     cp_async_commit();
     cp_async_wait_1();  // this tile has landed (the next may still be in flight)
@@ -295,17 +306,22 @@ __global__ void __launch_bounds__(256, 2) lowrank_kv_kernel(LowrankParams p) {
         mma16816(cacc[2 * np + 1], a0, a1, a2, a3, b2, b3);
       }
     }
+    if ((tile + 1) % kKvChunk == 0 || tile + 1 == ntiles) {
+      // last tile of a chunk: its sum goes to the chunk's partial
+      float* dst = p.c_partial + (((int64_t)(tile / kKvChunk) * p.B * p.H + bh) * 64) * 128;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int d = pn * 64 + nt * 8 + tig * 2;
+        const int r0 = pm * 16 + g;
+        *reinterpret_cast<float2*>(dst + r0 * 128 + d) = make_float2(cacc[nt][0], cacc[nt][1]);
+        *reinterpret_cast<float2*>(dst + (r0 + 8) * 128 + d) = make_float2(cacc[nt][2], cacc[nt][3]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) cacc[nt][e] = 0.f;
+      }
+    }
     __syncthreads();  // both tiles of this buffer consumed before it is refilled
   }
   cp_async_wait_0();
-  float* dst = p.c_partial + (((int64_t)split * p.B * p.H + bh) * 64) * 128;
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    const int d = pn * 64 + nt * 8 + tig * 2;
-    const int r0 = pm * 16 + g;
-    *reinterpret_cast<float2*>(dst + r0 * 128 + d) = make_float2(cacc[nt][0], cacc[nt][1]);
-    *reinterpret_cast<float2*>(dst + (r0 + 8) * 128 + d) = make_float2(cacc[nt][2], cacc[nt][3]);
-  }
 }
 
 __global__ void lowrank_reduce_kernel(const float* __restrict__ part, int splits, int BH, int R,

@@ -64,11 +64,11 @@ extern "C" int rola_b200_lowrank_kv_noalloc(const void* k_normed, int64_t k_sB, 
                                             int B, int L, int H, int R, int splits, void* C, void* Ct,
                                             rola_stream_t stream) {
   using namespace rola;
-  ROLA_CHECK(B > 0 && H > 0 && R > 0 && splits > 0, "lowrank_kv_noalloc: bad sizes");
-  const size_t need = (size_t)splits * B * H * R * 128;
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && R > 0 && splits > 0, "lowrank_kv_noalloc: bad sizes");
+  const size_t need = (size_t)lowrank_chunks(L) * B * H * R * 128;
   ROLA_CHECK(need <= kNoallocScratchFloats,
-             "lowrank_kv_noalloc: splits*B*H*R*D = %zu fp32 partials exceed the fixed scratch of %zu "
-             "(16 MiB); lower splits or use rola_b200_lowrank_kv with a workspace",
+             "lowrank_kv_noalloc: chunks*B*H*R*D = %zu fp32 partials (one per 1024 tokens) exceed the fixed "
+             "scratch of %zu (16 MiB); use rola_b200_lowrank_kv with a workspace",
              need, kNoallocScratchFloats);
   float* scratch = nullptr;
   ROLA_TRY(noalloc_scratch(&scratch));

@@ -77,12 +77,19 @@ def topk_count(topk_ratio: float, nb: int) -> int:
     return max(1, min(nb, int(topk_ratio * nb)))
 
 
+LOWRANK_CHUNK_TILES = 16  # 64-token tiles per fp32 partial of C (kKvChunk in csrc/kernels.h)
+
+
+def lowrank_chunks(L: int) -> int:
+    """Fp32 partials of the low-rank C reduction: one per 1024 tokens."""
+    return ((L + 63) // 64 + LOWRANK_CHUNK_TILES - 1) // LOWRANK_CHUNK_TILES
+
+
 def default_splits(B: int, H: int, L: int) -> int:
-    """Sequence splits of the low-rank C reduction: one wave of two CTAs per
-    SM (64-token tiles)."""
-    tiles = (L + 63) // 64
+    """CTA columns of the low-rank C reduction: one wave of two CTAs per SM.
+    (C itself does not depend on it: its partials follow fixed token chunks.)"""
     sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    return max(1, min(tiles, (2 * sms) // (B * H)))
+    return max(1, min(lowrank_chunks(L), (2 * sms) // (B * H)))
 
 
 # ---------------------------------------------------------------------------
@@ -139,7 +146,7 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
     center = e(B, H, HEAD_DIM)
     pooled_k = e(B, H, NB, HEAD_DIM)
     q_lr = e(B, L, H * R)
-    c_part = e(splits, B * H, R, HEAD_DIM, dt=torch.float32)
+    c_part = e(lowrank_chunks(L), B * H, R, HEAD_DIM, dt=torch.float32)
     C = e(B * H, R, HEAD_DIM) if keep else None
     Ct = e(B * H, HEAD_DIM, R)
     out = e(B, L, dim) if scatter is None else None

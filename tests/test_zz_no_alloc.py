@@ -56,7 +56,8 @@ def test_noalloc_matches_allocating_entry_point_twice():
     second = _case(2, 2, (2, 10, 20), seed=2)  # different shape and batch
     for case, splits in ((first, 6), (second, 3)):
         k, v, pk, cos, sin, rope_dim, B, L, H = case
-        scratch = torch.empty(splits * B * H * 64 * 128, dtype=torch.float32, device="cuda")
+        chunks = ((L + 63) // 64 + 15) // 16  # one fp32 partial of C per 1024 tokens
+        scratch = torch.empty(chunks * B * H * 64 * 128, dtype=torch.float32, device="cuda")
         C_ref, Ct_ref = _run("rola_b200_lowrank_kv", case, splits, scratch)
         C, Ct = _run("rola_b200_lowrank_kv_noalloc", case, splits)
         torch.cuda.synchronize()
@@ -70,6 +71,9 @@ def test_noalloc_matches_allocating_entry_point_twice():
 def test_noalloc_rejects_requests_beyond_the_scratch():
     case = _case(1, 4, (2, 8, 16), seed=3)
     k, v, pk, cos, sin, rope_dim, B, L, H = case
-    too_many = SCRATCH_FLOATS // (B * H * 64 * 128) + 1
-    with pytest.raises(ValueError, match="exceed the fixed scratch"):
-        _run("rola_b200_lowrank_kv_noalloc", case, too_many)
+    # a sequence with more 1024-token chunks than the scratch holds partials
+    # for: refused by the size check before any memory is touched
+    max_chunks = SCRATCH_FLOATS // (B * H * 64 * 128)
+    too_long = (k, v, pk, cos, sin, rope_dim, B, (max_chunks + 1) * 1024, H)
+    with pytest.raises(ValueError, match="exceed the fixed"):
+        _run("rola_b200_lowrank_kv_noalloc", too_long, 4)
