@@ -141,8 +141,9 @@ class ClockSampler:
 PRO_SAMPLE_TOKENS = 1024
 
 
-def cpu_sample_seconds(wl) -> tuple[float, str, int]:
-    """Seconds of one extrapolated layer on the host cores, the sample text and the thread count."""
+def cpu_sample_seconds(wl) -> tuple[float, str, int, float]:
+    """Seconds of one extrapolated layer on the host cores, the sample text, the
+    thread count and the seconds actually measured (the sample itself)."""
     from oracle import rola_oracle as orc
 
     threads = len(os.sched_getaffinity(0))
@@ -182,7 +183,7 @@ def cpu_sample_seconds(wl) -> tuple[float, str, int]:
     sample = (f"CPU oracle port (torch, fp32 math with the reference's bf16 rounding points): prologue on "
               f"{n} of {wl.B * L} tokens (x{wl.B * L / n:.1f}) + selection/sparse attention/low-rank/gate for 1 of "
               f"{wl.B * H} (batch, head) pairs over all {L} tokens (x{wl.B * H})")
-    return total, sample, threads
+    return total, sample, threads, t_pro + t_head
 
 
 def run_reference(args, wl, rank):
@@ -190,18 +191,26 @@ def run_reference(args, wl, rank):
         return
     for _ in range(args.warmup):
         cpu_sample_seconds(wl)
-    secs = []
+    secs, measured = [], []
     sample = ""
     threads = 0
     for _ in range(args.steps):
-        s, sample, threads = cpu_sample_seconds(wl)
+        s, sample, threads, m = cpu_sample_seconds(wl)
         secs.append(s)
+        measured.append(m)
     t = statistics.median(secs)
+    t_meas = statistics.median(measured)
     flops = wl.attn_flops()
     value = flops / t / 1e12
+    # each step times a bounded sample of the layer (the timed region is the
+    # sample: ms_per_step); the layer time and the metric are extrapolated
+    # from it, as `extrapolated` states
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "ms_per_layer": t * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_meas * 1e3, "ms_per_layer": t * 1e3,
+        "extrapolated": {"measured_ms_per_step": t_meas * 1e3, "layer_ms": t * 1e3, "factor": t / t_meas,
+                         "how": "prologue timed on a token sample and scaled by tokens; one (batch, head) of "
+                                "selection/attention/low-rank/gate over the full sequence, scaled by heads"},
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded random hidden states and weights)",
         "config": {"workload": workload_desc(wl), "global_batch": wl.B, "seq_len": wl.L},
@@ -587,7 +596,7 @@ def main():
 
     cpu_base = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        runs = [cpu_sample_seconds(wl) for _ in range(3)]
+        runs = [cpu_sample_seconds(wl)[:3] for _ in range(3)]
         secs = statistics.median(r[0] for r in runs)
         sample, threads = runs[0][1] + " (median of 3)", runs[0][2]
         cpu_base = {"value": flops_total / secs / 1e12, "unit": UNIT, "cores": threads, "kind": "port",

@@ -50,6 +50,15 @@ const char* rola_b200_last_error(void);
  * Synchronises the device.  Returns the ROLA_DEV_* code, or -1 on a CUDA error. */
 int rola_b200_device_status(int clear);
 
+/* Self-test of the device-side failure detection (no counterpart in the
+ * reference).  Launches one thread that waits on an mbarrier nothing completes,
+ * with a wall-time limit of limit_us microseconds (1 .. 1e6): the wait gives
+ * up, records ROLA_DEV_TIMEOUT_LOAD in the device error flag and the kernel
+ * returns.  Synchronises `stream`; returns ROLA_OK when the wait gave up as it
+ * must.  Afterwards rola_b200_device_status() reports the code and the
+ * context remains usable. */
+int rola_b200_check_wait_timeout(unsigned limit_us, rola_stream_t stream);
+
 /* (a4) QKV projection: out[M, N] (row stride N) = x[M, K] . w[N, K]^T + bias[N].
  * bias may be NULL.  N % 256 == 0, K % 64 == 0.  ssq (NULL to skip): fp32
  * [M, N/256], the sum of squares of each row's bf16 outputs per 256-column

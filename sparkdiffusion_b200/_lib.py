@@ -40,6 +40,7 @@ SIGNATURES = {
     "rola_b200_abi_version": [],
     "rola_b200_last_error": [],
     "rola_b200_device_status": [_I],
+    "rola_b200_check_wait_timeout": [ctypes.c_uint, _P],
     "rola_b200_qkv_gemm": [_P, _P, _P, _P, _P, _L, _L, _L, _P],
     "rola_b200_qk_norm_rope": [_P, _P, _L, _P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F,
                                _P, _P, _P, _P, _P, _P, _P, _P],

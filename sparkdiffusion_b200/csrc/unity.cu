@@ -10,3 +10,4 @@
 #include "peer.cu"
 #include "pipeline.cu"
 #include "noalloc.cu"
+#include "health.cu"
