@@ -69,6 +69,26 @@ int rola_b200_check_wait_timeout(unsigned limit_us, rola_stream_t stream);
 int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out, float* ssq, int64_t M, int64_t N,
                        int64_t K, rola_stream_t stream);
 
+/* (f1) Row-wise FP8 (e4m3) quantization of a bf16 [M, K] matrix with row
+ * stride ld: scale[m] = max_k |x[m,k]| / 448 + 1e-12 (fp32) and
+ * xq[m, k] = e4m3(bf16(x[m,k] / bf16(scale[m]))), xq dense [M, K] bytes.
+ * K % 8 == 0.  For the activations per token, and (once) for the QKV weight
+ * per output channel.
+ * Replaces quantize_activation_rowwise / quantize_weight_rowwise
+ * (sparkdiffusion/ops/quantization/fp8_linear.py:45-61). */
+int rola_b200_quantize_rows_e4m3(const void* x, int64_t ld, int64_t M, int64_t K, void* xq, float* scale,
+                                 rola_stream_t stream);
+
+/* (f1) FP8 QKV projection: out[M, N] (bf16, row stride N) =
+ * bf16((xq . wq^T)[m, n] * x_scale[m] * w_scale[n] + bias[n]), e4m3 operands
+ * from rola_b200_quantize_rows_e4m3 (xq [M, K], wq [N, K]), fp32 accumulation.
+ * bias may be NULL.  N % 256 == 0, K % 128 == 0.  ssq as rola_b200_qkv_gemm.
+ * Replaces the three torch._scaled_mm calls of fused_qkv_gemm_rope's FP8 mode
+ * (sparkdiffusion/ops/fused_kernel/fused_qkv_rope.py:270-285). */
+int rola_b200_qkv_gemm_fp8(const void* xq, const float* x_scale, const void* wq, const float* w_scale,
+                           const void* bias, void* out, float* ssq, int64_t M, int64_t N, int64_t K,
+                           rola_stream_t stream);
+
 /* (a4 epilogue, a5 q-pool, a6 block sums, a10 gate) in one pass over the rows.
  * q_raw/k_raw: token-major, row stride ld_raw.  ssq (optional): the
  * [B*L, ssq_ld] sums of squares written by rola_b200_qkv_gemm over the q|k|v
@@ -179,6 +199,16 @@ int rola_b200_center_from_sums(const float* ksum, int B, int NB, int dim, int L,
 int rola_b200_block_select(const void* pooled_q, const void* pooled_k, int BH, int NBq, int NBk, int topk,
                            float* scores_ws, int32_t* lut, rola_stream_t stream);
 
+/* Block size 64: per 128-row query tile t (query blocks 2t and 2t + 1 of a
+ * 64-token selection lut [BH, NB, topk], rows in any order), the ascending
+ * union of the two blocks' kept key blocks, padded with -1 to 2*topk entries,
+ * bits 28 and 29 of each entry marking which of the two blocks selected it,
+ * preceded by the number of 128-column key tiles (entry pairs) it needs:
+ * paired [BH, ceil(NB/2), 2*topk + 1] int32, the lut of rola_b200_sparse_attn
+ * with blk == 64.  No counterpart in the reference (its Triton kernel takes
+ * 64-row query blocks directly, fused_sparse_attn.py:204-213). */
+int rola_b200_pair_blocks(const int32_t* lut, int BH, int NB, int topk, int32_t* paired, rola_stream_t stream);
+
 /* (a9) q_lr = RoPE_rank(SiLU(q_normed . proj_q^T)).  Element (b, h, t, d) of
  * q_normed sits at q_normed + sB*b + sH*h + sT*t + d (elements; 16-byte rows).
  * proj_q [R, D], lr_cos/lr_sin [L, rope_dim] bf16 -> q_lr [B*L, H*R] bf16.  R == 64.
@@ -208,7 +238,11 @@ int rola_b200_lowrank_kv(const void* k_normed, int64_t k_sB, int64_t k_sH, int64
  * epilogue from the hidden states x (strided like q, x_s*) with gate_w [D] and
  * gate_b [H] bf16 (give one of gate / x; neither: gate 0).  out / o_sparse may
  * be NULL (not both).
- * blk == 128, R == 64.
+ * blk == 128: lut is the selection [B*H, NB, topk].  blk == 64 (the
+ * reference's default rola_blkq = rola_blkk = 64): lut is the paired table of
+ * rola_b200_pair_blocks for the 64-token selection [B*H, NB64, topk]; each
+ * 128-row query tile then attends to the union of its two blocks' key blocks,
+ * every row only to its own block's.  R == 64.
  * Replaces _rola_fwd_kernel (fused_sparse_attn.py:55-144), the o_lr matmul
  * (fused_lowrank.py:360-362) and _gate_fusion_kernel (fused_gate.py:27-127). */
 int rola_b200_sparse_attn(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT, const void* v,

@@ -162,6 +162,26 @@ def qkv_linear(x, w, b=None, out_dtype=None):
     return y.to(out_dtype or x.dtype)
 
 
+def quantize_rows_e4m3(x2: torch.Tensor):
+    """Row-wise FP8 quantization, the reference's quantize_activation_rowwise /
+    quantize_weight_rowwise (sparkdiffusion/ops/quantization/fp8_linear.py:45-61):
+    scale = amax|row| (of the bf16 values) / 448 + 1e-12 in fp32; q =
+    e4m3(bf16(x / bf16(scale))).  Returns (q float8_e4m3fn, scale fp32 [M])."""
+    scale = x2.abs().amax(dim=1, keepdim=True).float() / 448.0 + 1e-12
+    q = (x2 / scale.to(x2.dtype)).to(torch.float8_e4m3fn)
+    return q, scale.reshape(-1)
+
+
+def scaled_mm_rowwise(xq, x_scale, wq, w_scale, bias=None, out_dtype=torch.bfloat16):
+    """torch._scaled_mm(xq, wq.t(), scale_a=x_scale[:, None], scale_b=w_scale[None, :],
+    bias, out_dtype) as the reference's FP8 prologue calls it (fused_qkv_rope.py:274-285):
+    fp32 products of the e4m3 values, times both scales, plus the bias."""
+    y = (xq.to(F32) @ wq.to(F32).t()) * x_scale.reshape(-1, 1).to(F32) * w_scale.reshape(1, -1).to(F32)
+    if bias is not None:
+        y = y + bias.to(F32)
+    return y.to(out_dtype)
+
+
 def fused_qkv_gemm_rope(x, wq, bq, wk, bk, wv, bv, cos_sin, norm_wq, norm_wk, num_heads, eps=1e-6):
     """fused_qkv_rope.py:228-333 (bf16 branch): three linears, then the epilogue."""
     q_raw = qkv_linear(x, wq, bq)

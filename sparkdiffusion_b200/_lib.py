@@ -42,6 +42,8 @@ SIGNATURES = {
     "rola_b200_device_status": [_I],
     "rola_b200_check_wait_timeout": [ctypes.c_uint, _P],
     "rola_b200_qkv_gemm": [_P, _P, _P, _P, _P, _L, _L, _L, _P],
+    "rola_b200_quantize_rows_e4m3": [_P, _L, _L, _L, _P, _P, _P],
+    "rola_b200_qkv_gemm_fp8": [_P, _P, _P, _P, _P, _P, _P, _L, _L, _L, _P],
     "rola_b200_qk_norm_rope": [_P, _P, _L, _P, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F,
                                _P, _P, _P, _P, _P, _P, _P, _P],
     "rola_b200_qk_norm_pack": [_P, _P, _P, _L, _P, _I, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F,
@@ -53,6 +55,7 @@ SIGNATURES = {
     "rola_b200_smooth_k_center": [_P, _L, _L, _L, _I, _I, _I, _I, _P, _P, _P],
     "rola_b200_center_from_sums": [_P, _I, _I, _I, _I, _P, _P],
     "rola_b200_block_select": [_P, _P, _I, _I, _I, _I, _P, _P, _P],
+    "rola_b200_pair_blocks": [_P, _I, _I, _I, _P, _P],
     "rola_b200_lowrank_q": [_P, _L, _L, _L, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P],
     "rola_b200_lowrank_kv": [_P, _L, _L, _L, _P, _L, _L, _L, _P, _P, _P, _I, _I, _I, _I, _I, _I,
                              _P, _P, _P, _P],

@@ -26,12 +26,14 @@
 //                   Per KV block the whole S row is loaded at once, the row max
 //                   taken, the row's O rescale factor published, and
 //                   P = exp2(s*scale - m) written back over the S columns as
-//                   packed bf16; then the fused epilogue.
+//                   packed bf16, handed to the MMA in chunks of 32 keys so that
+//                   P V starts while the rest of P is computed; then the fused
+//                   epilogue.
 //   WG3 (96)        correction: rescales O in TMEM by the published factors
 //                   while the softmax computes P (every growth of the running
 //                   max when `rescale_threshold` is 0: the reference's
-//                   recurrence exactly); the MMA issuer waits for P and the
-//                   corrected O before P V.
+//                   recurrence exactly); the MMA issuer waits for the
+//                   corrected O, then for each P chunk before its K steps.
 // TMEM columns: S/P of tile t at [128 t, 128 t + 128), O of tile t at
 // [256 + 128 t, ...); the epilogue's o_lr reuses the S columns.
 #include "common.cuh"
@@ -51,8 +53,9 @@ constexpr int NSLOTS = 5;
 constexpr int OFF_Q = 0;                    // 2 tiles x 2 boxes
 constexpr int OFF_RING = 4 * TILE;          // 5 slots
 constexpr int OFF_BAR = OFF_RING + NSLOTS * SLOT;  // 224 KB
-constexpr int OFF_ALPHA = OFF_BAR + 256;    // per-row O rescale factors of both tiles [2][128] fp32
+constexpr int OFF_ALPHA = OFF_BAR + 512;    // per-row O rescale factors of both tiles [2][128] fp32
 constexpr int SMEM_BYTES = OFF_ALPHA + 1024 + 1024;
+constexpr int PCHUNKS = 4;                  // P handed to the MMA in 4 chunks of 32 keys
 }  // namespace attn
 
 // barrier slots
@@ -61,14 +64,34 @@ enum : int {
   B_FULL0,                       // ring slot s full (TMA): B_FULL0 + s
   B_EMPTY0 = B_FULL0 + 5,        // ring slot s consumed (MMA commit): B_EMPTY0 + s
   B_SF0 = B_EMPTY0 + 5, B_SF1,   // S of tile t ready (MMA -> softmax)
-  B_PF0, B_PF1,                  // P of tile t in TMEM and O rescaled (softmax -> MMA), 4 arrivals
-  B_OF0, B_OF1,                  // last P V of tile t complete
+  B_PF0,                         // P chunk c of tile t in TMEM (softmax -> MMA): B_PF0 + 4 t + c, 4 arrivals
+  B_OF0 = B_PF0 + 8, B_OF1,      // last P V of tile t complete
   B_LR0, B_LR1,                  // o_lr of tile t in TMEM
   B_AR0, B_AR1,                  // rescale factors of tile t published (softmax -> correction), 4 arrivals
   B_OC0, B_OC1,                  // O of tile t rescaled (correction -> MMA), 4 arrivals
   B_DRAIN,
   B_COUNT
 };
+// barriers, then the abort flag, the TMEM address and the epilogue's per-warp flags
+static_assert(8 * B_COUNT + 16 + 32 <= attn::OFF_ALPHA - attn::OFF_BAR, "barrier region too small");
+
+// block size 64: one entry of a tile's paired union (launch_pair_blocks) -> the
+// key block (padding -1 -> block 0, which the softmax masks out entirely)
+__device__ __forceinline__ int pair_block(const AttnParams& p, int32_t e) {
+  if (e < 0) return 0;
+  int j = e & 0x0fffffff;
+  if (j >= p.NBk) {
+    set_device_error(kDevBadIndex);
+    j = p.NBk - 1;
+  }
+  return j;
+}
+// valid columns (0..64) of the 64-column half holding entry e, for a row of
+// query block `half` (0 or 1) of the tile: none unless that block selected it
+__device__ __forceinline__ int pair_valid(const AttnParams& p, int32_t e, int half) {
+  if (e < 0 || !((e >> (28 + half)) & 1)) return 0;
+  return min(64, p.L - (e & 0x0fffffff) * 64);
+}
 
 __device__ __forceinline__ int lut_block(const AttnParams& p, const int32_t* lut_row, int i) {
   int j = lut_row[i];
@@ -97,9 +120,21 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
-  const int m0 = 2 * blockIdx.x;
-  const int nt = (m0 + 1 < p.NBq) ? 2 : 1;  // active tiles
-  const int topk = p.topk;
+  const int m0 = 2 * blockIdx.x;                              // first 128-row query tile
+  const int NQT = p.blk64 ? (p.NBq + 1) / 2 : p.NBq;           // 128-row query tiles
+  const int nt = (m0 + 1 < NQT) ? 2 : 1;  // active tiles
+  // Row of tile t in p.lut: the LUT row (block 128) or the tile's paired union
+  // (block 64: the count, then 2k entries).  Main-loop iterations: the LUT
+  // length, or for block 64 the larger key-tile count of the two tiles (the
+  // other tile's extra key tiles are padding and fully masked).
+  const int ent = p.blk64 ? 2 * p.topk + 1 : p.topk;
+  auto tile_row = [&](int t) { return p.lut + ((int64_t)bh * NQT + m0 + t) * ent + (p.blk64 ? 1 : 0); };
+  int topk = p.topk;
+  if (p.blk64) {
+    topk = tile_row(0)[-1];
+    if (nt == 2) topk = max(topk, tile_row(1)[-1]);
+    topk = max(1, min(topk, p.topk));
+  }
 
   if (threadIdx.x == 0) {
     mbar_init(bar(B_Q), 1);
@@ -109,7 +144,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(B_SF0 + t), 1);
-      mbar_init(bar(B_PF0 + t), 4);
+      for (int c = 0; c < PCHUNKS; ++c) mbar_init(bar(B_PF0 + PCHUNKS * t + c), 4);
       mbar_init(bar(B_OF0 + t), 1);
       mbar_init(bar(B_LR0 + t), 1);
       mbar_init(bar(B_AR0 + t), 4);
@@ -163,9 +198,20 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         const uint32_t dst = acquire(SLOT);
         if (!ok) return;
         const int s = r % NSLOTS;
-        const int j = lut_block(p, p.lut + ((int64_t)bh * p.NBq + m0 + t) * topk, i);
-        tma_load_4d(dst, m, bar(B_FULL0 + s), 0, j * 128, h, b);
-        tma_load_4d(dst + TILE, m, bar(B_FULL0 + s), 64, j * 128, h, b);
+        if (!p.blk64) {
+          const int j = lut_block(p, tile_row(t), i);
+          tma_load_4d(dst, m, bar(B_FULL0 + s), 0, j * 128, h, b);
+          tma_load_4d(dst + TILE, m, bar(B_FULL0 + s), 64, j * 128, h, b);
+        } else {
+          // two 64-row key blocks stacked into one 128-row block (64-row boxes;
+          // the 128-byte swizzle follows the address, so the halves line up)
+          const int32_t* row = tile_row(t);
+          const int j0 = pair_block(p, row[2 * i]), j1 = pair_block(p, row[2 * i + 1]);
+          tma_load_4d(dst, m, bar(B_FULL0 + s), 0, j0 * 64, h, b);
+          tma_load_4d(dst + TILE / 2, m, bar(B_FULL0 + s), 0, j1 * 64, h, b);
+          tma_load_4d(dst + TILE, m, bar(B_FULL0 + s), 64, j0 * 64, h, b);
+          tma_load_4d(dst + TILE + TILE / 2, m, bar(B_FULL0 + s), 64, j1 * 64, h, b);
+        }
         ++r;
       };
       for (int t = 0; t < nt && ok; ++t) load_block(&tk, t, 0);
@@ -242,20 +288,31 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       for (int t = 0; t < nt && ok; ++t) issue_s(t);
       for (int i = 0; i < topk && ok; ++i) {
         for (int t = 0; t < nt && ok; ++t) {
-          if (!mbar_wait(bar(B_PF0 + t), i & 1, abort_flag, kDevTimeoutSoftmax) ||
-              !mbar_wait(bar(B_OC0 + t), i & 1, abort_flag, kDevTimeoutSoftmax)) {
+          if (!mbar_wait(bar(B_OC0 + t), i & 1, abort_flag, kDevTimeoutSoftmax)) {
             ok = false;
             break;
           }
           const int e = pop();
           if (e < 0) break;
           const uint32_t sv = slot_addr(e);
+          // P V in the order the softmax hands P over: the K steps of chunk c
+          // (32 keys) start as soon as that chunk is in TMEM, so most of P V
+          // runs under the softmax's exp2 work instead of after it
+          for (int c = 0; c < PCHUNKS && ok; ++c) {
+            if (!mbar_wait(bar(B_PF0 + PCHUNKS * t + c), i & 1, abort_flag, kDevTimeoutSoftmax)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            // A = P from TMEM (16 bf16 of K = 8 packed columns per step), B = V (MN-major)
-            mma_bf16_ts(tmem + 256 + 128 * t, tmem + 128 * t + kk * 8, sdesc_sw128(sv + kk * 2048, TILE, 1024),
-                        id_pv, (i > 0 || kk > 0) ? 1u : 0u);
+            for (int k2 = 0; k2 < 2; ++k2) {
+              // A = P from TMEM (16 bf16 of K = 8 packed columns per step), B = V (MN-major)
+              const int kk = 2 * c + k2;
+              mma_bf16_ts(tmem + 256 + 128 * t, tmem + 128 * t + kk * 8, sdesc_sw128(sv + kk * 2048, TILE, 1024),
+                          id_pv, (i > 0 || kk > 0) ? 1u : 0u);
+            }
           }
+          if (!ok) break;
           mma_commit(bar(B_EMPTY0 + e % NSLOTS));
           if (i + 1 < topk) {
             issue_s(t);  // overwrites P_t(i) in TMEM after P_t(i) V_t(i) in issue order
@@ -338,7 +395,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       const uint32_t lane_off = (uint32_t)(q * 32) << 16;
       const uint32_t tS = tmem + 128 * t + lane_off;
       const uint32_t tO = tmem + 256 + 128 * t + lane_off;
-      const int32_t* lut_row = p.lut + ((int64_t)bh * p.NBq + m0 + t) * topk;
+      const int32_t* lut_row = tile_row(t);
       const float scale = p.qk_scale;
       // the row's gate value (computed by the norm pass), loaded before the main
       // loop so that its latency is hidden behind it
@@ -346,7 +403,11 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       const float gate_pref = (p.has_lowrank && !p.has_x && p.gate != nullptr && tok_row < p.L)
                                   ? bf2f(p.gate[((int64_t)b * p.L + tok_row) * p.H + h])
                                   : 0.f;
-      float m_run = -INFINITY, l_run = 0.f;
+      // block 64: a tile's first key tiles may be entirely masked for this row
+      // (blocks only the other query block selected), so the running max starts
+      // finite: exp2(-inf - m) is then 0 instead of NaN, and the first real
+      // block's rescale factor exp2(-FLT_MAX - m) is 0
+      float m_run = p.blk64 ? -FLT_MAX : -INFINITY, l_run = 0.f;
       bool ok = true;
       for (int i = 0; i < topk; ++i) {
         if (!__all_sync(0xffffffffu, mbar_wait(bar(B_SF0 + t), i & 1, abort_flag, kDevTimeoutMma))) {
@@ -354,17 +415,29 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           break;
         }
         tc_fence_after();
-        const int j = lut_block(p, lut_row, i);
-        const int valid = p.L - j * 128;
+        // valid columns of each 64-column half of the key tile: past L (a partial
+        // last block), or, block 64, every column of a key block this row's query
+        // block did not select
+        int valid_lo, valid_hi;
+        if (!p.blk64) {
+          const int valid = p.L - lut_block(p, lut_row, i) * 128;
+          valid_lo = min(valid, 64);
+          valid_hi = min(valid - 64, 64);
+        } else {
+          valid_lo = pair_valid(p, lut_row[2 * i], row >> 6);
+          valid_hi = pair_valid(p, lut_row[2 * i + 1], row >> 6);
+        }
         // the whole S row: four 32-column loads, one wait
         uint32_t v[128];
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
         tmem_ld_wait();
-        if (valid < 128) {
+        if (valid_lo < 64 || valid_hi < 64) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
-            if (c >= valid) v[c] = __float_as_uint(-INFINITY);
+          for (int c = 0; c < 64; ++c) {
+            if (c >= valid_lo) v[c] = __float_as_uint(-INFINITY);
+            if (c >= valid_hi) v[64 + c] = __float_as_uint(-INFINITY);
+          }
         }
         // row max: 8 independent chains of three-input maxima
         float mx8[8];
@@ -395,8 +468,18 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         // P = exp2(s*scale - m), packed bf16 over the S columns (already in registers).
         // s*scale - m and the row sums run as packed fp32x2 operations (two
         // columns per instruction), the row sum in two independent pairs.
+        // P goes to the MMA in chunks of 32 keys: chunk c is published (its
+        // stores waited for, then one arrival per warp) once chunk c + 1 is
+        // computed, so the wait costs no exp2 time.
         const uint64_t sc2 = f2_pack(scale, scale), nm2 = f2_pack(-m_use, -m_use);
         uint64_t rs2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+        auto publish_p = [&](int c) {
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(B_PF0 + PCHUNKS * t + c));
+        };
+        static_assert(PCHUNKS == 4, "P chunks are 32 keys");
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t w[16];
@@ -411,18 +494,16 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
             rs2[e & 1] = add_f32x2(rs2[e & 1], f2_pack(p0, p1));
             w[e] = pack_bf2(p0, p1);
           }
+          if (c > 0) publish_p(c - 1);
           tmem_st16(tS + c * 16, w);
         }
-        tmem_st_wait();
+        publish_p(3);
         float rsa, rsb, rsc, rsd;
         f2_unpack(rs2[0], rsa, rsb);
         f2_unpack(rs2[1], rsc, rsd);
         const float rs = (rsa + rsc) + (rsb + rsd);
         l_run = l_run * alpha + rs;
         m_run = m_use;
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(B_PF0 + t));
       }
 
       // ---------------------------------------------------------- epilogue
@@ -600,7 +681,8 @@ int launch_sparse_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUten
   }
   if (launch_regs < LAUNCH_REGS) return -1;
   cudaFuncSetAttribute(sparse_attn_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  dim3 grid((p.NBq + 1) / 2, p.B * p.H);
+  const int nqt = p.blk64 ? (p.NBq + 1) / 2 : p.NBq;  // 128-row query tiles
+  dim3 grid((nqt + 1) / 2, p.B * p.H);
   sparse_attn_tcgen05<<<grid, THREADS, SMEM_BYTES, s>>>(tq, tk, tv, tqlr, tct, tx, p);
   return (int)cudaGetLastError();
 }

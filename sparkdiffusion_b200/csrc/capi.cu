@@ -77,7 +77,7 @@ EncodeTiledFn encode_fn() {
 
 // bf16 tensor of rank 2 or 3: dims innermost first, strides (bytes) of dims 1.., box innermost first
 int make_map(CUtensorMap* m, const void* ptr, int rank, const uint64_t* dims, const uint64_t* strides_bytes,
-             const uint32_t* box, const char* what) {
+             const uint32_t* box, const char* what, bool bytes = false) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(ROLA_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", what);
   ROLA_CHECK(aligned16(ptr), "%s: base address must be 16-byte aligned", what);
@@ -90,7 +90,8 @@ int make_map(CUtensorMap* m, const void* ptr, int rank, const uint64_t* dims, co
     bd[i] = box[i];
   }
   for (int i = 0; i < rank - 1; ++i) gs[i] = strides_bytes[i];
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(ptr), gd, gs, bd, es,
+  CUresult r = fn(m, bytes ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank,
+                  const_cast<void*>(ptr), gd, gs, bd, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(ROLA_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
@@ -187,6 +188,43 @@ static int qkv_gemm_impl(const void* x, const void* w, const void* bias, void* o
 int rola_b200_qkv_gemm(const void* x, const void* w, const void* bias, void* out, float* ssq, int64_t M, int64_t N,
                        int64_t K, rola_stream_t stream) {
   return qkv_gemm_impl(x, w, bias, out, ssq, M, N, K, nullptr, stream);
+}
+
+int rola_b200_quantize_rows_e4m3(const void* x, int64_t ld, int64_t M, int64_t K, void* xq, float* scale,
+                                 rola_stream_t stream) {
+  ROLA_CHECK(x && xq && scale, "quantize_rows_e4m3: null pointer");
+  ROLA_CHECK(M > 0 && M < (1ll << 31) && K > 0 && K % 8 == 0 && K <= 65536 && ld >= K && ld % 8 == 0,
+             "quantize_rows_e4m3: bad sizes (K a multiple of 8, row stride >= K)");
+  ROLA_CHECK(aligned16(x) && aligned16(xq), "quantize_rows_e4m3: 16-byte aligned rows required");
+  return cuda_status(launch_quantize_rows_e4m3(BF(x), ld, (int)M, (int)K, reinterpret_cast<uint8_t*>(xq), scale,
+                                               S(stream)),
+                     "quantize_rows_e4m3");
+}
+
+int rola_b200_qkv_gemm_fp8(const void* xq, const float* x_scale, const void* wq, const float* w_scale,
+                           const void* bias, void* out, float* ssq, int64_t M, int64_t N, int64_t K,
+                           rola_stream_t stream) {
+  ROLA_CHECK(xq && x_scale && wq && w_scale && out, "qkv_gemm_fp8: null pointer");
+  ROLA_CHECK(M > 0 && M < (1ll << 31), "qkv_gemm_fp8: M out of range");
+  ROLA_CHECK(N > 0 && N % 256 == 0 && N <= 65536, "qkv_gemm_fp8: N must be a positive multiple of 256");
+  ROLA_CHECK(K > 0 && K % 128 == 0 && K <= 65536, "qkv_gemm_fp8: K must be a positive multiple of 128");
+  ROLA_CHECK(aligned16(out), "qkv_gemm_fp8: out must be 16-byte aligned");
+  CUtensorMap ta, tb;
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)K};
+    const uint32_t box[2] = {128, 128};
+    ROLA_TRY(make_map(&ta, xq, 2, dims, strides, box, "qkv_gemm_fp8: xq", true));
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint64_t strides[1] = {(uint64_t)K};
+    const uint32_t box[2] = {128, 256};
+    ROLA_TRY(make_map(&tb, wq, 2, dims, strides, box, "qkv_gemm_fp8: wq", true));
+  }
+  return cuda_status(launch_gemm_bf16(ta, tb, BF(bias), BFm(out), N, ssq, (int)M, (int)N, (int)K, nullptr, S(stream),
+                                      x_scale, w_scale),
+                     "qkv_gemm_fp8");
 }
 
 // Runs the streaming norm pass.  ssq: the QKV GEMM's per-256-column sums of
@@ -441,6 +479,13 @@ int rola_b200_block_select(const void* pooled_q, const void* pooled_k, int BH, i
   return cuda_status(launch_topk(scores_ws, BH * NBq, NBk, topk, lut, S(stream)), "block_select/topk");
 }
 
+int rola_b200_pair_blocks(const int32_t* lut, int BH, int NB, int topk, int32_t* paired, rola_stream_t stream) {
+  ROLA_CHECK(lut && paired, "pair_blocks: null pointer");
+  ROLA_CHECK(BH > 0 && NB > 0 && topk >= 1 && topk <= NB && topk < (1 << 20) && NB < (1 << 28),
+             "pair_blocks: bad sizes");
+  return cuda_status(launch_pair_blocks(lut, BH, NB, topk, NB, paired, S(stream)), "pair_blocks");
+}
+
 int rola_b200_lowrank_q(const void* q_normed, int64_t sB, int64_t sH, int64_t sT, const void* proj_q,
                         const void* lr_cos, const void* lr_sin, int rope_dim, int B, int L, int H, int R, void* q_lr,
                         rola_stream_t stream) {
@@ -501,12 +546,13 @@ int rola_b200_lowrank_kv(const void* k_normed, int64_t k_sB, int64_t k_sH, int64
                      "lowrank_kv/reduce");
 }
 
-// head-view 4-D map: dims (d = 128, t = L, h = H, b = B) with element strides (1, sT, sH, sB)
+// head-view 4-D map: dims (d = 128, t = L, h = H, b = B) with element strides (1, sT, sH, sB);
+// boxes of 64 columns x `rows` tokens
 static int make_head_map(CUtensorMap* m, const void* ptr, int cols, int64_t sB, int64_t sH, int64_t sT, int L, int H,
-                         int B, const char* what) {
+                         int B, const char* what, int rows = 128) {
   const uint64_t dims[4] = {(uint64_t)cols, (uint64_t)L, (uint64_t)H, (uint64_t)B};
   const uint64_t strides[3] = {(uint64_t)sT * 2, (uint64_t)sH * 2, (uint64_t)sB * 2};
-  const uint32_t box[4] = {64, 128, 1, 1};
+  const uint32_t box[4] = {64, (uint32_t)rows, 1, 1};
   return make_map(m, ptr, 4, dims, strides, box, what);
 }
 
@@ -524,7 +570,7 @@ static int sparse_attn_impl(const void* q, const void* k, int64_t qk_sB, int64_t
                             rola_stream_t stream) {
   ROLA_CHECK(q && k && v && lut, "sparse_attn: null pointer");
   ROLA_CHECK(out || o_sparse || peer, "sparse_attn: no output requested");
-  ROLA_CHECK(blk == 128, "sparse_attn: block size must be 128");
+  ROLA_CHECK(blk == 128 || blk == 64, "sparse_attn: block size must be 128 or 64");
   ROLA_CHECK(B > 0 && L > 0 && H > 0 && (int64_t)B * H < 65536, "sparse_attn: bad sizes");
   const int NB = (L + blk - 1) / blk;
   ROLA_CHECK(topk >= 1 && topk <= NB, "sparse_attn: topk must be in [1, NB]");
@@ -541,8 +587,8 @@ static int sparse_attn_impl(const void* q, const void* k, int64_t qk_sB, int64_t
   memset(&tx, 0, sizeof(tx));
   if (x) ROLA_TRY(make_head_map(&tx, x, 128, x_sB, x_sH, x_sT, L, H, B, "sparse_attn: x"));
   ROLA_TRY(make_head_map(&tq, q, 128, qk_sB, qk_sH, qk_sT, L, H, B, "sparse_attn: q"));
-  ROLA_TRY(make_head_map(&tk, k, 128, qk_sB, qk_sH, qk_sT, L, H, B, "sparse_attn: k"));
-  ROLA_TRY(make_head_map(&tv, v, 128, v_sB, v_sH, v_sT, L, H, B, "sparse_attn: v"));
+  ROLA_TRY(make_head_map(&tk, k, 128, qk_sB, qk_sH, qk_sT, L, H, B, "sparse_attn: k", blk));
+  ROLA_TRY(make_head_map(&tv, v, 128, v_sB, v_sH, v_sT, L, H, B, "sparse_attn: v", blk));
   if (q_lr) {
     ROLA_TRY(make_head_map(&tqlr, q_lr, 64, (int64_t)L * H * 64, 64, (int64_t)H * 64, L, H, B, "sparse_attn: q_lr"));
     const uint64_t dims[3] = {64, 128, (uint64_t)B * H};
@@ -567,6 +613,7 @@ static int sparse_attn_impl(const void* q, const void* k, int64_t qk_sB, int64_t
   p.NBq = NB;
   p.NBk = NB;
   p.topk = topk;
+  p.blk64 = blk == 64;
   p.has_lowrank = q_lr != nullptr;
   p.qk_scale = (float)(0.08838834764831845 * 1.4426950408889634);  // 128^-0.5 * log2(e)
   p.eps_lr = eps_lr;

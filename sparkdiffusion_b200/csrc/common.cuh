@@ -11,6 +11,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <float.h>
 #include <stdint.h>
 
 #ifndef __CUDACC__
@@ -215,6 +216,17 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[smem desc] * B[smem desc], 8-bit floating-point operands
+// (both e4m3 here; the instruction descriptor names their formats)
+__device__ __forceinline__ void mma_f8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // arrive on `bar` once every tcgen05 op issued so far by this thread completes
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
@@ -227,6 +239,15 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_ma
          | (1u << 10)                           // B format bf16
          | ((a_mn_major ? 1u : 0u) << 15)       // A major
          | ((b_mn_major ? 1u : 0u) << 16)       // B major
+         | ((uint32_t)(N >> 3) << 17)           // N
+         | ((uint32_t)(M >> 4) << 24);          // M
+}
+
+// instruction descriptor, kind::f8f6f4, e4m3 x e4m3 -> fp32, dense, both K-major
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4)                              // D format f32
+         | (0u << 7)                            // A format e4m3
+         | (0u << 10)                           // B format e4m3
          | ((uint32_t)(N >> 3) << 17)           // N
          | ((uint32_t)(M >> 4) << 24);          // M
 }

@@ -5,6 +5,15 @@
 // reference prologue (sparkdiffusion/ops/fused_kernel/fused_qkv_rope.py:287-289)
 // with one GEMM over the concatenated [3*dim, dim] weight.
 //
+// FP8 variant (kFp8): e4m3 operands with one fp32 scale per row of A (token)
+// and per row of W (output channel), the reference's row-wise FP8 prologue
+// (`torch._scaled_mm(x_fp8, w_fp8.t(), scale_a, scale_b, bias, out_dtype=bf16)`,
+// fused_qkv_rope.py:270-285 with the recipe of ops/quantization/fp8_linear.py:45-61):
+// the accumulator times scale_a[m] times scale_b[n], plus the bias, rounded to
+// bf16.  The shared-memory tiles, the TMA boxes and the descriptors are the
+// same bytes as in bf16 (128-byte rows: 128 e4m3 or 64 bf16 values; every MMA
+// consumes 32 bytes of each row: K = 32 e4m3 or 16 bf16).
+//
 // Persistent kernel: one CTA per SM walks the 128 x 256 output tiles
 // (tile = blockIdx.x + i * gridDim.x, rasterised in groups of 16 M-tiles so
 // the tiles in flight at one time share A and W through L2).  K step 64 (one
@@ -40,12 +49,14 @@ constexpr int GROUP_M = 16;
 constexpr int ACC_COLS = 2 * BN;  // two accumulators
 }  // namespace gemm
 
+template <bool kFp8>
 __global__ void __launch_bounds__(gemm::THREADS_SIDE, 1)
-    gemm_bf16_tcgen05(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
-                      const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out, int64_t ldo,
-                      float* __restrict__ ssq, int M, int N, int K, const __grid_constant__ NormRopeParams side,
-                      int side_items) {
+    gemm_tcgen05(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                 const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ out, int64_t ldo,
+                 float* __restrict__ ssq, int M, int N, int K, const __grid_constant__ NormRopeParams side,
+                 int side_items, const float* __restrict__ scale_a, const float* __restrict__ scale_b) {
   using namespace gemm;
+  constexpr int BKE = kFp8 ? 2 * BK : BK;  // K elements per 128-byte stage row
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -63,7 +74,7 @@ __global__ void __launch_bounds__(gemm::THREADS_SIDE, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (M + BM - 1) / BM, num_n = N / BN;
   const int num_tiles = num_m * num_n;
-  const int nk = K / BK;
+  const int nk = K / BKE;
   // my tiles: blockIdx.x, blockIdx.x + gridDim.x, ...
   const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   auto tile_coords = [&](int lt, int& m0, int& n_tile) {
@@ -114,8 +125,8 @@ __global__ void __launch_bounds__(gemm::THREADS_SIDE, 1)
           }
           const uint32_t sa = base + s * STAGE_BYTES;
           mbar_expect_tx(full(s), STAGE_BYTES);
-          tma_load_2d(sa, &ta, full(s), kb * BK, m0);
-          tma_load_2d(sa + A_BYTES, &tb, full(s), kb * BK, n_tile * BN);
+          tma_load_2d(sa, &ta, full(s), kb * BKE, m0);
+          tma_load_2d(sa + A_BYTES, &tb, full(s), kb * BKE, n_tile * BN);
         }
       }
       // make sure no load is still writing shared memory when the CTA exits
@@ -124,7 +135,7 @@ __global__ void __launch_bounds__(gemm::THREADS_SIDE, 1)
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      const uint32_t idesc = idesc_bf16_f32(BM, BN, false, false);
+      const uint32_t idesc = kFp8 ? idesc_e4m3_f32(BM, BN) : idesc_bf16_f32(BM, BN, false, false);
       bool ok = true;
       int it = 0;
       for (int lt = 0; lt < my_tiles && ok; ++lt) {
@@ -146,7 +157,11 @@ __global__ void __launch_bounds__(gemm::THREADS_SIDE, 1)
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t da = sdesc_sw128(sa + kk * 32, 16, 1024);
             const uint64_t db = sdesc_sw128(sb + kk * 32, 16, 1024);
-            mma_bf16_ss(acc, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (kFp8) {
+              mma_f8_ss(acc, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            } else {
+              mma_bf16_ss(acc, da, db, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           mma_commit(empty(s));
         }
@@ -169,6 +184,8 @@ __global__ void __launch_bounds__(gemm::THREADS_SIDE, 1)
       const int gm_row = m0 + row;
       const uint32_t acc = tmem + a * BN + ((uint32_t)(q * 32) << 16);
       float ss = 0.f;  // sum of squares of this row's bf16 outputs in this tile
+      float row_scale = 1.f;
+      if (kFp8 && gm_row < M) row_scale = scale_a[gm_row];
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t v[32];
@@ -179,6 +196,10 @@ __global__ void __launch_bounds__(gemm::THREADS_SIDE, 1)
           float f[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
+          if (kFp8) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) f[i] = (f[i] * row_scale) * __ldg(scale_b + col + i);
+          }
           if (bias) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) f[i] += bf2f(bias[col + i]);
@@ -228,9 +249,11 @@ __global__ void __launch_bounds__(gemm::THREADS_SIDE, 1)
 static int g_num_sms = 0;
 
 int launch_gemm_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const __nv_bfloat16* bias, __nv_bfloat16* out,
-                     int64_t ldo, float* ssq, int M, int N, int K, const NormRopeParams* side, cudaStream_t s) {
+                     int64_t ldo, float* ssq, int M, int N, int K, const NormRopeParams* side, cudaStream_t s,
+                     const float* scale_a, const float* scale_b) {
   using namespace gemm;
-  if (N % BN != 0 || K % BK != 0 || M <= 0) return -1;
+  const bool fp8 = scale_a != nullptr;
+  if (N % BN != 0 || K % (fp8 ? 2 * BK : BK) != 0 || M <= 0 || fp8 != (scale_b != nullptr)) return -1;
   if (g_num_sms == 0) {
     int dev = 0;
     cudaGetDevice(&dev);
@@ -248,11 +271,79 @@ int launch_gemm_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const __nv_bf
     smem += norm_smem_bytes(kNormRingCompact, nslots, sp.blk, true);
     if (smem > 227 * 1024) return -1;
   }
-  cudaFuncSetAttribute(gemm_bf16_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   const int num_tiles = ((M + BM - 1) / BM) * (N / BN);
   const int grid = num_tiles < g_num_sms ? num_tiles : g_num_sms;
-  gemm_bf16_tcgen05<<<grid, side_items ? THREADS_SIDE : THREADS, smem, s>>>(ta, tb, bias, out, ldo, ssq, M, N, K, sp,
-                                                                           side_items);
+  const int threads = side_items ? THREADS_SIDE : THREADS;
+  if (fp8) {
+    cudaFuncSetAttribute(gemm_tcgen05<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    gemm_tcgen05<true><<<grid, threads, smem, s>>>(ta, tb, bias, out, ldo, ssq, M, N, K, sp, side_items, scale_a,
+                                                   scale_b);
+  } else {
+    cudaFuncSetAttribute(gemm_tcgen05<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    gemm_tcgen05<false><<<grid, threads, smem, s>>>(ta, tb, bias, out, ldo, ssq, M, N, K, sp, side_items, nullptr,
+                                                    nullptr);
+  }
+  return (int)cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Row-wise e4m3 quantization (the FP8 GEMM's operands), restating
+// quantize_activation_rowwise / quantize_weight_rowwise
+// (sparkdiffusion/ops/quantization/fp8_linear.py:45-61): scale = amax|row| / 448
+// + 1e-12 in fp32; q = e4m3(bf16(x / bf16(scale))), the bf16 quotient rounded
+// to nearest even as torch divides bf16 tensors, then rounded to nearest even
+// e4m3 (|q| <= 448 (1 + 2^-8) here, inside e4m3's range).  One CTA per row.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint16_t cvt_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));  // hi -> upper byte
+  return r;
+}
+
+__global__ void __launch_bounds__(128) quantize_rows_e4m3_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld,
+                                                                 int K, uint8_t* __restrict__ xq,
+                                                                 float* __restrict__ scale) {
+  __shared__ float s_red[4];
+  const int64_t m = blockIdx.x;
+  const __nv_bfloat16* row = x + m * ld;
+  float amax = 0.f;
+  for (int c = threadIdx.x * 8; c < K; c += 128 * 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + c);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float a, b;
+      unpack_bf2(w[e], a, b);
+      amax = fmaxf(amax, fmaxf(fabsf(a), fabsf(b)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
+  const float sc = __fadd_rn(__fdiv_rn(amax, 448.0f), 1e-12f);
+  const float sc_bf = rbf(sc);
+  if (threadIdx.x == 0) scale[m] = sc;
+  uint8_t* qrow = xq + m * (int64_t)K;
+  for (int c = threadIdx.x * 8; c < K; c += 128 * 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + c);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    uint16_t q[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float a, b;
+      unpack_bf2(w[e], a, b);
+      q[e] = cvt_e4m3x2(rbf(__fdiv_rn(a, sc_bf)), rbf(__fdiv_rn(b, sc_bf)));
+    }
+    *reinterpret_cast<uint2*>(qrow + c) =
+        make_uint2((uint32_t)q[0] | ((uint32_t)q[1] << 16), (uint32_t)q[2] | ((uint32_t)q[3] << 16));
+  }
+}
+
+int launch_quantize_rows_e4m3(const __nv_bfloat16* x, int64_t ld, int M, int K, uint8_t* xq, float* scale,
+                              cudaStream_t s) {
+  quantize_rows_e4m3_kernel<<<M, 128, 0, s>>>(x, ld, K, xq, scale);
   return (int)cudaGetLastError();
 }
 

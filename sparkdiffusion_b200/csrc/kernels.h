@@ -67,6 +67,9 @@ int launch_scores(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH, int 
                   cudaStream_t s);
 // lut[bh, m, :] = top-k of scores[bh, m, :] (ties -> lower index), ascending int32
 int launch_topk(const float* scores, int rows, int NBk, int k, int32_t* lut, cudaStream_t s);
+// block size 64: per 128-row query tile, the union of its two query blocks' kept
+// key blocks with selection masks: paired [BH, ceil(NBq/2), 2k + 1] int32
+int launch_pair_blocks(const int32_t* lut, int BH, int NBq, int k, int NBk, int32_t* paired, cudaStream_t s);
 // scores + top-k in one kernel (NBk <= 768; same results as launch_scores + launch_topk)
 int launch_select_fused(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH, int NBq, int NBk, int k,
                         int32_t* lut, cudaStream_t s);
@@ -98,8 +101,14 @@ int launch_lowrank_reduce(const float* c_partial, int splits, int BH, int R, __n
 // ssq (optional) [M, N/256]: per-row sum of squares of the bf16 outputs of each 256-column tile
 // side (optional): a compact norm-only pass (B = 1) that spare warps of the
 // persistent GEMM run alongside the tensor-core work
+// scale_a [M], scale_b [N] (both or neither): e4m3 operands (ta, tb over uint8), out = acc*scale_a*scale_b + bias
 int launch_gemm_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const __nv_bfloat16* bias, __nv_bfloat16* out,
-                     int64_t ldo, float* ssq, int M, int N, int K, const NormRopeParams* side, cudaStream_t s);
+                     int64_t ldo, float* ssq, int M, int N, int K, const NormRopeParams* side, cudaStream_t s,
+                     const float* scale_a = nullptr, const float* scale_b = nullptr);
+// row-wise e4m3 quantization of a bf16 [M, K] matrix (row stride ld): scale[m] =
+// amax_k|x|/448 + 1e-12 (fp32), xq = e4m3(bf16(x / bf16(scale))) (fp8_linear.py:51-61)
+int launch_quantize_rows_e4m3(const __nv_bfloat16* x, int64_t ld, int M, int K, uint8_t* xq, float* scale,
+                              cudaStream_t s);
 
 // attn.cu -----------------------------------------------------------------
 struct AttnParams {
@@ -118,6 +127,10 @@ struct AttnParams {
   int peer_n, peer_Ls, head_offset;
   int64_t peer_sB, peer_sT;
   int B, L, H, NBq, NBk, topk, has_lowrank;
+  // block size 64 (blk64 = 1): lut is the paired table of launch_pair_blocks
+  // (NBq, NBk count 64-token blocks; topk = k of the 64-block selection); the K
+  // and V maps have 64-row boxes
+  int blk64;
   float qk_scale;  // D^-1/2 * log2(e)
   float eps_lr;    // finfo(dtype).eps
   float rescale_threshold;  // log2 growth of the running max that triggers an O rescale (0 = always)

@@ -399,4 +399,54 @@ int launch_select_fused(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH
   return (int)cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Block size 64: the attention kernel's 128-row query tiles hold two 64-token
+// query blocks (2t, 2t + 1).  For each tile, the union of the two blocks' kept
+// key blocks, ascending, padded with -1 to 2k entries, each entry carrying in
+// bits 28-29 which of the two query blocks selected it (bit 28: block 2t, bit
+// 29: block 2t + 1), preceded by the number of 128-column key tiles (pairs of
+// union entries) the tile needs:
+//   paired[bh][t] = { count, e_0, ..., e_{2k-1} }
+// The LUT rows may be in any order (an injected LUT, e.g. the reference's).
+// ---------------------------------------------------------------------------
+__global__ void pair_blocks_kernel(const int32_t* __restrict__ lut, int BH, int NBq, int k, int NBk,
+                                   int32_t* __restrict__ paired) {
+  const int NT = (NBq + 1) / 2;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)BH * NT) return;
+  const int bh = (int)(i / NT), t = (int)(i % NT);
+  int32_t* out = paired + i * (2 * k + 1);
+  int u = 0;  // union entries written so far (kept ascending by insertion)
+  for (int half = 0; half < 2; ++half) {
+    const int m = 2 * t + half;
+    if (m >= NBq) break;
+    const int32_t* row = lut + ((int64_t)bh * NBq + m) * k;
+    for (int e = 0; e < k; ++e) {
+      int j = row[e];
+      if (j < 0 || j >= NBk) {
+        set_device_error(kDevBadIndex);
+        j = j < 0 ? 0 : NBk - 1;
+      }
+      const int32_t bit = 1 << (28 + half);
+      int pos = 0;
+      while (pos < u && (out[1 + pos] & 0x0fffffff) < j) ++pos;
+      if (pos < u && (out[1 + pos] & 0x0fffffff) == j) {
+        out[1 + pos] |= bit;
+        continue;
+      }
+      for (int q = u; q > pos; --q) out[1 + q] = out[q];
+      out[1 + pos] = j | bit;
+      ++u;
+    }
+  }
+  for (int q = u; q < 2 * k; ++q) out[1 + q] = -1;
+  out[0] = (u + 1) / 2;
+}
+
+int launch_pair_blocks(const int32_t* lut, int BH, int NBq, int k, int NBk, int32_t* paired, cudaStream_t s) {
+  const int64_t n = (int64_t)BH * ((NBq + 1) / 2);
+  pair_blocks_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(lut, BH, NBq, k, NBk, paired);
+  return (int)cudaGetLastError();
+}
+
 }  // namespace rola

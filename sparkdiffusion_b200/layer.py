@@ -110,6 +110,35 @@ class WanSelfAttentionRoLaB200(nn.Module):
             self._qkv_cache = (key, w, b)
         return self._qkv_cache[1], self._qkv_cache[2]
 
+    @staticmethod
+    def _is_fp8(mod) -> bool:
+        """The reference's FP8Linear (sparkdiffusion/ops/quantization/fp8_linear.py:134-155): e4m3
+        ``weight_fp8 [out, in]`` and fp32 ``w_scale_t [1, out]`` buffers instead of ``weight``."""
+        return hasattr(mod, "weight_fp8") and hasattr(mod, "w_scale_t")
+
+    def _fp8_qkv(self):
+        """(w_fp8 [3*dim, dim], w_scale [3*dim], bias) when q/k/v were converted to
+        FP8Linear (prequantize_qkv / convert_dit_linears_to_fp8), else None."""
+        mods = (self.q, self.k, self.v)
+        if not all(self._is_fp8(m) for m in mods):
+            if any(self._is_fp8(m) for m in mods):
+                raise ValueError("q, k and v must all be FP8Linear or all nn.Linear")
+            return None
+        biases = [getattr(m, "bias", None) for m in mods]
+
+        def build():
+            w8 = torch.cat([m.weight_fp8.view(torch.uint8) for m in mods], 0).view(torch.float8_e4m3fn)
+            ws = torch.cat([m.w_scale_t.reshape(-1).float() for m in mods], 0)
+            b = None if any(t is None for t in biases) else torch.cat(biases, 0).to(torch.bfloat16)
+            return w8, ws, b
+
+        if torch.compiler.is_compiling():
+            return build()
+        key = tuple(t.data_ptr() for m in mods for t in (m.weight_fp8, m.w_scale_t))
+        if self._qkv_cache is None or self._qkv_cache[0] != key:
+            self._qkv_cache = (key, *build())
+        return self._qkv_cache[1:]
+
     def attention_core(self, x: torch.Tensor, freqs: torch.Tensor, rope_cache=None) -> torch.Tensor:
         """Everything of the forward except the output projection."""
         if torch.is_grad_enabled() and self.training:
@@ -118,8 +147,8 @@ class WanSelfAttentionRoLaB200(nn.Module):
             raise RuntimeError("WanSelfAttentionRoLaB200 runs on CUDA tensors only")
         if self.attn_precision != "bf16":
             raise ValueError("the B200 path implements attn_precision='bf16'")
-        if self.rola_blkq != 128 or self.rola_blkk != 128:
-            raise ValueError("the B200 attention kernel supports rola_blkq == rola_blkk == 128")
+        if self.rola_blkq != self.rola_blkk or self.rola_blkq not in (64, 128):
+            raise ValueError("the B200 attention kernel supports rola_blkq == rola_blkk in (64, 128)")
         B, L, dim = x.shape
         if L < max(self.rola_blkq, self.rola_blkk):
             raise ValueError("sequence shorter than one block")
@@ -133,17 +162,24 @@ class WanSelfAttentionRoLaB200(nn.Module):
             lr_cos, lr_sin, rope_dim = rope_cache[1][0], rope_cache[1][1], rope_cache[1][2]
         else:
             lr_cos, lr_sin, rope_dim = prepare_lowrank_cos_sin(freqs, freqs.shape[0], self.rola_rank, torch.bfloat16)
-        w_qkv, b_qkv = self._fused_qkv()
+        fp8 = self._fp8_qkv()
+        if fp8 is not None:
+            w_qkv, w_scale, b_qkv = fp8
+        else:
+            (w_qkv, b_qkv), w_scale = self._fused_qkv(), None
         nwq = self.norm_q.weight if self.qk_norm else None
         nwk = self.norm_k.weight if self.qk_norm else None
         if self._pg is not None and torch.distributed.get_world_size(self._pg) > 1:
+            if w_scale is not None:
+                raise ValueError("the sequence-parallel route takes bf16 q/k/v projections")
             from .ulysses import ulysses_rola_attention
             return ulysses_rola_attention(self, x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, nwq, nwk)
-        NB = (L + 127) // 128
+        blk = self.rola_blkq
+        NB = (L + blk - 1) // blk
         topk = ops.topk_count(self.rola_topk_ratio, NB)
         return torch.ops.rola_b200.attention_core(x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, nwq, nwk,
                                                   self.proj_q.weight, self.proj_k.weight, self.gate_proj.weight,
-                                                  self.gate_bias, self.num_heads, topk, self.eps)
+                                                  self.gate_bias, self.num_heads, topk, self.eps, blk, w_scale)
 
     def _o_weight(self):
         """bf16 copy of the output projection for the tcgen05 GEMM (cached like the QKV weight)."""
@@ -159,6 +195,11 @@ class WanSelfAttentionRoLaB200(nn.Module):
         del seq_lens
         out = self.attention_core(x, freqs, rope_cache)
         B, L, dim = out.shape
+        if self._is_fp8(self.o):
+            # FP8Linear output projection: per-token quantization of the attention output
+            xq, xs = ops.quantize_rows_e4m3(out.reshape(B * L, dim))
+            y = ops.qkv_gemm_fp8(xq, xs, self.o.weight_fp8, self.o.w_scale_t, getattr(self.o, "bias", None))
+            return y.view(B, L, dim).to(x.dtype)
         if dim % 256 == 0:
             # self.o (wan_rola_attention.py:447) on the same persistent tcgen05 GEMM as the QKV projection
             w, b = self._o_weight()

@@ -61,7 +61,7 @@ def _require_cuda(*ts: torch.Tensor | None) -> None:
             continue
         if not t.is_cuda:
             raise ValueError("sparkdiffusion_b200 ops run on CUDA tensors only (no CPU fallback)")
-        if t.dtype not in (torch.bfloat16, torch.float32, torch.int32):
+        if t.dtype not in (torch.bfloat16, torch.float32, torch.int32, torch.float8_e4m3fn):
             raise ValueError(f"unsupported dtype {t.dtype}")
 
 
@@ -119,6 +119,52 @@ def qkv_gemm(x2d: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = Non
         raise ValueError("qkv_gemm: ssq must be a contiguous fp32 [M, N/256] tensor")
     _lib.call("rola_b200_qkv_gemm", _ptr(x2d), _ptr(w), _ptr(b), _ptr(out), _ptr(ssq), M, N, K, _stream())
     return out
+
+
+def quantize_rows_e4m3(x2d: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Row-wise FP8 quantization of bf16 ``[M, K]`` (the reference's
+    quantize_activation_rowwise / quantize_weight_rowwise,
+    sparkdiffusion/ops/quantization/fp8_linear.py:45-61) -> ``(xq float8_e4m3fn
+    [M, K], scale fp32 [M])`` with ``x ~= xq * scale[:, None]``."""
+    _require_cuda(x2d)
+    if x2d.dtype != BF16 or x2d.dim() != 2 or x2d.stride(1) != 1:
+        raise ValueError("quantize_rows_e4m3: bf16 [M, K] rows with unit column stride required")
+    M, K = x2d.shape
+    xq = torch.empty(M, K, device=x2d.device, dtype=torch.float8_e4m3fn)
+    scale = torch.empty(M, device=x2d.device, dtype=torch.float32)
+    _lib.call("rola_b200_quantize_rows_e4m3", _ptr(x2d), x2d.stride(0), M, K, _ptr(xq), _ptr(scale), _stream())
+    return xq, scale
+
+
+def qkv_gemm_fp8(xq: torch.Tensor, x_scale: torch.Tensor, wq: torch.Tensor, w_scale: torch.Tensor,
+                 bias: torch.Tensor | None = None, ssq: torch.Tensor | None = None) -> torch.Tensor:
+    """``out[M, N] = bf16((xq . wq^T) * x_scale[:, None] * w_scale[None, :] + bias)`` on
+    tcgen05 with e4m3 operands (the reference's FP8 prologue, torch._scaled_mm with
+    row-wise scales, fused_qkv_rope.py:270-285).  ``ssq`` as in ``qkv_gemm``."""
+    _require_cuda(xq, wq, x_scale, w_scale, bias)
+    if xq.dtype != torch.float8_e4m3fn or wq.dtype != torch.float8_e4m3fn:
+        raise ValueError("qkv_gemm_fp8: float8_e4m3fn operands required")
+    M, K = xq.shape
+    N = wq.shape[0]
+    if wq.shape[1] != K:
+        raise ValueError(f"qkv_gemm_fp8: weight {tuple(wq.shape)} does not match x {tuple(xq.shape)}")
+    xs = x_scale.reshape(-1).to(torch.float32).contiguous()
+    ws = w_scale.reshape(-1).to(torch.float32).contiguous()
+    if xs.numel() != M or ws.numel() != N:
+        raise ValueError("qkv_gemm_fp8: one scale per row of x and per output channel required")
+    out = torch.empty(M, N, device=xq.device, dtype=BF16)
+    b = None if bias is None else bias.to(BF16).contiguous()
+    if ssq is not None and (ssq.dtype != torch.float32 or ssq.shape != (M, N // 256) or not ssq.is_contiguous()):
+        raise ValueError("qkv_gemm_fp8: ssq must be a contiguous fp32 [M, N/256] tensor")
+    _lib.call("rola_b200_qkv_gemm_fp8", _ptr(xq.contiguous()), _ptr(xs), _ptr(wq.contiguous()), _ptr(ws), _ptr(b),
+              _ptr(out), _ptr(ssq), M, N, K, _stream())
+    return out
+
+
+def prequantize_qkv_weight(w_qkv: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """FP8 copy of the concatenated ``[Wq; Wk; Wv]`` with per-output-channel scales
+    (quantize_weight_rowwise, fp8_linear.py:45-53) -> ``(w_fp8, w_scale [3*dim])``."""
+    return quantize_rows_e4m3(w_qkv.to(BF16).contiguous())
 
 
 def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, ksum, lr_cos, lr_sin, rope_dim,
@@ -202,6 +248,12 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
     main.wait_stream(s_sel)
     main.wait_stream(s_kv)
     main.wait_stream(s_q)
+    attn_lut = lut
+    if blk == 64:
+        # 128-row query tiles of two 64-token blocks: the union of their kept key
+        # blocks with selection masks (rola_b200_pair_blocks)
+        attn_lut = e(B * H, (NB + 1) // 2, 2 * topk + 1, dt=torch.int32)
+        _lib.call("rola_b200_pair_blocks", _ptr(lut), B * H, NB, topk, _ptr(attn_lut), st)
     eps_lr = float(torch.finfo(BF16).eps)
     if events is not None:
         events["attn"][0].record()
@@ -214,11 +266,11 @@ def head_local_attention(q_rope, k_rope, q_normed, k_normed, v, gate, pooled_q, 
         xs, gw, gb = (0, 0, 0), None, None
     if scatter is not None:
         _lib.call("rola_b200_sparse_attn_scatter", _ptr(q_rope), _ptr(k_rope), L * dim, HEAD_DIM, dim, _ptr(v),
-                  vs[0], HEAD_DIM, vs[1], _ptr(lut), B, L, H, blk, topk, _ptr(q_lr), _ptr(Ct), _ptr(gate), eps_lr,
+                  vs[0], HEAD_DIM, vs[1], _ptr(attn_lut), B, L, H, blk, topk, _ptr(q_lr), _ptr(Ct), _ptr(gate), eps_lr,
                   scatter["dst"], scatter["world"], scatter["head_offset"], scatter["H_total"], st)
     else:
         _lib.call("rola_b200_sparse_attn", _ptr(q_rope), _ptr(k_rope), L * dim, HEAD_DIM, dim, _ptr(v), vs[0],
-                  HEAD_DIM, vs[1], _ptr(lut), B, L, H, blk, topk, _ptr(q_lr), _ptr(Ct), _ptr(gate), _ptr(x),
+                  HEAD_DIM, vs[1], _ptr(attn_lut), B, L, H, blk, topk, _ptr(q_lr), _ptr(Ct), _ptr(gate), _ptr(x),
                   xs[0], HEAD_DIM, xs[1], _ptr(gw), _ptr(gb), eps_lr, _ptr(out), _ptr(o_sparse), L * dim, HEAD_DIM,
                   dim, st)
     if events is not None:
@@ -245,8 +297,8 @@ def rola_attention_from_qkv(q_raw, k_raw, v_raw, x, cos_sin, lr_cos, lr_sin, rop
     H = num_heads
     if dim != H * HEAD_DIM:
         raise ValueError(f"hidden size {dim} != num_heads*128")
-    if blk != 128:
-        raise ValueError("the B200 attention kernel supports block size 128")
+    if blk not in (64, 128):
+        raise ValueError("the B200 attention kernel supports block sizes 64 and 128")
     for t in (q_raw, k_raw, v_raw):
         if t.stride(2) != 1:
             raise ValueError("q/k/v must have unit column stride")
@@ -285,16 +337,24 @@ def rola_attention_from_qkv(q_raw, k_raw, v_raw, x, cos_sin, lr_cos, lr_sin, rop
 
 def rola_attention_core(x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk, proj_q, proj_k,
                         gate_w, gate_b, num_heads: int, blk: int = 128, topk: int = 1, eps: float = 1e-6,
-                        splits: int | None = None, keep: bool = False, events: dict | None = None):
+                        splits: int | None = None, keep: bool = False, events: dict | None = None,
+                        w_scale: torch.Tensor | None = None):
     """RoLa forward from hidden states ``x [B, L, H*D]`` up to (excluding) the
     output projection: ``WanSelfAttentionRoLa.fused_forward`` minus ``self.o``
     (sparkdiffusion/networks/wan_rola_attention.py:414-446).  ``w_qkv`` is the
-    concatenated ``[Wq; Wk; Wv]`` of shape ``[3*dim, dim]``."""
+    concatenated ``[Wq; Wk; Wv]`` of shape ``[3*dim, dim]``: bf16, or float8_e4m3fn
+    with per-output-channel scales ``w_scale [3*dim]`` (the reference's FP8 mode:
+    the hidden states are quantized per token once for all three projections,
+    fused_qkv_rope.py:270-285)."""
     B, L, dim = x.shape
     ssq = torch.empty(B * L, 3 * dim // 256, device=x.device, dtype=torch.float32)
     if events is not None:
         events["gemm"][0].record()
-    qkv = qkv_gemm(x.reshape(B * L, dim), w_qkv, b_qkv, ssq).view(B, L, 3 * dim)
+    if w_scale is not None:
+        xq, xs = quantize_rows_e4m3(x.reshape(B * L, dim))
+        qkv = qkv_gemm_fp8(xq, xs, w_qkv, w_scale, b_qkv, ssq).view(B, L, 3 * dim)
+    else:
+        qkv = qkv_gemm(x.reshape(B * L, dim), w_qkv, b_qkv, ssq).view(B, L, 3 * dim)
     if events is not None:
         events["gemm"][1].record()
     res = rola_attention_from_qkv(qkv[..., :dim], qkv[..., dim:2 * dim], qkv[..., 2 * dim:], x, cos_sin, lr_cos,
@@ -442,8 +502,8 @@ def fused_sparse_attn(q, k, v, topk_ratio: float = 0.1, blkq: int = 64, blkk: in
         raise ValueError(f"invalid num_heads={num_heads} for leading dimension {BH}")
     if force_local_sink:
         raise ValueError("force_local_sink is not supported by the B200 path")
-    if blkq != blkk or blkq != 128:
-        raise ValueError("the B200 attention kernel supports blkq == blkk == 128")
+    if blkq != blkk or blkq not in (64, 128):
+        raise ValueError("the B200 attention kernel supports blkq == blkk in (64, 128)")
     _require_cuda(q, k, v)
     H = num_heads
     B = BH // H
@@ -453,6 +513,10 @@ def fused_sparse_attn(q, k, v, topk_ratio: float = 0.1, blkq: int = 64, blkk: in
     pq = mean_pool(q4, blkq)
     pk = mean_pool(k4, blkk, center=smooth_k_center(k4, blkk))
     lut = block_select(pq, pk, topk)
+    if blkq == 64:
+        paired = torch.empty(B * H, (NB + 1) // 2, 2 * topk + 1, device=q.device, dtype=torch.int32)
+        _lib.call("rola_b200_pair_blocks", _ptr(lut), B * H, NB, topk, _ptr(paired), _stream())
+        lut = paired
     o = torch.empty_like(v4)
     s = q4.stride()
     vs = v4.stride()
@@ -511,18 +575,24 @@ def fused_qkv_gemm_rope(x, q_proj, k_proj, v_proj, freqs, norm_q_weight, norm_k_
     """QKV projection + full-width qk-RMSNorm + interleaved RoPE
     (sparkdiffusion/ops/fused_kernel/fused_qkv_rope.py:228-333).  Returns q, k,
     v as ``[B*H, L, D]`` (and q/k normed ``[B, L, H, D]``), the reference's layouts."""
-    if fp8_weights is not None:
-        raise ValueError("fp8 QKV weights are not supported by the B200 path yet")
     if head_dim != HEAD_DIM:
         raise ValueError("head_dim must be 128")
     B, L, dim = x.shape
     H = num_heads
-    w = torch.cat([q_proj.weight, k_proj.weight, v_proj.weight], 0).to(BF16)
     bias = None
     if q_proj.bias is not None:
         bias = torch.cat([q_proj.bias, k_proj.bias, v_proj.bias], 0).to(BF16)
     ssq = torch.empty(B * L, 3 * dim // 256, device=x.device, dtype=torch.float32) if H % 2 == 0 else None
-    qkv = qkv_gemm(x.reshape(B * L, dim), w, bias, ssq).view(B, L, 3 * dim)
+    if fp8_weights is not None:
+        # {'q'|'k'|'v': (w_fp8 [dim, dim], w_scale_t [1, dim])} from the reference's prequantize_qkv:
+        # one activation quantization shared by the three projections (fused_qkv_rope.py:270-285)
+        w8 = torch.cat([fp8_weights[n][0].view(torch.uint8) for n in ("q", "k", "v")], 0).view(torch.float8_e4m3fn)
+        ws = torch.cat([fp8_weights[n][1].reshape(-1) for n in ("q", "k", "v")], 0)
+        xq, xs = quantize_rows_e4m3(x.reshape(B * L, dim).to(BF16).contiguous())
+        qkv = qkv_gemm_fp8(xq, xs, w8, ws, bias, ssq).view(B, L, 3 * dim)
+    else:
+        w = torch.cat([q_proj.weight, k_proj.weight, v_proj.weight], 0).to(BF16)
+        qkv = qkv_gemm(x.reshape(B * L, dim), w, bias, ssq).view(B, L, 3 * dim)
     if cos_sin is None:
         cos_sin = prepare_cos_sin(freqs, L, head_dim)
     e = lambda: torch.empty(B, L, dim, device=x.device, dtype=BF16)  # noqa: E731

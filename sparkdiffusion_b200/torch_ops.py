@@ -12,7 +12,8 @@ Ops (inputs and layouts as in ``ops``; outputs are new tensors):
 
 * ``qkv_gemm(x2d, w, bias?) -> [M, N]`` bf16 (the QKV projection and ``self.o``);
 * ``attention_core(x, w_qkv, b_qkv?, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq?,
-  norm_wk?, proj_q, proj_k, gate_w, gate_b, num_heads, topk, eps) -> [B, L, H*D]``
+  norm_wk?, proj_q, proj_k, gate_w, gate_b, num_heads, topk, eps, blk=128, w_scale?) -> [B, L, H*D]``
+  (``w_scale`` given: ``w_qkv`` is float8_e4m3fn, the reference's FP8 mode)
   bf16: ``fused_forward`` minus ``self.o`` (wan_rola_attention.py:414-446);
 * ``block_select(pooled_q, pooled_k, topk) -> [B*H, NBq, topk]`` int32;
 * ``fused_sparse_attn(q, k, v, topk_ratio, blkq, blkk, num_heads) -> [B, H, L, D]``
@@ -46,14 +47,14 @@ def _(x2d, w, bias):
 def attention_core(x: Tensor, w_qkv: Tensor, b_qkv: Optional[Tensor], cos_sin: Tensor, lr_cos: Tensor,
                    lr_sin: Tensor, rope_dim: int, norm_wq: Optional[Tensor], norm_wk: Optional[Tensor],
                    proj_q: Tensor, proj_k: Tensor, gate_w: Tensor, gate_b: Tensor, num_heads: int, topk: int,
-                   eps: float) -> Tensor:
+                   eps: float, blk: int = 128, w_scale: Optional[Tensor] = None) -> Tensor:
     return ops.rola_attention_core(x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk, proj_q,
-                                   proj_k, gate_w, gate_b, num_heads, 128, topk, eps)
+                                   proj_k, gate_w, gate_b, num_heads, blk, topk, eps, w_scale=w_scale)
 
 
 @attention_core.register_fake
 def _(x, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk, proj_q, proj_k, gate_w, gate_b,
-      num_heads, topk, eps):
+      num_heads, topk, eps, blk=128, w_scale=None):
     return x.new_empty(x.shape, dtype=BF16)
 
 

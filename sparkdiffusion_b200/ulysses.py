@@ -172,7 +172,8 @@ def _gemm_scatter_overlapped(x_local, w_qkv, b_qkv, nwq, nwk, gw, gb, xc, H, p, 
 def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, norm_wq, norm_wk,
                                   proj_q, proj_k, gate_w, gate_b, num_heads: int, topk: int, group=None,
                                   eps: float = 1e-6, splits: int | None = None, events: dict | None = None,
-                                  transport: str = "peer", chunks: int | None = None, record: dict | None = None):
+                                  transport: str = "peer", chunks: int | None = None, record: dict | None = None,
+                                  blk: int = 128):
     """Sequence-sharded RoLa forward: ``x_local [B, Ls, H*D]`` on this rank ->
     ``[B, Ls, H*D]`` (excluding the output projection).  ``cos_sin`` and the
     low-rank tables cover the whole sequence (global positions).
@@ -183,7 +184,8 @@ def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin
     The peer transport overlaps the QKV GEMM with the scattering norm pass in
     token chunks (``chunk_plan``; ``chunks`` forces that many equal chunks,
     1 turns the overlap off).  ``record`` (a dict) receives this rank's LUT
-    (``lut``, int32 ``[B*Hl, NB, k]`` of heads ``rank*Hl ...``)."""
+    (``lut``, int32 ``[B*Hl, NB, k]`` of heads ``rank*Hl ...``).  ``blk``: the
+    selection block size (128 or 64)."""
     if transport not in ("peer", "nccl"):
         raise ValueError(f"unknown transport {transport!r}")
     p = dist.get_world_size(group)
@@ -247,7 +249,8 @@ def ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin
         k_n = k_n.view(B, L, Hl * HEAD_DIM)
         v = v.view(B, L, Hl * HEAD_DIM)
         gate = gate.view(B, L, Hl)
-    blk = 128
+    if blk not in (64, 128):
+        raise ValueError("block size must be 64 or 128")
     NB = (L + blk - 1) // blk
     q_rope = torch.empty_like(q_n)
     k_rope = torch.empty_like(k_n)
@@ -290,11 +293,12 @@ def ulysses_rola_attention(layer, x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin
         cos_sin = _all_gather_rows(cos_sin, group)
         lr_cos = _all_gather_rows(lr_cos, group)
         lr_sin = _all_gather_rows(lr_sin, group)
-    NB = (L + 127) // 128
+    blk = layer.rola_blkq
+    NB = (L + blk - 1) // blk
     topk = ops.topk_count(layer.rola_topk_ratio, NB)
     return ulysses_rola_attention_params(x_local, w_qkv, b_qkv, cos_sin, lr_cos, lr_sin, rope_dim, nwq, nwk,
                                          layer.proj_q.weight, layer.proj_k.weight, layer.gate_proj.weight,
-                                         layer.gate_bias, layer.num_heads, topk, group, layer.eps)
+                                         layer.gate_bias, layer.num_heads, topk, group, layer.eps, blk=blk)
 
 
 def _all_gather_rows(t: torch.Tensor, group) -> torch.Tensor:
