@@ -521,6 +521,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       if (ok) {
         const int tok = (m0 + t) * 128 + row;
         const float inv_l = 1.0f / l_run;
+        const uint64_t il2 = f2_pack(inv_l, inv_l);
         // one pass over TMEM: the row's o_sparse and o_lr values, rounded to
         // bf16 as the reference materialises them, stay in registers as packed
         // pairs (64 + 64) for the statistics and the fused output
@@ -535,13 +536,16 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            // each bf16 rounding of a column pair is one packed conversion
-            const uint32_t op = pack_bf2(__uint_as_float(ov[2 * e]) * inv_l, __uint_as_float(ov[2 * e + 1]) * inv_l);
+            // o = acc / l as one fp32x2 multiply, rounded to bf16 by one packed
+            // conversion; the squares rounded to bf16 by one bf16x2 multiply
+            // (the product of two bf16 values is exact in fp32, so this is the
+            // fp32 square rounded once)
+            float a0, a1;
+            f2_unpack(mul_f32x2(f2_pack(__uint_as_float(ov[2 * e]), __uint_as_float(ov[2 * e + 1])), il2), a0, a1);
+            const uint32_t op = pack_bf2(a0, a1);
             osp[8 * c + e] = op;
-            float o0, o1;
-            unpack_bf2(op, o0, o1);
-            float q0 = o0 * o0, q1 = o1 * o1;
-            rbf2(q0, q1);
+            float q0, q1;
+            unpack_bf2(mul_bf16x2(op, op), q0, q1);
             ss_os += q0;
             ss_os += q1;
             if (lowrank) {
@@ -609,10 +613,14 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
               float os0, os1, l0, l1;
               unpack_bf2(osp[8 * c + e], os0, os1);
               unpack_bf2(lrp[8 * c + e], l0, l1);
-              l0 *= lr_scale;
-              l1 *= lr_scale;
+              f2_unpack(mul_f32x2(f2_pack(l0, l1), f2_pack(lr_scale, lr_scale)), l0, l1);
               rbf2(l0, l1);
-              wo[e] = pack_bf2((os0 * inv_rms + gate * l0) * os_rms, (os1 * inv_rms + gate * l1) * os_rms);
+              // (os / os_rms + gate * l) * os_rms with os / os_rms as os * (1 / os_rms)
+              const uint64_t u = fma_f32x2(f2_pack(os0, os1), f2_pack(inv_rms, inv_rms),
+                                           mul_f32x2(f2_pack(gate, gate), f2_pack(l0, l1)));
+              float r0, r1;
+              f2_unpack(mul_f32x2(u, f2_pack(os_rms, os_rms)), r0, r1);
+              wo[e] = pack_bf2(r0, r1);
             } else {
               wo[e] = osp[8 * c + e];
             }

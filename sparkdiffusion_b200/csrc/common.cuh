@@ -55,6 +55,12 @@ __device__ __forceinline__ void unpack_bf2(uint32_t u, float& lo, float& hi) {
 // rbf of two values with one conversion instruction (the conversions run on
 // the MUFU/XU pipe, a quarter of the FMA pipe's rate; pairing halves them)
 __device__ __forceinline__ void rbf2(float& a, float& b) { unpack_bf2(pack_bf2(a, b), a, b); }
+// bf16x2 product, each half rounded once to bf16 (nearest even)
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;

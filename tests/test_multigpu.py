@@ -108,3 +108,72 @@ def test_ulysses_matches_single_gpu(tmp_path, world, transport, chunks):
     ref = ops.rola_attention_core(inp["x"], inp["w_qkv"], None, *common, wl.H, 128, wl.topk)
     torch.cuda.synchronize()
     assert torch.equal(got["out"], ref.cpu()), f"ulysses {world} GPUs ({transport}) differs from the single GPU"
+
+
+def _layer_rank_main(rank, world, blk, port, out_path):
+    """The drop-in layer under the model's context-parallel hook: each rank gets
+    its sequence shard of the hidden states and of the RoPE frequencies (as
+    WanModel passes them, wan2pt1.py:825-826), the layer runs the Ulysses route."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from sparkdiffusion_b200 import peer
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    layer, x, freqs = _layer_case(blk, dev)
+    L = x.shape[1]
+    Ls = L // world
+    layer.set_context_parallel_group(dist.group.WORLD, list(range(world)), torch.cuda.Stream())
+    with torch.no_grad():
+        y = layer(x[:, rank * Ls:(rank + 1) * Ls].contiguous(), torch.tensor([L]),
+                  freqs[rank * Ls:(rank + 1) * Ls])
+    torch.cuda.synchronize()
+    parts = [torch.empty_like(y) for _ in range(world)]
+    dist.all_gather(parts, y.contiguous())
+    if rank == 0:
+        torch.save({"out": torch.cat(parts, dim=1).cpu()}, out_path)
+    peer.release_all()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _layer_case(blk, dev):
+    from sparkdiffusion_b200.layer import WanSelfAttentionRoLaB200
+    from sparkdiffusion_b200.rope import wan_rope_freqs
+
+    torch.manual_seed(11)
+    grid = (4, 16, 30)  # L = 1920: 15 blocks of 128 / 30 of 64
+    layer = WanSelfAttentionRoLaB200(1024, 8, True, 1e-6, rola_topk_ratio=0.25, rola_rank=64, rola_blkq=blk,
+                                     rola_blkk=blk)
+    with torch.no_grad():  # a gate that varies per token (the trained layer's is not constant)
+        layer.gate_proj.weight.normal_(0.0, 0.05)
+        layer.norm_q.weight.uniform_(0.5, 1.5)
+        layer.norm_k.weight.uniform_(0.5, 1.5)
+    layer = layer.to(torch.bfloat16).to(dev).eval()
+    g = torch.Generator().manual_seed(12)
+    x = torch.randn(1, grid[0] * grid[1] * grid[2], 1024, generator=g).to(torch.bfloat16).to(dev)
+    return layer, x, wan_rope_freqs(*grid).to(dev)
+
+
+@pytest.mark.parametrize("blk", [128, 64])
+def test_layer_context_parallel_matches_single_gpu(tmp_path, blk):
+    """WanSelfAttentionRoLaB200 after set_context_parallel_group on 2 ranks equals
+    the same layer on one GPU, bit for bit (output projection included)."""
+    world = 2
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out_path = str(tmp_path / "layer_cp.pt")
+    mp.start_processes(_layer_rank_main, args=(world, blk, _free_port(), out_path), nprocs=world,
+                       start_method="spawn")
+    got = torch.load(out_path)["out"]
+    layer, x, freqs = _layer_case(blk, torch.device("cuda", 0))
+    with torch.no_grad():
+        ref = layer(x, torch.tensor([x.shape[1]]), freqs)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref.cpu()), f"context-parallel layer (blk {blk}) differs from the single GPU"
