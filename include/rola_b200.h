@@ -221,8 +221,9 @@ int rola_b200_lowrank_q(const void* q_normed, int64_t sB, int64_t sH, int64_t sT
  * rola_b200_lowrank_q (k_s* and v_s* strides) -> C [B*H, R, D] and
  * Ct [B*H, D, R] bf16 (either may be NULL).  c_partial_ws: fp32 scratch of
  * chunks*B*H*R*D floats, chunks = ceil(ceil(L/64)/16): one partial sum per
- * 1024 tokens, added in order, so C is the same for any `splits` (the number
- * of CTA columns of the reduction, a parallelism knob).  R == 64.
+ * 1024 tokens, added in order, so C does not depend on the launch.  `splits`
+ * (> 0) is accepted for ABI compatibility and ignored: the kernel runs
+ * persistent CTAs, two per SM.  R == 64; lr_cos / lr_sin 16-byte aligned.
  * Replaces fused_lowrank.py:331-358 (k_lr projection + cuBLAS k_lr^T v). */
 int rola_b200_lowrank_kv(const void* k_normed, int64_t k_sB, int64_t k_sH, int64_t k_sT, const void* v, int64_t v_sB,
                          int64_t v_sH, int64_t v_sT, const void* proj_k, const void* lr_cos, const void* lr_sin,

@@ -518,6 +518,7 @@ int rola_b200_lowrank_kv(const void* k_normed, int64_t k_sB, int64_t k_sH, int64
   ROLA_CHECK(k_normed && v && proj_k && c_partial_ws && (C || Ct), "lowrank_kv: null pointer");
   ROLA_CHECK(R == 64, "lowrank_kv: rank must be 64");
   ROLA_CHECK(rope_dim >= 0 && rope_dim <= R / 2 && (rope_dim == 0 || (lr_cos && lr_sin)), "lowrank_kv: bad rope_dim");
+  ROLA_CHECK(rope_dim == 0 || (aligned16(lr_cos) && aligned16(lr_sin)), "lowrank_kv: 16-byte aligned RoPE tables required");
   ROLA_CHECK(B > 0 && L > 0 && H > 0 && splits > 0 && splits <= 4096, "lowrank_kv: bad sizes");
   ROLA_CHECK(aligned16(k_normed) && aligned16(v) && k_sB % 8 == 0 && k_sH % 8 == 0 && k_sT % 8 == 0 &&
                  v_sB % 8 == 0 && v_sH % 8 == 0 && v_sT % 8 == 0,

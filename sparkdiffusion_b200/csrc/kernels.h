@@ -85,7 +85,7 @@ struct LowrankParams {
   int64_t v_sB, v_sH, v_sT;
   __nv_bfloat16* lr_out;      // q_lr: element (b,t,h,r) at lr_out + (b*L+t)*H*R + h*R + r
   float* c_partial;           // [lowrank_chunks(L), B*H, R, D]
-  int B, L, H, R, rope_dim, splits;  // splits: CTA columns of the C reduction
+  int B, L, H, R, rope_dim, splits;  // splits: unused by the kernels (the C reduction is persistent)
 };
 // C partials: one per chunk of kKvChunk 64-token tiles, [lowrank_chunks(L), B*H, R, D] fp32
 constexpr int kKvChunk = 16;

@@ -86,8 +86,8 @@ def lowrank_chunks(L: int) -> int:
 
 
 def default_splits(B: int, H: int, L: int) -> int:
-    """CTA columns of the low-rank C reduction: one wave of two CTAs per SM.
-    (C itself does not depend on it: its partials follow fixed token chunks.)"""
+    """The C ABI's ``splits`` argument of the low-rank reduction (kept for ABI
+    compatibility; the kernel is persistent and C follows fixed token chunks)."""
     sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
     return max(1, min(lowrank_chunks(L), (2 * sms) // (B * H)))
 
