@@ -293,8 +293,11 @@ __global__ void __launch_bounds__(512) select_fused_kernel(const __nv_bfloat16* 
                                                            int k, int32_t* __restrict__ lut) {
   constexpr int ROWS = 16 * RW;
   extern __shared__ uint32_t sel_smem[];
-  uint32_t* sk = sel_smem;                                    // [NBk][65] words (bf16 pairs)
-  uint32_t* sq = sel_smem + ((NBk * kSelWords + 3) & ~3);     // [ROWS][64] words, 16-byte aligned
+  // pooled K padded with zero rows to 32 * PER rows, so the score loop runs
+  // every column group of every lane with no branch in it
+  const int per = (NBk + 31) / 32;
+  uint32_t* sk = sel_smem;                                       // [32 * PER][65] words (bf16 pairs)
+  uint32_t* sq = sel_smem + ((32 * PER * kSelWords + 3) & ~3);   // [ROWS][64] words, 16-byte aligned
   const int bh = blockIdx.y;
   const int m0 = blockIdx.x * ROWS;
   const uint4* kb = reinterpret_cast<const uint4*>(pk + (int64_t)bh * NBk * 128);
@@ -318,6 +321,7 @@ __global__ void __launch_bounds__(512) select_fused_kernel(const __nv_bfloat16* 
       }
     }
   }
+  for (int i = NBk * kSelWords + threadIdx.x; i < 32 * PER * kSelWords; i += blockDim.x) sk[i] = 0u;
   const uint4* qb = reinterpret_cast<const uint4*>(pq + (int64_t)bh * NBq * 128);
   for (int i = threadIdx.x; i < ROWS * 16; i += blockDim.x) {
     const int r = i >> 4;
@@ -326,7 +330,6 @@ __global__ void __launch_bounds__(512) select_fused_kernel(const __nv_bfloat16* 
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int per = (NBk + 31) / 32;
   {
     const int rr0 = warp * RW;  // the RW query rows of this warp
     if (m0 + rr0 >= NBq) return;
@@ -342,15 +345,13 @@ __global__ void __launch_bounds__(512) select_fused_kernel(const __nv_bfloat16* 
       for (int a = 0; a < RW; ++a) unpack_bf2(sq[(rr0 + a) * 64 + w], q0[a], q1[a]);
 #pragma unroll
       for (int i = 0; i < PER; ++i) {
-        const int j = lane + 32 * i;
-        if (i < per && j < NBk) {
-          float k0, k1;
-          unpack_bf2(sk[j * kSelWords + w], k0, k1);
+        const int j = lane + 32 * i;  // rows past NBk are zero (their scores are never selected)
+        float k0, k1;
+        unpack_bf2(sk[j * kSelWords + w], k0, k1);
 #pragma unroll
-          for (int a = 0; a < RW; ++a) {
-            acc[a][i] = __fmaf_rn(q0[a], k0, acc[a][i]);
-            acc[a][i] = __fmaf_rn(q1[a], k1, acc[a][i]);
-          }
+        for (int a = 0; a < RW; ++a) {
+          acc[a][i] = __fmaf_rn(q0[a], k0, acc[a][i]);
+          acc[a][i] = __fmaf_rn(q1[a], k1, acc[a][i]);
         }
       }
     }
@@ -375,11 +376,12 @@ int launch_select_fused(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH
   // rows per warp: 4 when the grid covers the SMs twice over, else fewer
   int rw = 4;
   while (rw > 1 && (int64_t)BH * ((NBq + 16 * rw - 1) / (16 * rw)) < 2 * sms) rw >>= 1;
-  const int smem = (((NBk * kSelWords + 3) & ~3) + 16 * rw * 64) * 4;
-  dim3 grid((NBq + 16 * rw - 1) / (16 * rw), BH);
   const int per = (NBk + 31) / 32;
+  if (per > 20 && rw > 2) rw = 2;  // 4 x 24 accumulators per thread would spill
+  dim3 grid((NBq + 16 * rw - 1) / (16 * rw), BH);
 #define ROLA_SEL(P, RW)                                                                                   \
   do {                                                                                                    \
+    const int smem = (((32 * (P) * kSelWords + 3) & ~3) + 16 * (RW) * 64) * 4;                          \
     cudaFuncSetAttribute(select_fused_kernel<P, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);  \
     select_fused_kernel<P, RW><<<grid, 512, smem, s>>>(pq, pk, NBq, NBk, k, lut);                         \
   } while (0)
