@@ -175,12 +175,16 @@ static int qkv_gemm_impl(const void* x, const void* w, const void* bias, void* o
     const uint32_t box[2] = {64, 128};
     ROLA_TRY(make_map(&ta, x, 2, dims, strides, box, "qkv_gemm: x"));
   }
+  const bool pairs = side == nullptr && M >= 256;  // the two-SM kernel (no side job)
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
     const uint64_t strides[1] = {(uint64_t)K * 2};
-    const uint32_t box[2] = {64, 256};
+    const uint32_t box[2] = {64, pairs ? 128u : 256u};
     ROLA_TRY(make_map(&tb, w, 2, dims, strides, box, "qkv_gemm: w"));
   }
+  if (pairs)
+    return cuda_status(launch_gemm_bf16_2sm(ta, tb, BF(bias), BFm(out), N, ssq, (int)M, (int)N, (int)K, S(stream)),
+                       "qkv_gemm");
   return cuda_status(launch_gemm_bf16(ta, tb, BF(bias), BFm(out), N, ssq, (int)M, (int)N, (int)K, side, S(stream)),
                      "qkv_gemm");
 }

@@ -105,6 +105,10 @@ int launch_lowrank_reduce(const float* c_partial, int splits, int BH, int R, __n
 int launch_gemm_bf16(const CUtensorMap& ta, const CUtensorMap& tb, const __nv_bfloat16* bias, __nv_bfloat16* out,
                      int64_t ldo, float* ssq, int M, int N, int K, const NormRopeParams* side, cudaStream_t s,
                      const float* scale_a = nullptr, const float* scale_b = nullptr);
+// the same product on pairs of SMs (256 x 256 tiles, tcgen05 cta_group::2); tb_half
+// maps W with 128-row boxes (each CTA of a pair stages half of a W tile).  No side job.
+int launch_gemm_bf16_2sm(const CUtensorMap& ta, const CUtensorMap& tb_half, const __nv_bfloat16* bias,
+                         __nv_bfloat16* out, int64_t ldo, float* ssq, int M, int N, int K, cudaStream_t s);
 // row-wise e4m3 quantization of a bf16 [M, K] matrix (row stride ld): scale[m] =
 // amax_k|x|/448 + 1e-12 (fp32), xq = e4m3(bf16(x / bf16(scale))) (fp8_linear.py:51-61)
 int launch_quantize_rows_e4m3(const __nv_bfloat16* x, int64_t ld, int M, int K, uint8_t* xq, float* scale,
