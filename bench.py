@@ -44,8 +44,9 @@ UNIT = "TFLOP/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) per launch of the two tensor-bound kernels, 1 GPU.
 # Attention at C4: one ncu capture of C4's sequence with 8 of the 40 heads
-# (0.80 GB), times 5 (the traffic is per head).  GEMM: one capture at C3 scaled
-# to C4 by the rows processed (75600 / 32760).  C3 as captured.
+# (0.80 GB), times 5 (the traffic is per head).  GEMM: one capture of the
+# single-SM kernel at C3 scaled to C4 by the rows processed (75600 / 32760); the
+# SM-pair kernel keeps its W re-read pattern (2048-row raster groups).  C3 as captured.
 NCU_TRAFFIC_BYTES = {"C4": {"gemm": 8.9e9, "attn": 3.98e9}, "C3": {"gemm": 3.89e9, "attn": 1.57e9}}
 
 
@@ -623,7 +624,7 @@ def main():
 
     def roof(name, ach):
         tr = NCU_TRAFFIC_BYTES.get(args.workload, {}).get(name) if world == 1 else None
-        return {"kernel": {"gemm": "gemm_tcgen05<bf16>", "attn": "sparse_attn_tcgen05"}[name], "bound": "tensor",
+        return {"kernel": {"gemm": "gemm2sm_tcgen05", "attn": "sparse_attn_tcgen05"}[name], "bound": "tensor",
                 "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
                 "peak_kind": f"{peak_kind} bf16 burst", "frac_of_sustained": ach / peak_sust, "traffic": tr,
                 "ms_per_launch": t_gemm if name == "gemm" else t_attn}
