@@ -49,12 +49,15 @@ def rel_err(got: torch.Tensor, ref: torch.Tensor, mask: torch.Tensor | None = No
     return (d.max() / rms).item(), (d.mean() / rms).item()
 
 
-def selection_report(lut: torch.Tensor, fx: dict, heads: int, boundary_ulps: float = 2) -> tuple[dict, torch.Tensor]:
-    """Per-row set agreement of this build's ``lut`` (rows of heads 0..heads-1 first)
-    with the fixture's LUT.  Returns the report and the [heads, NB] agreement mask."""
+def selection_report(lut: torch.Tensor, fx: dict, heads: int, boundary_ulps: float = 2,
+                     B: int = 1) -> tuple[dict, torch.Tensor]:
+    """Per-row set agreement of this build's ``lut`` (``[B*H, NB, k]``, rows in
+    (batch, head) order) with the fixture's LUT, which holds heads 0..heads-1 of
+    every batch element in the same order.  Returns the report and the
+    ``[B*heads, NB]`` agreement mask."""
     ref = fx["lut"].long()
     _, NB, k = ref.shape
-    mine = lut.detach().cpu().long().reshape(-1, NB, k)[:heads]
+    mine = lut.detach().cpu().long().reshape(B, -1, NB, k)[:, :heads].reshape(B * heads, NB, k)
     vals, idx = fx["score_vals"].float(), fx["score_idx"].long()
     agree = (torch.sort(mine, -1).values == torch.sort(ref, -1).values).all(-1)
     rep = {"rows": int(agree.numel()), "agree": int(agree.sum()), "tie": 0, "boundary": 0, "unexplained": 0,
@@ -94,16 +97,16 @@ def sample_out(out: torch.Tensor, fx: dict, B: int, L: int, heads: int) -> torch
 
 
 def agree_mask(agree: torch.Tensor, fx: dict, heads: int, blk: int) -> torch.Tensor:
-    """``[1, S, heads*D]`` mask of sampled output elements whose query block's kept sets agree."""
-    a = agree[:, fx["tokens"].long() // blk].t()  # [S, heads]
-    return a[:, :, None].expand(-1, -1, HEAD_DIM).reshape(1, -1, heads * HEAD_DIM)
+    """``[B, S, heads*D]`` mask of sampled output elements whose query block's kept sets agree."""
+    a = agree.reshape(-1, heads, agree.shape[-1])[:, :, fx["tokens"].long() // blk].transpose(1, 2)  # [B, S, heads]
+    return a[..., None].expand(-1, -1, -1, HEAD_DIM).reshape(a.shape[0], -1, heads * HEAD_DIM)
 
 
 def output_parity(out: torch.Tensor, lut: torch.Tensor, fx: dict, B: int, L: int, H: int, blk: int) -> dict:
     """Selection report plus the gated output's error against the reference's on
     the sampled rows of the query blocks whose kept sets agree."""
     heads = fx["config"]["H"]
-    rep, agree = selection_report(lut, fx, heads)
+    rep, agree = selection_report(lut, fx, heads, B=B)
     mx, mn = rel_err(sample_out(out, fx, B, L, heads), fx["out"], agree_mask(agree, fx, heads, blk))
     return {"heads": heads, "lut_rows": rep["rows"], "lut_agree": rep["agree"], "lut_tie": rep["tie"],
             "lut_boundary": rep["boundary"], "lut_unexplained": rep["unexplained"],

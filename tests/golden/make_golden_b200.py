@@ -16,6 +16,9 @@ on seeded inputs and stores what the GPU tests need to compare against it:
   rank 64; from hidden states through the reference's cuBLAS projections and
   epilogue), the first ``C4_HEADS`` heads for selection, attention, low rank
   and gate (heads are independent after the prologue).
+* ``ref_b200_c5.pt``: configuration C5 (B=2: cond and uncond batched, H=40,
+  L=32760, top-13; from hidden states like C4), the first ``C4_HEADS`` heads of
+  both batch elements.
 
 Per configuration: the reference's LUT in its own (``torch.topk(sorted=False)``)
 order, its bf16 pooled scores of the top ``k + EXTRA`` key blocks of every row
@@ -49,11 +52,12 @@ sys.path.insert(0, ROOT)
 
 from oracle import rola_oracle as orc  # noqa: E402
 from sparkdiffusion_b200.rope import prepare_cos_sin, prepare_lowrank_cos_sin, wan_rope_freqs  # noqa: E402
-from sparkdiffusion_b200.workloads import C2, C4, make_inputs  # noqa: E402
+from sparkdiffusion_b200.workloads import C2, C4, C5, make_inputs  # noqa: E402
 
 EXTRA = 38          # stored scores per row: top k + EXTRA
 C2_TOKENS = 192     # sampled token rows
 C4_TOKENS = 256
+C5_TOKENS = 192
 C4_HEADS = 4
 ORACLE_HEADS = 2    # heads of C2 on which the reference is compared with the oracle
 
@@ -192,8 +196,7 @@ def make_c2(m) -> dict:
     return pack_result(wl, r, sample_tokens(L, C2_TOKENS, 11), sums, {"ref_vs_oracle": rvo})
 
 
-def make_c4(m) -> dict:
-    wl = C4
+def make_c4(m, wl=C4, tokens=C4_TOKENS, seed=12) -> dict:
     B, L, H, dim = wl.B, wl.L, wl.H, wl.dim
     inp = make_inputs(wl, device="cpu")
     sums = {k: checksum(v) for k, v in inp.items() if isinstance(v, torch.Tensor)}
@@ -209,13 +212,14 @@ def make_c4(m) -> dict:
         inp["norm_wk"].cuda(), H, 128, eps=1e-6, return_normed=True, fp8_weights=None, cos_sin=cos_sin)
     r = run_reference_tail(m, q_rope, k_rope, v_out, q_n, k_n, x, inp, wl, H, lr_tables,
                            heads=slice(0, C4_HEADS))
-    return pack_result(wl, r, sample_tokens(L, C4_TOKENS, 12), sums, {})
+    return pack_result(wl, r, sample_tokens(L, tokens, seed), sums, {})
 
 
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SPARKDIFFUSION_REF",
                                                               os.path.join(ROOT, "baseline", "_ref"))
     out_dir = sys.argv[2] if len(sys.argv) > 2 else os.path.join(ROOT, "gpurun_out")
+    which = (sys.argv[3] if len(sys.argv) > 3 else "c2,c4,c5").split(",")
     if not os.path.isdir(os.path.join(ref, "sparkdiffusion")):
         raise SystemExit(f"reference package not found under {ref}")
     if not torch.cuda.is_available():
@@ -223,15 +227,16 @@ def main():
     os.makedirs(out_dir, exist_ok=True)
     torch.cuda.set_device(0)
     m = import_reference(ref)
+    makers = {"c2": lambda: make_c2(m), "c4": lambda: make_c4(m),
+              "c5": lambda: make_c4(m, C5, C5_TOKENS, 13)}
     with torch.no_grad():
-        t0 = time.time()
-        c2 = make_c2(m)
-        torch.save(c2, os.path.join(out_dir, "ref_b200_c2.pt"))
-        print(f"C2 done in {time.time() - t0:.1f} s", flush=True)
-        t0 = time.time()
-        c4 = make_c4(m)
-        torch.save(c4, os.path.join(out_dir, "ref_b200_c4.pt"))
-        print(f"C4 done in {time.time() - t0:.1f} s", flush=True)
+        for name in which:
+            t0 = time.time()
+            fx = makers[name]()
+            torch.save(fx, os.path.join(out_dir, f"ref_b200_{name}.pt"))
+            print(f"{name} done in {time.time() - t0:.1f} s", flush=True)
+            del fx
+            torch.cuda.empty_cache()
 
 
 if __name__ == "__main__":

@@ -1,10 +1,10 @@
 """Parity against the reference's own bf16 fused path run on a B200.
 
-The fixtures ``tests/golden/ref_b200_{c2,c4}.pt`` hold what the unmodified
+The fixtures ``tests/golden/ref_b200_{c2,c4,c5}.pt`` hold what the unmodified
 SparkDiffusion fused inference path (``fused_qkv_gemm_rope`` or its epilogue
 kernel, ``fused_sparse_attn``, ``fused_lowrank``, ``fused_gate``, as
 ``WanSelfAttentionRoLa.fused_forward`` chains them, wan_rola_attention.py:414-446)
-produced on a B200 for the seeded C2 and C4 inputs (``make_golden_b200.py``).
+produced on a B200 for the seeded C2, C4 and C5 inputs (``make_golden_b200.py``).
 Checked here, at the full BASELINE shapes:
 
 (i)   selection: per-row set agreement of this build's LUT with the reference's;
@@ -20,7 +20,7 @@ Checked here, at the full BASELINE shapes:
       tolerance of the reference's output.
 
 Outputs are compared on the fixture's seeded sample of token rows (all heads of
-C2, heads 0-3 of C4).  Tolerance: max-abs <= 2e-2 and mean-abs <= 2e-3 of the
+C2, heads 0-3 of C4 and of both batch elements of C5).  Tolerance: max-abs <= 2e-2 and mean-abs <= 2e-3 of the
 RMS of the reference's sampled output.
 """
 
@@ -30,7 +30,7 @@ import torch
 from conftest import BF16_MAX, BF16_MEAN, assert_bf16_close, assert_ulp_close
 from sparkdiffusion_b200 import _lib, ops, refcheck
 from sparkdiffusion_b200.rope import prepare_cos_sin, prepare_lowrank_cos_sin, wan_rope_freqs
-from sparkdiffusion_b200.workloads import C2, C4, make_inputs
+from sparkdiffusion_b200.workloads import C2, C4, C5, make_inputs
 
 pytestmark = pytest.mark.gpu
 
@@ -72,8 +72,8 @@ _sample_out = refcheck.sample_out
 _agree_mask = refcheck.agree_mask
 
 
-def selection_report(lut, fx, heads):
-    return refcheck.selection_report(lut, fx, heads, BOUNDARY_ULPS)
+def selection_report(lut, fx, heads, B=1):
+    return refcheck.selection_report(lut, fx, heads, BOUNDARY_ULPS, B)
 
 
 def test_c2_against_reference_b200():
@@ -104,11 +104,13 @@ def test_c2_against_reference_b200():
                   "out (own LUT, agreeing blocks) vs reference")
 
 
-def test_c4_against_reference_b200():
-    """C4 from the hidden states (all 40 heads through the prologue, whose norm
-    spans every head); heads 0-3 compared with the reference."""
-    wl = C4
-    fx = _load("c4")
+@pytest.mark.parametrize("name", ["c4", "c5"])
+def test_from_hidden_states_against_reference_b200(name):
+    """C4 and C5 (B = 2: cond and uncond) from the hidden states (all 40 heads
+    through the prologue, whose norm spans every head); heads 0-3 of every batch
+    element compared with the reference."""
+    wl = {"c4": C4, "c5": C5}[name]
+    fx = _load(name)
     hs = fx["config"]["H"]
     B, L, H = wl.B, wl.L, wl.H
     g, (cos_sin, lr_cos, lr_sin, rope_dim) = _inputs(wl, fx)
@@ -119,12 +121,13 @@ def test_c4_against_reference_b200():
     assert _lib.device_status() == 0
     assert_ulp_close(_sample_heads(ex["q_rope"], fx, B, L, H, hs), fx["q_rope"].float(), "q_rope vs reference",
                      ulps=2, max_frac=2e-2)
-    rep, agree = selection_report(ex["lut"], fx, hs)
-    print(f"C4 selection vs reference (heads 0-{hs - 1}): {rep}")
+    rep, agree = selection_report(ex["lut"], fx, hs, B)
+    print(f"{name} selection vs reference (heads 0-{hs - 1}): {rep}")
     assert rep["unexplained"] == 0, rep
-    # reference LUT injected for heads 0-3 (the other heads keep this build's)
-    lut = ex["lut"].clone().view(B * H, wl.NB, wl.topk)
-    lut[:hs] = fx["lut"].to(torch.int32).cuda()
+    # reference LUT injected for heads 0-3 of every batch element (the other heads keep this build's)
+    lut = ex["lut"].clone().view(B, H, wl.NB, wl.topk)
+    lut[:, :hs] = fx["lut"].to(torch.int32).cuda().view(B, hs, wl.NB, wl.topk)
+    lut = lut.view(B * H, wl.NB, wl.topk)
     qkv = ex["qkv"]
     dim = wl.dim
     out_r, ex_r = ops.rola_attention_from_qkv(qkv[..., :dim], qkv[..., dim:2 * dim], qkv[..., 2 * dim:], g["x"],
