@@ -20,14 +20,18 @@ Checked here, at the full BASELINE shapes:
       tolerance of the reference's output.
 
 Outputs are compared on the fixture's seeded sample of token rows (all heads of
-C2, heads 0-3 of C4 and of both batch elements of C5).  Tolerance: max-abs <= 2e-2 and mean-abs <= 2e-3 of the
-RMS of the reference's sampled output.
+C2, heads 0-3 of C4 and of both batch elements of C5).  Tolerance: mean-abs <=
+2e-3 of the RMS of the reference's sampled output, and max-abs <= 2e-2 of it or,
+element by element, one bf16 rounding step of the reference's value: both sides
+are rounded to bf16, so an element several times the RMS can differ by one step
+(C5's o_sparse: one such element, 3.3e-2 of the RMS, mean 9e-6), which alone
+exceeds 2e-2 of the RMS.
 """
 
 import pytest
 import torch
 
-from conftest import BF16_MAX, BF16_MEAN, assert_bf16_close, assert_ulp_close
+from conftest import BF16_MAX, BF16_MEAN, assert_ulp_close
 from sparkdiffusion_b200 import _lib, ops, refcheck
 from sparkdiffusion_b200.rope import prepare_cos_sin, prepare_lowrank_cos_sin, wan_rope_freqs
 from sparkdiffusion_b200.workloads import C2, C4, C5, make_inputs
@@ -64,7 +68,9 @@ def _inputs(wl, fx):
 
 def _masked_close(got, ref, mask, name):
     mx, mn = refcheck.rel_err(got, ref, mask)
-    assert mx <= BF16_MAX and mn <= BF16_MEAN, f"{name}: max-abs/rms={mx:.3e} mean-abs/rms={mn:.3e}"
+    worst = refcheck.worst_of_bound(got, ref, mask)
+    assert (mx <= BF16_MAX or worst <= 1.0) and mn <= BF16_MEAN, (
+        f"{name}: max-abs/rms={mx:.3e} ({worst:.2f} of the per-element bound) mean-abs/rms={mn:.3e}")
 
 
 _sample_heads = refcheck.sample_heads
@@ -96,9 +102,9 @@ def test_c2_against_reference_b200():
     out_r, ex_r = ops.rola_attention_from_qkv(*args, keep=True, lut=fx["lut"].to(torch.int32).cuda())
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
-    assert_bf16_close(_sample_heads(ex_r["o_sparse"], fx, B, L, H, H), fx["o_sparse"].float(),
-                      "o_sparse (reference LUT) vs reference")
-    assert_bf16_close(_sample_out(out_r, fx, B, L, H), fx["out"].float(), "out (reference LUT) vs reference")
+    _masked_close(_sample_heads(ex_r["o_sparse"], fx, B, L, H, H), fx["o_sparse"].float(), None,
+                  "o_sparse (reference LUT) vs reference")
+    _masked_close(_sample_out(out_r, fx, B, L, H), fx["out"].float(), None, "out (reference LUT) vs reference")
     # (iii) own LUT, on the query blocks whose kept sets agree
     _masked_close(_sample_out(out, fx, B, L, H), fx["out"].float(), _agree_mask(agree, fx, H, wl.blk),
                   "out (own LUT, agreeing blocks) vs reference")
@@ -136,8 +142,8 @@ def test_from_hidden_states_against_reference_b200(name):
                                               keep=True, lut=lut)
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
-    assert_bf16_close(_sample_heads(ex_r["o_sparse"], fx, B, L, H, hs), fx["o_sparse"].float(),
-                      "o_sparse (reference LUT) vs reference")
-    assert_bf16_close(_sample_out(out_r, fx, B, L, hs), fx["out"].float(), "out (reference LUT) vs reference")
+    _masked_close(_sample_heads(ex_r["o_sparse"], fx, B, L, H, hs), fx["o_sparse"].float(), None,
+                  "o_sparse (reference LUT) vs reference")
+    _masked_close(_sample_out(out_r, fx, B, L, hs), fx["out"].float(), None, "out (reference LUT) vs reference")
     _masked_close(_sample_out(out, fx, B, L, hs), fx["out"].float(), _agree_mask(agree, fx, hs, wl.blk),
                   "out (own LUT, agreeing blocks) vs reference")
