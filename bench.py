@@ -370,7 +370,8 @@ def check_parity(args, wl, out1, lut1, step, x, rank, world, dev) -> dict:
     if fx is not None:
         r = refcheck.output_parity(out1, lut1, fx, B, L, H, wl.blk)
         # max-abs <= 2e-2 of the RMS, or (for outputs several times their RMS, where one
-        # bf16 step exceeds that) every element within one bf16 step of the reference's
+        # bf16 step exceeds that) every element within two bf16 steps of the reference's
+        # (this build's own LUT visits the blocks in another order than the reference's)
         r["ok"] = (r["lut_unexplained"] == 0 and r["out_mean_rel"] <= 2e-3
                    and (r["out_max_rel"] <= 2e-2 or r["out_worst_of_bound"] <= 1.0))
         res["vs_reference_b200"] = r

@@ -50,14 +50,14 @@ def rel_err(got: torch.Tensor, ref: torch.Tensor, mask: torch.Tensor | None = No
 
 
 def worst_of_bound(got: torch.Tensor, ref: torch.Tensor, mask: torch.Tensor | None = None,
-                   max_tol: float = 2e-2) -> float:
-    """Largest |got - ref| over the per-element bound max(max_tol * RMS(ref), one
-    bf16 step of the reference element): two bf16 results of the same value can
-    sit one rounding step apart, and for an element several times the RMS that
-    step alone exceeds 2e-2 of the RMS.  <= 1 means every element is within it."""
+                   max_tol: float = 2e-2, steps: float = 1.0) -> float:
+    """Largest |got - ref| over the per-element bound max(max_tol * RMS(ref),
+    ``steps`` bf16 steps of the reference element): two bf16 results of the same
+    value can sit a rounding step apart, and for an element several times the RMS
+    that step alone exceeds 2e-2 of the RMS.  <= 1 means every element is within it."""
     g, r = got.float().cpu(), ref.float().cpu()
     rms = r.pow(2).mean().sqrt().clamp_min(1e-30)
-    ratio = (g - r).abs() / torch.maximum(max_tol * rms, bf16_ulp(r))
+    ratio = (g - r).abs() / torch.maximum(max_tol * rms, steps * bf16_ulp(r))
     if mask is not None:
         ratio = ratio[mask]
     return ratio.max().item()
@@ -125,5 +125,6 @@ def output_parity(out: torch.Tensor, lut: torch.Tensor, fx: dict, B: int, L: int
     mx, mn = rel_err(got, fx["out"], mask)
     return {"heads": heads, "lut_rows": rep["rows"], "lut_agree": rep["agree"], "lut_tie": rep["tie"],
             "lut_boundary": rep["boundary"], "lut_unexplained": rep["unexplained"],
-            "out_max_rel": mx, "out_mean_rel": mn, "out_worst_of_bound": worst_of_bound(got, fx["out"], mask),
+            "out_max_rel": mx, "out_mean_rel": mn,
+            "out_worst_of_bound": worst_of_bound(got, fx["out"], mask, steps=2.0),
             "sampled_tokens": int(fx["tokens"].numel())}

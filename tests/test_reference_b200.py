@@ -25,7 +25,11 @@ C2, heads 0-3 of C4 and of both batch elements of C5).  Tolerance: mean-abs <=
 element by element, one bf16 rounding step of the reference's value: both sides
 are rounded to bf16, so an element several times the RMS can differ by one step
 (C5's o_sparse: one such element, 3.3e-2 of the RMS, mean 9e-6), which alone
-exceeds 2e-2 of the RMS.
+exceeds 2e-2 of the RMS.  With this build's own LUT (ascending, where the
+reference's is in torch.topk order) the online softmax visits the same blocks in
+another order, so P is rounded to bf16 against other running maxima and the
+gated output may differ by up to two steps per element (C5: 1.6 steps at one
+element, mean 5.8e-4 of the RMS).
 """
 
 import pytest
@@ -66,9 +70,9 @@ def _inputs(wl, fx):
     return g, (cos_sin.cuda(), lr_cos.cuda(), lr_sin.cuda(), rope_dim)
 
 
-def _masked_close(got, ref, mask, name):
+def _masked_close(got, ref, mask, name, steps=1.0):
     mx, mn = refcheck.rel_err(got, ref, mask)
-    worst = refcheck.worst_of_bound(got, ref, mask)
+    worst = refcheck.worst_of_bound(got, ref, mask, steps=steps)
     assert (mx <= BF16_MAX or worst <= 1.0) and mn <= BF16_MEAN, (
         f"{name}: max-abs/rms={mx:.3e} ({worst:.2f} of the per-element bound) mean-abs/rms={mn:.3e}")
 
@@ -107,7 +111,7 @@ def test_c2_against_reference_b200():
     _masked_close(_sample_out(out_r, fx, B, L, H), fx["out"].float(), None, "out (reference LUT) vs reference")
     # (iii) own LUT, on the query blocks whose kept sets agree
     _masked_close(_sample_out(out, fx, B, L, H), fx["out"].float(), _agree_mask(agree, fx, H, wl.blk),
-                  "out (own LUT, agreeing blocks) vs reference")
+                  "out (own LUT, agreeing blocks) vs reference", steps=2.0)
 
 
 @pytest.mark.parametrize("name", ["c4", "c5"])
@@ -146,4 +150,4 @@ def test_from_hidden_states_against_reference_b200(name):
                   "o_sparse (reference LUT) vs reference")
     _masked_close(_sample_out(out_r, fx, B, L, hs), fx["out"].float(), None, "out (reference LUT) vs reference")
     _masked_close(_sample_out(out, fx, B, L, hs), fx["out"].float(), _agree_mask(agree, fx, hs, wl.blk),
-                  "out (own LUT, agreeing blocks) vs reference")
+                  "out (own LUT, agreeing blocks) vs reference", steps=2.0)
