@@ -265,6 +265,36 @@ int rola_b200_sparse_attn_scatter(const void* q, const void* k, int64_t qk_sB, i
                                   float eps_lr, void* const* out_dst, int world, int head_offset, int H_total,
                                   rola_stream_t stream);
 
+/* (f4) Training forward of the block-sparse attention: out = the plain
+ * attention output (no low-rank branch, no gate), plus lse [B*H, Lpad] fp32
+ * (Lpad = 128 * ceil(L / 128)), the base-2 log-sum-exp of each row in units of
+ * D^-1/2 log2(e) (+inf on the padding rows), which the backward reads.  Sizes,
+ * strides and the lut convention (paired table for blk 64) as
+ * rola_b200_sparse_attn.  Replaces the forward of the external SLA kernel the
+ * reference trains with (`_attention.apply`, wan_rola_attention.py:320-321). */
+int rola_b200_sparse_attn_fwd_lse(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT,
+                                  const void* v, int64_t v_sB, int64_t v_sH, int64_t v_sT, const int32_t* lut, int B,
+                                  int L, int H, int blk, int topk, void* out, int64_t o_sB, int64_t o_sH, int64_t o_sT,
+                                  float* lse, rola_stream_t stream);
+
+/* Bytes of device workspace rola_b200_sparse_attn_bwd needs (0 for bad sizes). */
+size_t rola_b200_sparse_attn_bwd_workspace(int B, int L, int H, int blk);
+
+/* (f4) Backward of the block-sparse attention: dq, dk, dv (bf16, element
+ * (b, h, t, d) at p + g_sB*b + g_sH*h + g_sT*t + d) from q, k, v, the forward's
+ * out and lse, and dout (out and dout share o_s*).  lut is the selection
+ * [B*H, NB, topk] (blk 128 or 64); for blk 64, paired is its
+ * rola_b200_pair_blocks table (the forward's lut).  Exact gradient of the
+ * forward; no atomics (deterministic).  workspace: 16-byte aligned, at least
+ * rola_b200_sparse_attn_bwd_workspace bytes.  Replaces the backward of the
+ * external SLA kernel (`_attention.apply`, wan_rola_attention.py:320-321). */
+int rola_b200_sparse_attn_bwd(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT, const void* v,
+                              int64_t v_sB, int64_t v_sH, int64_t v_sT, const void* out, const void* dout, int64_t o_sB,
+                              int64_t o_sH, int64_t o_sT, const int32_t* lut, const int32_t* paired, const float* lse,
+                              int B, int L, int H, int blk, int topk, void* dq, void* dk, void* dv, int64_t g_sB,
+                              int64_t g_sH, int64_t g_sT, void* workspace, size_t workspace_bytes,
+                              rola_stream_t stream);
+
 /* Peer memory of the fused exchanges (CUDA IPC; no counterpart in the
  * reference).  peer_alloc: cudaMalloc of bytes on the current device and its
  * ROLA_PEER_HANDLE_BYTES-byte IPC handle; peer_open: map a handle made by

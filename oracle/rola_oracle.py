@@ -13,6 +13,11 @@ fp32 and its eager PyTorch pieces in bf16); the resulting golden vectors live
 in ``tests/golden`` together with the script that made them
 (``tests/golden/make_golden.py``).
 
+The training section (f4) restates the gradient of the block-sparse attention
+that the reference takes from the external SLA package; the package is absent,
+so that section is pinned against torch.autograd of its own forward
+restatement (parity of the backward against the SLA kernel itself: unpinned).
+
 Every function cites the reference file:line it restates (paths relative to
 the SparkDiffusion project root).
 
@@ -350,6 +355,73 @@ def sparse_attn_lut(q4, k4, v4, lut, blkq: int, blkk: int, out_dtype=None) -> to
         m_i = new_m
     o = (acc / l_i[..., None]).to(out_dtype or dt)
     return o.reshape(B, H, NBq * blkq, D)[:, :, :L].contiguous()
+
+
+# ---------------------------------------------------------------------------
+# (f4) training: the block-sparse attention and its exact gradient
+# ---------------------------------------------------------------------------
+# The reference trains through the external SLA package
+# (`_attention.apply(q, k, v, sparse_map, lut, real_topk, BLKQ, BLKK)`,
+# wan_rola_attention.py:293-327; the package is loaded from `SLA_SRC`,
+# :97-109, and is not part of the reference tree nor of this container, so no
+# version is pinned).  Its published algorithm is block-sparse softmax
+# attention, each query block attending to the key blocks of its LUT row, and
+# its backward is the exact gradient of that function.  Parity of the backward
+# is therefore pinned against torch.autograd of ``block_sparse_attention``
+# below (tests/test_oracle_backward.py), not against outputs of the SLA kernel.
+def block_mask(lut: torch.Tensor, L: int, blkq: int, blkk: int) -> torch.Tensor:
+    """``[B*H, L, L]`` bool: row t may attend to column u when the key block of
+    u is in the LUT row of the query block of t (small cases only)."""
+    lut = lut.long()
+    BH, NBq, _ = lut.shape
+    NBk = (L + blkk - 1) // blkk
+    sel = torch.zeros(BH, NBq, NBk, dtype=torch.bool)
+    sel.scatter_(-1, lut, True)
+    rows = torch.arange(L) // blkq
+    cols = torch.arange(L) // blkk
+    return sel[:, rows][:, :, cols]
+
+
+def block_sparse_attention(q4, k4, v4, lut, blkq: int, blkk: int, dtype=torch.float64):
+    """o = softmax_masked(q k^T D^-1/2) v over ``[B, H, L, D]`` in ``dtype``,
+    with the base-2 log-sum-exp per row (units of D^-1/2 log2 e, the forward
+    kernel's ``lse``).  Differentiable (plain torch ops)."""
+    B, H, L, D = q4.shape
+    mask = block_mask(lut.reshape(B * H, -1, lut.shape[-1]), L, blkq, blkk).reshape(B, H, L, L)
+    s = torch.matmul(q4.to(dtype), k4.to(dtype).transpose(-1, -2)) * D ** -0.5
+    s = s.masked_fill(~mask, -math.inf)
+    o = torch.matmul(torch.softmax(s, dim=-1), v4.to(dtype))
+    lse2 = torch.logsumexp(s, dim=-1) * LOG2E
+    return o, lse2
+
+
+def block_sparse_attention_backward(q4, k4, v4, lut, do4, blkq: int, blkk: int, dtype=torch.float64,
+                                    round_dtype=None, o_fwd=None):
+    """Exact gradient (dq, dk, dv) of ``block_sparse_attention``, written out:
+    P = softmax_masked(S), dV = P^T dO, dP = dO V^T, delta = rowsum(dO * O),
+    dS = P (dP - delta), dQ = D^-1/2 dS K, dK = D^-1/2 dS^T Q.
+
+    ``round_dtype`` (e.g. bf16) models the materialisation points of a
+    flash-style backward: P and dS are rounded before the products that take
+    them (dV, dQ, dK), and delta uses ``o_fwd``, the forward's materialised
+    output (``sparse_attn_lut``, whose P was rounded before P.V), when given."""
+    B, H, L, D = q4.shape
+    mask = block_mask(lut.reshape(B * H, -1, lut.shape[-1]), L, blkq, blkk).reshape(B, H, L, L)
+    q, k, v, do = (t.to(dtype) for t in (q4, k4, v4, do4))
+
+    def rnd(t):
+        return t if round_dtype is None else t.to(round_dtype).to(dtype)
+
+    s = (torch.matmul(q, k.transpose(-1, -2)) * D ** -0.5).masked_fill(~mask, -math.inf)
+    p = torch.softmax(s, dim=-1)
+    o = rnd(torch.matmul(p, v)) if o_fwd is None else o_fwd.to(dtype)
+    dv = torch.matmul(rnd(p).transpose(-1, -2), do)
+    dp = torch.matmul(do, v.transpose(-1, -2))
+    delta = (do * o).sum(-1, keepdim=True)
+    ds = rnd(p * (dp - delta))
+    dq = torch.matmul(ds, k) * D ** -0.5
+    dk = torch.matmul(ds.transpose(-1, -2), q) * D ** -0.5
+    return dq, dk, dv
 
 
 # ---------------------------------------------------------------------------

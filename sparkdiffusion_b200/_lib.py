@@ -63,6 +63,11 @@ SIGNATURES = {
                               _P, _L, _L, _L, _P, _P, _F, _P, _P, _L, _L, _L, _P],
     "rola_b200_sparse_attn_scatter": [_P, _P, _L, _L, _L, _P, _L, _L, _L, _P, _I, _I, _I, _I, _I, _P, _P,
                                       _P, _F, _P, _I, _I, _I, _P],
+    "rola_b200_sparse_attn_fwd_lse": [_P, _P, _L, _L, _L, _P, _L, _L, _L, _P, _I, _I, _I, _I, _I, _P, _L, _L, _L,
+                                      _P, _P],
+    "rola_b200_sparse_attn_bwd_workspace": [_I, _I, _I, _I],
+    "rola_b200_sparse_attn_bwd": [_P, _P, _L, _L, _L, _P, _L, _L, _L, _P, _P, _L, _L, _L, _P, _P, _P, _I, _I, _I,
+                                  _I, _I, _P, _P, _P, _L, _L, _L, _P, _Z, _P],
     "rola_b200_peer_alloc": [_Z, ctypes.POINTER(_P), _P],
     "rola_b200_peer_open": [_P, ctypes.POINTER(_P)],
     "rola_b200_peer_close": [_P],
@@ -81,6 +86,7 @@ SIGNATURES = {
 _RESTYPES = {
     "rola_b200_last_error": ctypes.c_char_p,
     "rola_b200_forward_workspace_bytes": _Z,
+    "rola_b200_sparse_attn_bwd_workspace": _Z,
 }
 
 MAX_RANKS = 8

@@ -520,6 +520,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       const bool staged = p.out != nullptr || p.peer_n > 0;
       if (ok) {
         const int tok = (m0 + t) * 128 + row;
+        if (p.lse) p.lse[(int64_t)bh * p.lse_ld + tok] = tok < p.L ? m_run + log2f(l_run) : INFINITY;
         const float inv_l = 1.0f / l_run;
         const uint64_t il2 = f2_pack(inv_l, inv_l);
         // one pass over TMEM: the row's o_sparse and o_lr values, rounded to

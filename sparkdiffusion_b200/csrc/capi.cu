@@ -572,7 +572,7 @@ static int sparse_attn_impl(const void* q, const void* k, int64_t qk_sB, int64_t
                             int topk, const void* q_lr, const void* Ct, const void* gate, const void* x, int64_t x_sB,
                             int64_t x_sH, int64_t x_sT, const void* gate_w, const void* gate_b, float eps_lr,
                             void* out, void* o_sparse, int64_t o_sB, int64_t o_sH, int64_t o_sT, const PeerOut* peer,
-                            rola_stream_t stream) {
+                            rola_stream_t stream, float* lse = nullptr) {
   ROLA_CHECK(q && k && v && lut, "sparse_attn: null pointer");
   ROLA_CHECK(out || o_sparse || peer, "sparse_attn: no output requested");
   ROLA_CHECK(blk == 128 || blk == 64, "sparse_attn: block size must be 128 or 64");
@@ -623,6 +623,8 @@ static int sparse_attn_impl(const void* q, const void* k, int64_t qk_sB, int64_t
   p.qk_scale = (float)(0.08838834764831845 * 1.4426950408889634);  // 128^-0.5 * log2(e)
   p.eps_lr = eps_lr;
   p.rescale_threshold = ROLA_RESCALE_THRESHOLD;
+  p.lse = lse;
+  p.lse_ld = 128 * ((L + 127) / 128);
   if (peer) {
     p.peer_n = peer->world;
     p.peer_Ls = L / peer->world;
@@ -656,6 +658,110 @@ int rola_b200_sparse_attn_scatter(const void* q, const void* k, int64_t qk_sB, i
   const PeerOut peer{out_dst, world, head_offset, H_total};
   return sparse_attn_impl(q, k, qk_sB, qk_sH, qk_sT, v, v_sB, v_sH, v_sT, lut, B, L, H, blk, topk, q_lr, Ct, gate,
                           nullptr, 0, 0, 0, nullptr, nullptr, eps_lr, nullptr, nullptr, 0, 0, 0, &peer, stream);
+}
+
+// ---------------------------------------------------------------------------
+// training: forward with the row log-sum-exp, backward
+// ---------------------------------------------------------------------------
+int rola_b200_sparse_attn_fwd_lse(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT,
+                                  const void* v, int64_t v_sB, int64_t v_sH, int64_t v_sT, const int32_t* lut, int B,
+                                  int L, int H, int blk, int topk, void* out, int64_t o_sB, int64_t o_sH, int64_t o_sT,
+                                  float* lse, rola_stream_t stream) {
+  ROLA_CHECK(out && lse, "sparse_attn_fwd_lse: null pointer");
+  ROLA_CHECK(aligned16(lse), "sparse_attn_fwd_lse: lse must be 16-byte aligned");
+  return sparse_attn_impl(q, k, qk_sB, qk_sH, qk_sT, v, v_sB, v_sH, v_sT, lut, B, L, H, blk, topk, nullptr, nullptr,
+                          nullptr, nullptr, 0, 0, 0, nullptr, nullptr, 0.f, out, nullptr, o_sB, o_sH, o_sT, nullptr,
+                          stream, lse);
+}
+
+struct BwdLayout {
+  size_t delta, map, inv, total;
+  int NB, NT, Lpad, width;
+};
+
+static BwdLayout bwd_layout(int B, int L, int H, int blk) {
+  BwdLayout f{};
+  f.NB = (L + blk - 1) / blk;
+  f.NT = (L + 127) / 128;
+  f.Lpad = 128 * f.NT;
+  f.width = f.NB + 2;
+  const size_t BH = (size_t)B * H;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  f.delta = take(BH * f.Lpad * 4);
+  f.map = take(BH * f.NB * f.NB);
+  f.inv = take(BH * f.NT * f.width * 4);
+  f.total = off;
+  return f;
+}
+
+size_t rola_b200_sparse_attn_bwd_workspace(int B, int L, int H, int blk) {
+  if (B <= 0 || L <= 0 || H <= 0 || (blk != 64 && blk != 128)) return 0;
+  return bwd_layout(B, L, H, blk).total;
+}
+
+int rola_b200_sparse_attn_bwd(const void* q, const void* k, int64_t qk_sB, int64_t qk_sH, int64_t qk_sT, const void* v,
+                              int64_t v_sB, int64_t v_sH, int64_t v_sT, const void* out, const void* dout, int64_t o_sB,
+                              int64_t o_sH, int64_t o_sT, const int32_t* lut, const int32_t* paired, const float* lse,
+                              int B, int L, int H, int blk, int topk, void* dq, void* dk, void* dv, int64_t g_sB,
+                              int64_t g_sH, int64_t g_sT, void* workspace, size_t workspace_bytes,
+                              rola_stream_t stream) {
+  ROLA_CHECK(q && k && v && out && dout && lut && lse && dq && dk && dv && workspace,
+             "sparse_attn_bwd: null pointer");
+  ROLA_CHECK(blk == 128 || blk == 64, "sparse_attn_bwd: block size must be 128 or 64");
+  ROLA_CHECK(blk == 128 || paired, "sparse_attn_bwd: block 64 needs the paired table");
+  ROLA_CHECK(B > 0 && L > 0 && H > 0 && (int64_t)B * H < 65536, "sparse_attn_bwd: bad sizes");
+  const BwdLayout f = bwd_layout(B, L, H, blk);
+  ROLA_CHECK(f.NB < (1 << 28), "sparse_attn_bwd: too many blocks");
+  ROLA_CHECK(topk >= 1 && topk <= f.NB, "sparse_attn_bwd: topk must be in [1, NB]");
+  ROLA_CHECK(workspace_bytes >= f.total, "sparse_attn_bwd: workspace of %zu bytes < %zu", workspace_bytes, f.total);
+  ROLA_CHECK(aligned16(workspace) && aligned16(lse), "sparse_attn_bwd: workspace and lse must be 16-byte aligned");
+  ROLA_CHECK(aligned16(out) && aligned16(dout) && o_sB % 8 == 0 && o_sH % 8 == 0 && o_sT % 8 == 0,
+             "sparse_attn_bwd: out / dout rows must be 16-byte aligned");
+  ROLA_CHECK(aligned16(dq) && aligned16(dk) && aligned16(dv) && g_sB % 8 == 0 && g_sH % 8 == 0 && g_sT % 8 == 0,
+             "sparse_attn_bwd: gradient rows must be 16-byte aligned");
+  CUtensorMap tq, tk, tv, tdo;
+  ROLA_TRY(make_head_map(&tq, q, 128, qk_sB, qk_sH, qk_sT, L, H, B, "sparse_attn_bwd: q", blk));
+  ROLA_TRY(make_head_map(&tk, k, 128, qk_sB, qk_sH, qk_sT, L, H, B, "sparse_attn_bwd: k", blk));
+  ROLA_TRY(make_head_map(&tv, v, 128, v_sB, v_sH, v_sT, L, H, B, "sparse_attn_bwd: v", blk));
+  ROLA_TRY(make_head_map(&tdo, dout, 128, o_sB, o_sH, o_sT, L, H, B, "sparse_attn_bwd: dout", blk));
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* delta = reinterpret_cast<float*>(ws + f.delta);
+  int32_t* inv = reinterpret_cast<int32_t*>(ws + f.inv);
+  cudaStream_t st = S(stream);
+  ROLA_TRY(cuda_status(
+      launch_attn_bwd_delta(BF(out), o_sB, o_sH, o_sT, BF(dout), o_sB, o_sH, o_sT, B, H, L, f.Lpad, delta, st),
+      "sparse_attn_bwd/delta"));
+  ROLA_TRY(cuda_status(launch_lut_invert(lut, B * H, f.NB, f.NB, topk, blk == 64, ws + f.map, inv, f.width, st),
+                       "sparse_attn_bwd/lut_invert"));
+  AttnBwdParams p{};
+  p.lut = blk == 64 ? paired : lut;
+  p.inv = inv;
+  p.inv_width = f.width;
+  p.lse = lse;
+  p.delta = delta;
+  p.dq = BFm(dq);
+  p.dk = BFm(dk);
+  p.dv = BFm(dv);
+  p.g_sB = g_sB;
+  p.g_sH = g_sH;
+  p.g_sT = g_sT;
+  p.B = B;
+  p.L = L;
+  p.H = H;
+  p.NBq = f.NB;
+  p.NBk = f.NB;
+  p.NQT = f.NT;
+  p.NKT = f.NT;
+  p.Lpad = f.Lpad;
+  p.topk = topk;
+  p.blk64 = blk == 64;
+  p.qk_scale = (float)(0.08838834764831845 * 1.4426950408889634);  // 128^-0.5 * log2(e)
+  return cuda_status(launch_attn_bwd(tq, tk, tv, tdo, p, st), "sparse_attn_bwd");
 }
 
 // ---------------------------------------------------------------------------

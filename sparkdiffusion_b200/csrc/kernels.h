@@ -138,8 +138,41 @@ struct AttnParams {
   float qk_scale;  // D^-1/2 * log2(e)
   float eps_lr;    // finfo(dtype).eps
   float rescale_threshold;  // log2 growth of the running max that triggers an O rescale (0 = always)
+  // optional (training): base-2 log-sum-exp of each row, lse[bh * lse_ld + t] =
+  // m + log2(l) in units of qk_scale, +inf on the padding rows t in [L, lse_ld)
+  float* lse;
+  int lse_ld;  // 128 * (number of 128-row query tiles)
 };
 int launch_sparse_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tqlr,
                        const CUtensorMap& tct, const CUtensorMap& tx, const AttnParams& p, cudaStream_t s);
+
+// attn_bwd.cu -------------------------------------------------------------
+struct AttnBwdParams {
+  const int32_t* lut;  // dq: [B*H, NQT, topk] (block 128) or the paired table [B*H, NQT, 2 topk + 1] (block 64)
+  const int32_t* inv;  // dkdv: inverse table [B*H, NKT, inv_width] of launch_lut_invert
+  int inv_width;
+  const float* lse;    // [B*H, Lpad] base-2 log-sum-exp of the forward (+inf on padding rows)
+  const float* delta;  // [B*H, Lpad] rowsum(dO * O)
+  __nv_bfloat16* dq;   // gradients: element (b,h,t,d) at base + b*g_sB + h*g_sH + t*g_sT + d
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  int64_t g_sB, g_sH, g_sT;
+  int B, L, H;
+  int NBq, NBk;        // blocks of the selection (64- or 128-token)
+  int NQT, NKT, Lpad;  // 128-row query / key tiles, Lpad = 128 * NQT
+  int topk, blk64;
+  float qk_scale;      // D^-1/2 * log2(e)
+};
+// delta[bh, t] = sum_d dO * O in fp32 (0 on t in [L, Lpad))
+int launch_attn_bwd_delta(const __nv_bfloat16* o, int64_t o_sB, int64_t o_sH, int64_t o_sT, const __nv_bfloat16* dout,
+                          int64_t d_sB, int64_t d_sH, int64_t d_sT, int B, int H, int L, int Lpad, float* delta,
+                          cudaStream_t s);
+// inverse of a selection lut [BH, NBq, topk]: per key tile the ascending list of the
+// query blocks that selected it (map: BH*NBq*NBk bytes of scratch; width = NBq + 2)
+int launch_lut_invert(const int32_t* lut, int BH, int NBq, int NBk, int topk, int blk64, uint8_t* map, int32_t* inv,
+                      int width, cudaStream_t s);
+// dq (query-stationary), then dk and dv (key-stationary); maps as the forward's (rows = block size)
+int launch_attn_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
+                    const AttnBwdParams& p, cudaStream_t s);
 
 }  // namespace rola

@@ -6,6 +6,7 @@
 #include "lowrank.cu"
 #include "gemm.cu"
 #include "attn.cu"
+#include "attn_bwd.cu"
 #include "capi.cu"
 #include "peer.cu"
 #include "pipeline.cu"

@@ -8,12 +8,16 @@ interface: ``forward(x [B, L, dim], seq_lens, freqs [L, D/2], rope_cache=None)
 -> [B, L, dim]`` (sparse_attn_registry.py:16-18, wan2pt1.py:468-472).  It is
 registered as ``"rola_b200"``.
 
-Inference only (the reference's fused path has the same gating,
-wan_rola_attention.py:467-477): the forward raises under autograd or on CPU
-tensors instead of falling back.  The kernels are reached through the custom
-operators ``torch.ops.rola_b200.*`` (``torch_ops``), so ``torch.compile`` of a
-model holding these layers captures each as one opaque node (meta tensors run
-the operators' shape functions only).
+Inference runs the fused B200 path (the reference's fused path has the same
+gating, wan_rola_attention.py:467-477).  Under autograd (training, or an input
+that requires grad) the forward takes the reference's non-fused training
+route instead (``train.training_attention_core``): eager projections, norm,
+RoPE, low-rank branch and gate, with the block-sparse attention's forward and
+backward on the tcgen05 kernels in place of the external SLA package.  CPU
+tensors raise instead of falling back.  The inference kernels are reached
+through the custom operators ``torch.ops.rola_b200.*`` (``torch_ops``), so
+``torch.compile`` of a model holding these layers captures each as one opaque
+node (meta tensors run the operators' shape functions only).
 """
 
 from __future__ import annotations
@@ -139,10 +143,13 @@ class WanSelfAttentionRoLaB200(nn.Module):
             self._qkv_cache = (key, *build())
         return self._qkv_cache[1:]
 
+    def _autograd_route(self, x: torch.Tensor) -> bool:
+        """The reference trains through its non-fused forward whenever autograd
+        records (wan_rola_attention.py:467-477); so does this layer."""
+        return torch.is_grad_enabled() and (self.training or x.requires_grad)
+
     def attention_core(self, x: torch.Tensor, freqs: torch.Tensor, rope_cache=None) -> torch.Tensor:
         """Everything of the forward except the output projection."""
-        if torch.is_grad_enabled() and self.training:
-            raise RuntimeError("WanSelfAttentionRoLaB200 is inference-only (no backward kernels)")
         if x.device.type == "cpu":
             raise RuntimeError("WanSelfAttentionRoLaB200 runs on CUDA tensors only")
         if self.attn_precision != "bf16":
@@ -152,6 +159,11 @@ class WanSelfAttentionRoLaB200(nn.Module):
         B, L, dim = x.shape
         if L < max(self.rola_blkq, self.rola_blkk):
             raise ValueError("sequence shorter than one block")
+        if self._autograd_route(x):
+            if self._pg is not None and torch.distributed.get_world_size(self._pg) > 1:
+                raise RuntimeError("the sequence-parallel route of WanSelfAttentionRoLaB200 is inference-only")
+            from .train import training_attention_core
+            return training_attention_core(self, x, freqs)
         x = x.to(torch.bfloat16).contiguous()
         D = self.head_dim
         if rope_cache is not None and rope_cache[0] is not None:
@@ -194,6 +206,8 @@ class WanSelfAttentionRoLaB200(nn.Module):
     def forward(self, x: torch.Tensor, seq_lens: torch.Tensor, freqs: torch.Tensor, rope_cache=None) -> torch.Tensor:
         del seq_lens
         out = self.attention_core(x, freqs, rope_cache)
+        if self._autograd_route(x):
+            return self.o(out)  # wan_rola_attention.py:552
         B, L, dim = out.shape
         if self._is_fp8(self.o):
             # FP8Linear output projection: per-token quantization of the attention output
@@ -215,7 +229,9 @@ class WanSelfAttentionB200(nn.Module):
     block-sparse kernel with every key block selected) and the output
     projection on the same GEMM.  Same parameter names and shapes (q, k, v, o,
     norm_q, norm_k) as the reference layer, so its checkpoints load unchanged.
-    Inference only."""
+    Under autograd the reference's differentiable route (wan2pt1.py:313-328) runs,
+    with the attention's forward and backward on the tcgen05 kernels (every
+    key block selected)."""
 
     def __init__(self, dim: int, num_heads: int, qk_norm: bool = True, eps: float = 1e-6):
         super().__init__()
@@ -251,14 +267,15 @@ class WanSelfAttentionB200(nn.Module):
 
     def forward(self, x: torch.Tensor, seq_lens: torch.Tensor, freqs: torch.Tensor, rope_cache=None) -> torch.Tensor:
         del seq_lens
-        if torch.is_grad_enabled() and self.training:
-            raise RuntimeError("WanSelfAttentionB200 is inference-only (no backward kernels)")
         if not x.is_cuda:
             raise RuntimeError("WanSelfAttentionB200 runs on CUDA tensors only")
         if self.head_dim != 128 or self.dim % 256 != 0:
             raise ValueError("the B200 path needs head_dim 128 and an even head count")
         B, L, dim = x.shape
         H = self.num_heads
+        if torch.is_grad_enabled() and (self.training or x.requires_grad):
+            from .train import dense_training_forward
+            return dense_training_forward(self, x, freqs)
         x = x.to(torch.bfloat16).contiguous()
         if rope_cache is not None and rope_cache[0] is not None:
             cos_sin = rope_cache[0].to(torch.float32).contiguous()

@@ -612,3 +612,79 @@ def fused_qkv_gemm_rope(x, q_proj, k_proj, v_proj, freqs, norm_q_weight, norm_k_
     if return_normed:
         return (*outs, q_n.view(B, L, H, head_dim), k_n.view(B, L, H, head_dim))
     return outs
+
+
+# ---------------------------------------------------------------------------
+# training: block-sparse attention forward with the row log-sum-exp, backward
+# ---------------------------------------------------------------------------
+def _head_view_ok(t: torch.Tensor) -> bool:
+    """``[B, H, L, 128]`` view the kernels can map: unit d stride, 16-byte rows."""
+    return (t.dim() == 4 and t.shape[-1] == HEAD_DIM and t.stride(3) == 1 and t.data_ptr() % 16 == 0
+            and all(s % 8 == 0 for s in t.stride()[:3]))
+
+
+def _token_major(t: torch.Tensor) -> torch.Tensor:
+    """``[B, H, L, D]`` view of a contiguous ``[B, L, H, D]`` copy of ``t``."""
+    return t.transpose(1, 2).contiguous().transpose(1, 2)
+
+
+def lse_rows(L: int) -> int:
+    """Row stride of the ``lse`` table: L rounded up to whole 128-row tiles."""
+    return 128 * ((L + 127) // 128)
+
+
+def sparse_attention_fwd_lse(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, lut: torch.Tensor, blk: int,
+                             topk: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Block-sparse attention over ``q, k, v [B, H, L, 128]`` (bf16) with the
+    selection ``lut`` (block 128: ``[B*H, NB, topk]``; block 64: the paired
+    table of ``rola_b200_pair_blocks``).  Returns ``(o [B, H, L, 128]`` (a view
+    of a token-major ``[B, L, H, 128]`` tensor), ``lse [B*H, Lpad]`` fp32)``."""
+    _require_cuda(q, k, v, lut)
+    if not (q.dtype == k.dtype == v.dtype == BF16):
+        raise ValueError("sparse_attention_fwd_lse: bf16 q, k, v required")
+    B, H, L, D = q.shape
+    if k.shape != q.shape or v.shape != q.shape or D != HEAD_DIM:
+        raise ValueError("sparse_attention_fwd_lse: q, k, v must all be [B, H, L, 128]")
+    if not (_head_view_ok(q) and _head_view_ok(k) and q.stride() == k.stride()):
+        q, k = _token_major(q), _token_major(k)
+    if not _head_view_ok(v):
+        v = _token_major(v)
+    o = torch.empty(B, L, H, D, device=q.device, dtype=BF16).transpose(1, 2)
+    lse = torch.empty(B * H, lse_rows(L), device=q.device, dtype=torch.float32)
+    lut = lut.contiguous()
+    _lib.call("rola_b200_sparse_attn_fwd_lse", _ptr(q), _ptr(k), *q.stride()[:3], _ptr(v), *v.stride()[:3],
+              _ptr(lut), B, L, H, blk, topk, _ptr(o), *o.stride()[:3], _ptr(lse), _stream())
+    return o, lse
+
+
+def sparse_attention_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, do: torch.Tensor,
+                         lut: torch.Tensor, paired: torch.Tensor | None, lse: torch.Tensor, blk: int,
+                         topk: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Gradients ``(dq, dk, dv)`` ``[B, H, L, 128]`` bf16 of
+    ``sparse_attention_fwd_lse`` given ``do = dL/do``; ``lut`` is the selection
+    ``[B*H, NB, topk]`` and ``paired`` its block-64 pairing (the forward's lut;
+    None for block 128)."""
+    _require_cuda(q, k, v, o, do, lut, paired, lse)
+    B, H, L, D = q.shape
+    if not (_head_view_ok(q) and _head_view_ok(k) and q.stride() == k.stride()):
+        q, k = _token_major(q), _token_major(k)
+    if not _head_view_ok(v):
+        v = _token_major(v)
+    if not _head_view_ok(o):
+        raise ValueError("sparse_attention_bwd: o must be the forward's output")
+    do = do.to(BF16)
+    if do.stride() != o.stride() or do.data_ptr() % 16:
+        d2 = torch.empty_like(o)
+        d2.copy_(do)
+        do = d2
+    g = torch.empty(3, B, L, H, D, device=q.device, dtype=BF16)
+    dq, dk, dv = (g[i].transpose(1, 2) for i in range(3))
+    ws_bytes = _lib.lib().rola_b200_sparse_attn_bwd_workspace(B, L, H, blk)
+    if ws_bytes == 0:
+        raise ValueError("sparse_attention_bwd: bad sizes")
+    ws = torch.empty(ws_bytes, device=q.device, dtype=torch.uint8)
+    _lib.call("rola_b200_sparse_attn_bwd", _ptr(q), _ptr(k), *q.stride()[:3], _ptr(v), *v.stride()[:3], _ptr(o),
+              _ptr(do), *o.stride()[:3], _ptr(lut.contiguous()), _ptr(None if paired is None else paired.contiguous()),
+              _ptr(lse), B, L, H, blk, topk, _ptr(dq), _ptr(dk), _ptr(dv), *dq.stride()[:3], _ptr(ws), ws_bytes,
+              _stream())
+    return dq, dk, dv

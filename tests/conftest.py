@@ -36,14 +36,16 @@ BF16_MAX = 2e-2
 BF16_MEAN = 2e-3
 
 
-def assert_bf16_close(got, ref, name="", max_tol=BF16_MAX, mean_tol=BF16_MEAN, ulp_floor=False):
+def assert_bf16_close(got, ref, name="", max_tol=BF16_MAX, mean_tol=BF16_MEAN, ulp_floor=False, steps=1.0):
     """max-abs <= ``max_tol`` and mean-abs <= ``mean_tol`` of the RMS of ``ref``.
 
     ``ulp_floor``: for a bf16 result checked against an fp32 (unrounded) oracle,
     each element may instead differ by one bf16 rounding step (ulp) of its own
     magnitude where that step exceeds ``max_tol`` of the RMS: an output whose
     largest elements sit ~6x above its RMS cannot be represented in bf16 closer
-    than that (one step is then up to ~4e-2 of the RMS)."""
+    than that (one step is then up to ~4e-2 of the RMS).  ``steps`` widens the
+    per-element floor to that many steps (results that pass through several
+    bf16 roundings, e.g. gradients)."""
     if not ulp_floor:
         mx, mn = rel_err(got, ref)
         assert mx <= max_tol and mn <= mean_tol, f"{name}: max-abs/rms={mx:.3e} mean-abs/rms={mn:.3e}"
@@ -53,11 +55,11 @@ def assert_bf16_close(got, ref, name="", max_tol=BF16_MAX, mean_tol=BF16_MEAN, u
     rms = r.pow(2).mean().sqrt().clamp_min(1e-30)
     d = (g - r).abs()
     step = torch.exp2(torch.floor(torch.log2(r.abs().clamp_min(1e-30))) - 7)
-    bound = torch.maximum(max_tol * rms, step)
+    bound = torch.maximum(max_tol * rms, steps * step)
     worst = (d / bound).max().item()
     mx, mn = (d.max() / rms).item(), (d.mean() / rms).item()
     assert worst <= 1.0 and mn <= mean_tol, (f"{name}: max-abs/rms={mx:.3e} ({worst:.2f} of the per-element bound "
-                                             f"max({max_tol:g}*rms, 1 bf16 step)), mean-abs/rms={mn:.3e}")
+                                             f"max({max_tol:g}*rms, {steps:g} bf16 step)), mean-abs/rms={mn:.3e}")
 
 
 def assert_ulp_close(got, ref, name="", ulps=2, max_frac=1e-3, mean_tol=BF16_MEAN):
