@@ -18,18 +18,20 @@
 // P and dS are rounded to bf16 where they feed an MMA (as the forward rounds
 // P before P.V); every accumulation is fp32 in tensor memory.
 //
-// Block size 64 runs on 128-row tiles as in the forward: the dq kernel takes
-// the paired LUT of launch_pair_blocks (two 64-row key blocks stacked per key
-// tile, selection bits per query half); the dkdv kernel takes an inverse
-// table whose entries are 64-row query blocks with two selection bits (key
-// block 2J, key block 2J+1 of key tile J), stacked two per query tile.
+// Both kernels keep a 128-row tile stationary (Q and dO of a query tile, or K
+// and V of a key tile) and walk the other side in steps of 64 rows: a 128-row
+// block is two steps, a 64-row block (block size 64) one step whose selection
+// bits say which 64-row half of the stationary tile selected it.  The S / dP
+// accumulators of a step are double-buffered in tensor memory, and the two
+// softmax warpgroups take alternate steps, so the MMA warp computes step i+1's
+// S and dP while step i's P and dS are computed, and two steps' exp2 work runs
+// at once.
 //
-// Both kernels: 384 threads.  Warp 0 lane 0 is the TMA producer (no
-// multicast), warp 1 owns tensor memory and issues the MMAs (one elected
-// thread), warpgroups 1 and 2 each take one 64-column half of the S / dP tile
-// for all 128 rows (thread = TMEM lane = tile row) and then the epilogue of
-// that half.  Every mbarrier wait is bounded (error flag + abort, as in the
-// forward).
+// 384 threads.  Warp 0 lane 0: TMA producer (no multicast).  Warp 1: tensor
+// memory owner and MMA issuer (one elected thread).  Warpgroups 1 and 2: the
+// steps of even / odd index (thread = TMEM lane = stationary-tile row), then
+// the epilogue of one 64-column half of the accumulators each.  Every
+// mbarrier wait is bounded (error flag + abort, as in the forward).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -37,31 +39,34 @@ namespace rola {
 
 namespace bwd {
 constexpr int THREADS = 384;
-constexpr int TILE = 16384;  // [128 rows x 64 bf16] box, 128-byte swizzle
-constexpr int SLOT = 2 * TILE;  // one 128 x 128 bf16 tile
-constexpr int STAGES = 2;
-// dq kernel: Q and dO of the query tile, then the ring of (K, V) key tiles
-constexpr int DQ_OFF_Q = 0, DQ_OFF_DO = SLOT, DQ_OFF_RING = 2 * SLOT;
-constexpr int DQ_ENTRY = 2 * SLOT;
+constexpr int BOX = 8192;          // [64 rows x 64 bf16] box, 128-byte swizzle
+constexpr int HALF = 2 * BOX;      // 64 rows x 128 d: one step's operand
+constexpr int TILE = 2 * HALF;     // 128 rows x 128 d: the stationary operands
+constexpr int BOX128 = 2 * BOX;    // [128 rows x 64 bf16] (two 64-row boxes stacked)
+constexpr int STAGES = 4;
+// dq kernel: Q and dO of the query tile, then the ring of (K, V) 64-row steps
+constexpr int DQ_OFF_Q = 0, DQ_OFF_DO = TILE, DQ_OFF_RING = 2 * TILE;
+constexpr int DQ_ENTRY = 2 * HALF;
 constexpr int DQ_OFF_BAR = DQ_OFF_RING + STAGES * DQ_ENTRY;  // 192 KB
-// dkdv kernel: K and V of the key tile, then the ring of (Q, dO, lse2, delta) query tiles
-constexpr int KV_OFF_K = 0, KV_OFF_V = SLOT, KV_OFF_RING = 2 * SLOT;
-constexpr int KV_ENTRY = 2 * SLOT + 1024;  // + 128 lse2 + 128 delta (fp32)
-constexpr int KV_OFF_BAR = KV_OFF_RING + STAGES * KV_ENTRY;  // 194 KB
+// dkdv kernel: K and V of the key tile, then the ring of (Q, dO, lse2, delta) 64-row steps
+constexpr int KV_OFF_K = 0, KV_OFF_V = TILE, KV_OFF_RING = 2 * TILE;
+constexpr int KV_ENTRY = 2 * HALF + 1024;  // + 64 lse2 + 64 delta (fp32), padded to keep 1024-byte alignment
+constexpr int KV_OFF_BAR = KV_OFF_RING + STAGES * KV_ENTRY;  // 196 KB
 constexpr int BAR_BYTES = 256;
 constexpr int DQ_SMEM = DQ_OFF_BAR + BAR_BYTES + 1024;
 constexpr int KV_SMEM = KV_OFF_BAR + BAR_BYTES + 1024;
 static_assert(KV_ENTRY % 1024 == 0, "ring entries keep the 1024-byte swizzle alignment");
+static_assert(KV_SMEM <= 227 * 1024 && DQ_SMEM <= 227 * 1024, "shared memory per CTA");
 constexpr float kSmScale = 0.08838834764831845f;  // 128^-1/2
 }  // namespace bwd
 
 enum : int {
-  G_TILE = 0,          // stationary tiles loaded (Q, dO / K, V)
-  G_FULL0,             // ring entry s loaded: G_FULL0 + s
+  G_TILE = 0,                        // stationary tiles loaded
+  G_FULL0,                           // ring entry s loaded: G_FULL0 + s
   G_EMPTY0 = G_FULL0 + bwd::STAGES,  // ring entry s consumed (MMA commit)
-  G_SF = G_EMPTY0 + bwd::STAGES,     // S and dP of the current block in TMEM
-  G_DS,                // dS (dq) / P^T and dS^T (dkdv) in TMEM, 8 warp arrivals
-  G_ACC,               // accumulators final
+  G_SF0 = G_EMPTY0 + bwd::STAGES,    // S and dP of a step in TMEM buffer b: G_SF0 + b
+  G_DS0 = G_SF0 + 2,                 // dS (and P) of a step in TMEM buffer b, 4 warp arrivals: G_DS0 + b
+  G_ACC = G_DS0 + 2,                 // accumulators final
   G_COUNT
 };
 static_assert(8 * G_COUNT + 16 <= bwd::BAR_BYTES, "barrier region too small");
@@ -72,17 +77,9 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                : "memory");
 }
 
-// key block of entry i of a 128-block LUT row (clamped, error flag on a bad index)
-__device__ __forceinline__ int bwd_block(const int32_t* row, int i, int nb) {
-  int j = row[i];
-  if (j < 0 || j >= nb) {
-    set_device_error(kDevBadIndex);
-    j = j < 0 ? 0 : nb - 1;
-  }
-  return j;
-}
-// 64-row block of a paired / inverse entry (padding -1 -> block 0, masked by the caller)
-__device__ __forceinline__ int bwd_block64(int32_t e, int nb) {
+// block index of a LUT / inverse-table entry (selection bits and the -1
+// padding of a paired table stripped; error flag on an index outside [0, nb))
+__device__ __forceinline__ int entry_block(int32_t e, int nb) {
   if (e < 0) return 0;
   int j = e & 0x0fffffff;
   if (j >= nb) {
@@ -92,37 +89,36 @@ __device__ __forceinline__ int bwd_block64(int32_t e, int nb) {
   return j;
 }
 
-// load a 128-row tile (two 64-column boxes) of map m at rows r0 (and, block 64,
-// the lower 64 rows from r1)
-__device__ __forceinline__ void load_tile(uint32_t dst, const CUtensorMap* m, uint32_t bar, int r0, int r1, bool two,
-                                          int h, int b) {
-  if (!two) {
-    tma_load_4d(dst, m, bar, 0, r0, h, b);
-    tma_load_4d(dst + bwd::TILE, m, bar, 64, r0, h, b);
-  } else {
-    tma_load_4d(dst, m, bar, 0, r0, h, b);
-    tma_load_4d(dst + bwd::TILE / 2, m, bar, 0, r1, h, b);
-    tma_load_4d(dst + bwd::TILE, m, bar, 64, r0, h, b);
-    tma_load_4d(dst + bwd::TILE + bwd::TILE / 2, m, bar, 64, r1, h, b);
-  }
+// the 64 rows starting at row r0 of map m (64-row boxes), both column halves
+__device__ __forceinline__ void load_half(uint32_t dst, const CUtensorMap* m, uint32_t bar, int r0, int h, int b) {
+  tma_load_4d(dst, m, bar, 0, r0, h, b);
+  tma_load_4d(dst + bwd::BOX, m, bar, 64, r0, h, b);
+}
+// the 128 rows starting at row r0 as two stacked 64-row boxes per column half
+__device__ __forceinline__ void load_tile(uint32_t dst, const CUtensorMap* m, uint32_t bar, int r0, int h, int b) {
+  tma_load_4d(dst, m, bar, 0, r0, h, b);
+  tma_load_4d(dst + bwd::BOX, m, bar, 0, r0 + 64, h, b);
+  tma_load_4d(dst + bwd::BOX128, m, bar, 64, r0, h, b);
+  tma_load_4d(dst + bwd::BOX128 + bwd::BOX, m, bar, 64, r0 + 64, h, b);
 }
 
-// issue X (+)= A B^T over D = 128 with both operands K-major 128 x 128 tiles
-__device__ __forceinline__ void mma_tile_ss(uint32_t d_tmem, uint32_t sa, uint32_t sb, uint32_t idesc) {
+// X[128 x 64] = A[128 x 128] B[64 x 128]^T over D: A a stationary 128-row
+// tile, B one step's 64-row operand, both K-major
+__device__ __forceinline__ void mma_step_ss(uint32_t d_tmem, uint32_t sa, uint32_t sb, uint32_t idesc) {
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
-    const uint32_t off = (kk >> 2) * bwd::TILE + (kk & 3) * 32;
-    mma_bf16_ss(d_tmem, sdesc_sw128(sa + off, 16, 1024), sdesc_sw128(sb + off, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+    const uint32_t ka = (kk >> 2) * bwd::BOX128 + (kk & 3) * 32;
+    const uint32_t kb = (kk >> 2) * bwd::BOX + (kk & 3) * 32;
+    mma_bf16_ss(d_tmem, sdesc_sw128(sa + ka, 16, 1024), sdesc_sw128(sb + kb, 16, 1024), idesc, kk > 0 ? 1u : 0u);
   }
 }
-// issue X (+)= A B with A packed bf16 in TMEM (each warpgroup's 64 K-columns
-// packed into the first 32 TMEM columns of its half) and B an MN-major tile
-__device__ __forceinline__ void mma_tile_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t sb, uint32_t idesc, bool acc) {
+// X[128 x 128] (+)= A[128 x 64] B[64 x 128]: A packed bf16 in TMEM (32
+// columns), B one step's 64-row operand read MN-major
+__device__ __forceinline__ void mma_step_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t sb, uint32_t idesc, bool acc) {
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    mma_bf16_ts(d_tmem, a_tmem + 64 * (kk >> 2) + 8 * (kk & 3), sdesc_sw128(sb + kk * 2048, bwd::TILE, 1024), idesc,
+  for (int kk = 0; kk < 4; ++kk)
+    mma_bf16_ts(d_tmem, a_tmem + 8 * kk, sdesc_sw128(sb + kk * 2048, bwd::BOX, 1024), idesc,
                 (acc || kk > 0) ? 1u : 0u);
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -175,11 +171,10 @@ __global__ void lut_scatter_kernel(const int32_t* __restrict__ lut, int BH, int 
   map[(bh * NBk + j) * NBq + i] = 1;
 }
 
-// one warp per (bh, key tile J).  Row layout (width NBq + 2 int32): [count,
-// entries...].  Block 128: entries are query blocks, count = their number.
-// Block 64: entries are 64-row query blocks i | bit 28 (selected key block 2J)
-// | bit 29 (selected key block 2J+1), padded with -1 to an even number; count
-// = number of stacked pairs.
+// one warp per (bh, 128-row key tile J).  Row layout (width NBq + 2 int32):
+// [count, entries...].  Block 128: entries are the query blocks that selected
+// key block J.  Block 64: entries are the 64-row query blocks i that selected
+// key block 2J or 2J+1, as i | bit 28 (selected 2J) | bit 29 (selected 2J+1).
 __global__ void lut_invert_kernel(const uint8_t* __restrict__ map, int BH, int NBq, int NBk, int blk64, int width,
                                   int32_t* __restrict__ inv) {
   const int NKT = blk64 ? (NBk + 1) / 2 : NBk;
@@ -204,11 +199,13 @@ __global__ void lut_invert_kernel(const uint8_t* __restrict__ map, int BH, int N
     if (bits) out[1 + n + __popc(ball & ((1u << lane) - 1u))] = blk64 ? (i | (bits << 28)) : i;
     n += __popc(ball);
   }
-  if (lane == 0) {
-    if (blk64 && (n & 1)) out[1 + n] = -1;
-    out[0] = blk64 ? (n + 1) / 2 : n;
-  }
+  if (lane == 0) out[0] = n;
 }
+
+// Tensor memory of both kernels (512 columns): S (or S^T) of buffer b at
+// [128 b, 128 b + 64), dP (or dP^T) at [128 b + 64, 128 b + 128); P^T and dS
+// (dS^T) packed bf16 over the first 32 columns of those; accumulators at
+// [256, 384) (dQ, or dV) and [384, 512) (dK).
 
 // ---------------------------------------------------------------------------
 // dq kernel: one CTA per (128-row query tile, b*h)
@@ -231,10 +228,15 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int m = blockIdx.x;  // 128-row query tile
   const bool two = p.blk64 != 0;
-  // LUT row of this tile: block 128 the plain row, block 64 the paired row (count first)
+  // LUT row of this tile.  Block 128: topk key blocks, two 64-key steps each.
+  // Block 64: the paired table's union (count of pairs first), one step per entry.
   const int ent = two ? 2 * p.topk + 1 : p.topk;
   const int32_t* row = p.lut + ((int64_t)bh * p.NQT + m) * ent + (two ? 1 : 0);
-  const int n = two ? max(1, min(row[-1], p.topk)) : p.topk;
+  const int n = two ? 2 * max(1, min(row[-1], p.topk)) : 2 * p.topk;  // steps
+  // key rows of step i
+  auto step_key = [&](int i) {
+    return two ? 64 * entry_block(row[i], p.NBk) : 128 * entry_block(row[i >> 1], p.NBk) + 64 * (i & 1);
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(bar(G_TILE), 1);
@@ -242,8 +244,10 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
       mbar_init(bar(G_FULL0 + s), 1);
       mbar_init(bar(G_EMPTY0 + s), 1);
     }
-    mbar_init(bar(G_SF), 1);
-    mbar_init(bar(G_DS), 8);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(G_SF0 + t), 1);
+      mbar_init(bar(G_DS0 + t), 4);
+    }
     mbar_init(bar(G_ACC), 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -259,32 +263,22 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // S/dS [0,128), dP [128,256), dQ [256,384)
+  const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ TMA
-      mbar_expect_tx(bar(G_TILE), 2 * SLOT);
-      load_tile(base + DQ_OFF_Q, &tq, bar(G_TILE), 128 * m, 128 * m + 64, two, h, b);
-      load_tile(base + DQ_OFF_DO, &tdo, bar(G_TILE), 128 * m, 128 * m + 64, two, h, b);
-      bool ok = true;
-      for (int i = 0; i < n && ok; ++i) {
+      mbar_expect_tx(bar(G_TILE), 2 * TILE);
+      load_tile(base + DQ_OFF_Q, &tq, bar(G_TILE), 128 * m, h, b);
+      load_tile(base + DQ_OFF_DO, &tdo, bar(G_TILE), 128 * m, h, b);
+      for (int i = 0; i < n; ++i) {
         const int s = i % STAGES;
-        if (!mbar_wait(bar(G_EMPTY0 + s), ((i / STAGES) & 1) ^ 1, abort_flag, kDevTimeoutMma)) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait(bar(G_EMPTY0 + s), ((i / STAGES) & 1) ^ 1, abort_flag, kDevTimeoutMma)) break;
         const uint32_t dst = base + DQ_OFF_RING + s * DQ_ENTRY;
-        mbar_expect_tx(bar(G_FULL0 + s), 2 * SLOT);
-        int r0, r1 = 0;
-        if (!two) {
-          r0 = 128 * bwd_block(row, i, p.NBk);
-        } else {
-          r0 = 64 * bwd_block64(row[2 * i], p.NBk);
-          r1 = 64 * bwd_block64(row[2 * i + 1], p.NBk);
-        }
-        load_tile(dst, &tk, bar(G_FULL0 + s), r0, r1, two, h, b);
-        load_tile(dst + SLOT, &tv, bar(G_FULL0 + s), r0, r1, two, h, b);
+        mbar_expect_tx(bar(G_FULL0 + s), 2 * HALF);
+        const int r0 = step_key(i);
+        load_half(dst, &tk, bar(G_FULL0 + s), r0, h, b);
+        load_half(dst + HALF, &tv, bar(G_FULL0 + s), r0, h, b);
       }
       // drain: no TMA may still target shared memory when the CTA exits
       const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
@@ -294,48 +288,62 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA
+    // order: S_i, dP_i, then dQ += dS_{i-1} K_{i-1} once step i-1's dS is in
+    // TMEM, so the tensor core computes S_i / dP_i during step i-1's softmax
     if (elect_one()) {
-      const uint32_t id_ss = idesc_bf16_f32(128, 128, false, false);
-      const uint32_t id_ts = idesc_bf16_f32(128, 128, false, true);
+      const uint32_t id_s = idesc_bf16_f32(128, 64, false, false);
+      const uint32_t id_q = idesc_bf16_f32(128, 128, false, true);
       bool ok = mbar_wait(bar(G_TILE), 0, abort_flag, kDevTimeoutLoad);
+      auto issue_dq = [&](int i) {
+        if (!mbar_wait(bar(G_DS0 + (i & 1)), (i >> 1) & 1, abort_flag, kDevTimeoutSoftmax)) {
+          ok = false;
+          return;
+        }
+        tc_fence_after();
+        const uint32_t sk = base + DQ_OFF_RING + (i % STAGES) * DQ_ENTRY;
+        mma_step_ts(tmem + 256, tmem + 128 * (i & 1), sk, id_q, i > 0);  // dQ += dS K
+        mma_commit(bar(G_EMPTY0 + i % STAGES));
+      };
       for (int i = 0; i < n && ok; ++i) {
         const int s = i % STAGES;
-        if (!mbar_wait(bar(G_FULL0 + s), (i / STAGES) & 1, abort_flag, kDevTimeoutLoad)) break;
+        if (!mbar_wait(bar(G_FULL0 + s), (i / STAGES) & 1, abort_flag, kDevTimeoutLoad)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t sk = base + DQ_OFF_RING + s * DQ_ENTRY, sv = sk + SLOT;
-        mma_tile_ss(tmem, base + DQ_OFF_Q, sk, id_ss);          // S  = Q K^T
-        mma_tile_ss(tmem + 128, base + DQ_OFF_DO, sv, id_ss);   // dP = dO V^T
-        mma_commit(bar(G_SF));
-        if (!mbar_wait(bar(G_DS), i & 1, abort_flag, kDevTimeoutSoftmax)) break;
-        tc_fence_after();
-        mma_tile_ts(tmem + 256, tmem, sk, id_ts, i > 0);        // dQ += dS K
-        mma_commit(bar(G_EMPTY0 + s));
+        const uint32_t sk = base + DQ_OFF_RING + s * DQ_ENTRY, sv = sk + HALF;
+        const uint32_t tb = tmem + 128 * (i & 1);
+        mma_step_ss(tb, base + DQ_OFF_Q, sk, id_s);        // S  = Q K^T
+        mma_step_ss(tb + 64, base + DQ_OFF_DO, sv, id_s);  // dP = dO V^T
+        mma_commit(bar(G_SF0 + (i & 1)));
+        if (i > 0) issue_dq(i - 1);
       }
+      if (ok) issue_dq(n - 1);
       mma_commit(bar(G_ACC));
     }
   } else if (warp >= 4) {
-    // ---------------------------------------------------- dS, then the dQ epilogue
-    const int hc = (warp - 4) >> 2;  // key half (columns) of this warpgroup
+    // -------------------------------------- dS of alternate steps, then the dQ epilogue
+    const int wg = (warp - 4) >> 2;  // steps i with i % 2 == wg; epilogue columns [64 wg, 64 wg + 64)
     const int q = warp & 3;
-    const int r = q * 32 + lane;      // tile row = TMEM lane
+    const int r = q * 32 + lane;  // query row of the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    const uint32_t tS = tmem + lane_off + 64 * hc, tdP = tmem + 128 + lane_off + 64 * hc;
+    const uint32_t tS = tmem + lane_off + 128 * wg, tdP = tS + 64;
     const int tok = 128 * m + r;
     const float lse = p.lse[(int64_t)bh * p.Lpad + tok];
     const float dlt = p.delta[(int64_t)bh * p.Lpad + tok];
     const uint64_t sc2 = f2_pack(p.qk_scale, p.qk_scale), nl2 = f2_pack(-lse, -lse);
     bool ok = true;
-    for (int i = 0; i < n; ++i) {
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(G_SF), i & 1, abort_flag, kDevTimeoutMma))) {
+    for (int i = wg; i < n; i += 2) {
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(G_SF0 + wg), (i >> 1) & 1, abort_flag, kDevTimeoutMma))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      int valid;  // valid key columns of this half for this row
+      int valid;  // valid key columns of this step for this row
       if (!two) {
-        valid = min(64, max(0, p.L - 128 * bwd_block(row, i, p.NBk) - 64 * hc));
+        valid = min(64, max(0, p.L - step_key(i)));
       } else {
-        const int32_t e = row[2 * i + hc];
+        const int32_t e = row[i];
         valid = (e < 0 || !((e >> (28 + (r >> 6))) & 1)) ? 0 : min(64, p.L - 64 * (e & 0x0fffffff));
       }
 #pragma unroll
@@ -352,28 +360,26 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
           f2_unpack(fma_f32x2(f2_pack(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sc2, nl2), x0, x1);
           const float p0 = col < valid ? ex2_approx(x0) : 0.f;
           const float p1 = col + 1 < valid ? ex2_approx(x1) : 0.f;
-          const float d0 = p0 * (__uint_as_float(dv[2 * e]) - dlt);
-          const float d1 = p1 * (__uint_as_float(dv[2 * e + 1]) - dlt);
-          w[e] = pack_bf2(d0, d1);
+          w[e] = pack_bf2(p0 * (__uint_as_float(dv[2 * e]) - dlt), p1 * (__uint_as_float(dv[2 * e + 1]) - dlt));
         }
-        tmem_st16(tS + 16 * c, w);  // packed dS over the S columns of this half
+        tmem_st16(tS + 16 * c, w);  // packed dS over the first 32 S columns of the buffer
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(G_DS));
+      if (lane == 0) mbar_arrive(bar(G_DS0 + wg));
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(G_ACC), 0, abort_flag, kDevTimeoutMma));
     tc_fence_after();
     if (ok) {
-      const uint32_t tQ = tmem + 256 + lane_off + 64 * hc;
+      const uint32_t tQ = tmem + 256 + lane_off + 64 * wg;
       uint32_t v[64];
       tmem_ld32(tQ, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
       tmem_ld32(tQ + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
       tmem_ld_wait();
       if (tok < p.L) {
         uint4* dst = reinterpret_cast<uint4*>(p.dq + (int64_t)b * p.g_sB + (int64_t)h * p.g_sH + (int64_t)tok * p.g_sT +
-                                              64 * hc);
+                                              64 * wg);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           uint32_t w4[4];
@@ -416,9 +422,13 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
   const int J = blockIdx.x;  // 128-row key tile
   const bool two = p.blk64 != 0;
   const int32_t* row = p.inv + ((int64_t)bh * p.NKT + J) * p.inv_width;
-  // query tiles to visit (block 64: stacked pairs of entries)
-  const int n = max(0, min(row[0], two ? (p.inv_width - 1) / 2 : p.inv_width - 1));
+  const int cnt = max(0, min(row[0], p.inv_width - 1));
   const int32_t* ents = row + 1;
+  // steps: block 128, two 64-row halves of each query block; block 64, one per entry
+  const int n = two ? cnt : 2 * cnt;
+  auto step_query = [&](int i) {
+    return two ? 64 * entry_block(ents[i], p.NBq) : 128 * entry_block(ents[i >> 1], p.NBq) + 64 * (i & 1);
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(bar(G_TILE), 1);
@@ -426,8 +436,10 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
       mbar_init(bar(G_FULL0 + s), 1);
       mbar_init(bar(G_EMPTY0 + s), 1);
     }
-    mbar_init(bar(G_SF), 1);
-    mbar_init(bar(G_DS), 8);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(G_SF0 + t), 1);
+      mbar_init(bar(G_DS0 + t), 4);
+    }
     mbar_init(bar(G_ACC), 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -443,39 +455,26 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // S^T/P^T [0,128), dP^T/dS^T [128,256), dV [256,384), dK [384,512)
+  const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ TMA
-      mbar_expect_tx(bar(G_TILE), 2 * SLOT);
-      load_tile(base + KV_OFF_K, &tk, bar(G_TILE), 128 * J, 128 * J + 64, two, h, b);
-      load_tile(base + KV_OFF_V, &tv, bar(G_TILE), 128 * J, 128 * J + 64, two, h, b);
-      bool ok = true;
-      for (int i = 0; i < n && ok; ++i) {
+      mbar_expect_tx(bar(G_TILE), 2 * TILE);
+      load_tile(base + KV_OFF_K, &tk, bar(G_TILE), 128 * J, h, b);
+      load_tile(base + KV_OFF_V, &tv, bar(G_TILE), 128 * J, h, b);
+      const float* lse_row = p.lse + (int64_t)bh * p.Lpad;
+      const float* dlt_row = p.delta + (int64_t)bh * p.Lpad;
+      for (int i = 0; i < n; ++i) {
         const int s = i % STAGES;
-        if (!mbar_wait(bar(G_EMPTY0 + s), ((i / STAGES) & 1) ^ 1, abort_flag, kDevTimeoutMma)) {
-          ok = false;
-          break;
-        }
+        if (!mbar_wait(bar(G_EMPTY0 + s), ((i / STAGES) & 1) ^ 1, abort_flag, kDevTimeoutMma)) break;
         const uint32_t dst = base + KV_OFF_RING + s * KV_ENTRY;
-        mbar_expect_tx(bar(G_FULL0 + s), 2 * SLOT + 1024);
-        const int64_t srow = (int64_t)bh * p.Lpad;
-        if (!two) {
-          const int qi = bwd_block(ents, i, p.NBq);
-          load_tile(dst, &tq, bar(G_FULL0 + s), 128 * qi, 0, false, h, b);
-          load_tile(dst + SLOT, &tdo, bar(G_FULL0 + s), 128 * qi, 0, false, h, b);
-          bulk_load(dst + 2 * SLOT, p.lse + srow + 128 * qi, 512, bar(G_FULL0 + s));
-          bulk_load(dst + 2 * SLOT + 512, p.delta + srow + 128 * qi, 512, bar(G_FULL0 + s));
-        } else {
-          const int i0 = bwd_block64(ents[2 * i], p.NBq), i1 = bwd_block64(ents[2 * i + 1], p.NBq);
-          load_tile(dst, &tq, bar(G_FULL0 + s), 64 * i0, 64 * i1, true, h, b);
-          load_tile(dst + SLOT, &tdo, bar(G_FULL0 + s), 64 * i0, 64 * i1, true, h, b);
-          bulk_load(dst + 2 * SLOT, p.lse + srow + 64 * i0, 256, bar(G_FULL0 + s));
-          bulk_load(dst + 2 * SLOT + 256, p.lse + srow + 64 * i1, 256, bar(G_FULL0 + s));
-          bulk_load(dst + 2 * SLOT + 512, p.delta + srow + 64 * i0, 256, bar(G_FULL0 + s));
-          bulk_load(dst + 2 * SLOT + 768, p.delta + srow + 64 * i1, 256, bar(G_FULL0 + s));
-        }
+        mbar_expect_tx(bar(G_FULL0 + s), 2 * HALF + 512);
+        const int r0 = step_query(i);
+        load_half(dst, &tq, bar(G_FULL0 + s), r0, h, b);
+        load_half(dst + HALF, &tdo, bar(G_FULL0 + s), r0, h, b);
+        bulk_load(dst + 2 * HALF, lse_row + r0, 256, bar(G_FULL0 + s));
+        bulk_load(dst + 2 * HALF + 256, dlt_row + r0, 256, bar(G_FULL0 + s));
       }
       const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
       bool drained = mbar_wait_until(bar(G_TILE), 0, deadline);
@@ -485,51 +484,64 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA
     if (elect_one()) {
-      const uint32_t id_ss = idesc_bf16_f32(128, 128, false, false);
-      const uint32_t id_ts = idesc_bf16_f32(128, 128, false, true);
+      const uint32_t id_s = idesc_bf16_f32(128, 64, false, false);
+      const uint32_t id_a = idesc_bf16_f32(128, 128, false, true);
       bool ok = mbar_wait(bar(G_TILE), 0, abort_flag, kDevTimeoutLoad);
+      auto issue_acc = [&](int i) {
+        if (!mbar_wait(bar(G_DS0 + (i & 1)), (i >> 1) & 1, abort_flag, kDevTimeoutSoftmax)) {
+          ok = false;
+          return;
+        }
+        tc_fence_after();
+        const uint32_t sq = base + KV_OFF_RING + (i % STAGES) * KV_ENTRY, sdo = sq + HALF;
+        const uint32_t tb = tmem + 128 * (i & 1);
+        mma_step_ts(tmem + 256, tb, sdo, id_a, i > 0);      // dV += P^T dO
+        mma_step_ts(tmem + 384, tb + 64, sq, id_a, i > 0);  // dK += dS^T Q
+        mma_commit(bar(G_EMPTY0 + i % STAGES));
+      };
       for (int i = 0; i < n && ok; ++i) {
         const int s = i % STAGES;
-        if (!mbar_wait(bar(G_FULL0 + s), (i / STAGES) & 1, abort_flag, kDevTimeoutLoad)) break;
+        if (!mbar_wait(bar(G_FULL0 + s), (i / STAGES) & 1, abort_flag, kDevTimeoutLoad)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t sq = base + KV_OFF_RING + s * KV_ENTRY, sdo = sq + SLOT;
-        mma_tile_ss(tmem, base + KV_OFF_K, sq, id_ss);          // S^T  = K Q^T
-        mma_tile_ss(tmem + 128, base + KV_OFF_V, sdo, id_ss);   // dP^T = V dO^T
-        mma_commit(bar(G_SF));
-        if (!mbar_wait(bar(G_DS), i & 1, abort_flag, kDevTimeoutSoftmax)) break;
-        tc_fence_after();
-        mma_tile_ts(tmem + 256, tmem, sdo, id_ts, i > 0);       // dV += P^T dO
-        mma_tile_ts(tmem + 384, tmem + 128, sq, id_ts, i > 0);  // dK += dS^T Q
-        mma_commit(bar(G_EMPTY0 + s));
+        const uint32_t sq = base + KV_OFF_RING + s * KV_ENTRY, sdo = sq + HALF;
+        const uint32_t tb = tmem + 128 * (i & 1);
+        mma_step_ss(tb, base + KV_OFF_K, sq, id_s);        // S^T  = K Q^T
+        mma_step_ss(tb + 64, base + KV_OFF_V, sdo, id_s);  // dP^T = V dO^T
+        mma_commit(bar(G_SF0 + (i & 1)));
+        if (i > 0) issue_acc(i - 1);
       }
+      if (ok && n > 0) issue_acc(n - 1);
       mma_commit(bar(G_ACC));
     }
   } else if (warp >= 4) {
-    // ---------------------------------------------- P^T, dS^T, then the dK/dV epilogue
-    const int hc = (warp - 4) >> 2;  // query half (columns) of this warpgroup
+    // ---------------------------------- P^T, dS^T of alternate steps, then the dK/dV epilogue
+    const int wg = (warp - 4) >> 2;
     const int q = warp & 3;
-    const int r = q * 32 + lane;      // key row = TMEM lane
+    const int r = q * 32 + lane;  // key row of the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    const uint32_t tS = tmem + lane_off + 64 * hc, tdP = tmem + 128 + lane_off + 64 * hc;
+    const uint32_t tS = tmem + lane_off + 128 * wg, tdP = tS + 64;
     const uint64_t sc2 = f2_pack(p.qk_scale, p.qk_scale);
     bool ok = true;
-    for (int i = 0; i < n; ++i) {
+    for (int i = wg; i < n; i += 2) {
       const int s = i % STAGES;
-      bool got = mbar_wait(bar(G_SF), i & 1, abort_flag, kDevTimeoutMma);
-      // the entry's lse2 / delta (bulk copies) are visible once its load barrier completed
+      bool got = mbar_wait(bar(G_SF0 + wg), (i >> 1) & 1, abort_flag, kDevTimeoutMma);
+      // the step's lse2 / delta (bulk copies) are visible once its load barrier completed
       got = got && mbar_wait(bar(G_FULL0 + s), (i / STAGES) & 1, abort_flag, kDevTimeoutLoad);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      bool sel = true;  // this key row's block was selected by this half's query block
+      bool sel = true;  // block 64: did this step's query block select this key row's block?
       if (two) {
-        const int32_t e = ents[2 * i + hc];
+        const int32_t e = ents[i];
         sel = e >= 0 && ((e >> (28 + (r >> 6))) & 1);
       }
-      const float* lse_s = reinterpret_cast<const float*>(gbase + KV_OFF_RING + s * KV_ENTRY + 2 * SLOT) + 64 * hc;
-      const float* dlt_s = lse_s + 128;
+      const float* lse_s = reinterpret_cast<const float*>(gbase + KV_OFF_RING + s * KV_ENTRY + 2 * HALF);
+      const float* dlt_s = lse_s + 64;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t sv[32], dv[32];
@@ -550,13 +562,13 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
           wp[e] = pack_bf2(p0, p1);
           wd[e] = pack_bf2(p0 * (__uint_as_float(dv[2 * e]) - d2.x), p1 * (__uint_as_float(dv[2 * e + 1]) - d2.y));
         }
-        tmem_st16(tS + 16 * c, wp);   // packed P^T over the S^T columns of this half
-        tmem_st16(tdP + 16 * c, wd);  // packed dS^T over the dP^T columns of this half
+        tmem_st16(tS + 16 * c, wp);   // packed P^T over the first 32 S^T columns of the buffer
+        tmem_st16(tdP + 16 * c, wd);  // packed dS^T over the first 32 dP^T columns
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(G_DS));
+      if (lane == 0) mbar_arrive(bar(G_DS0 + wg));
     }
     if (ok && n > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(G_ACC), 0, abort_flag, kDevTimeoutMma));
     tc_fence_after();
@@ -569,7 +581,7 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
       for (int which = 0; which < 2; ++which) {  // dV, then dK (scaled by D^-1/2)
         uint32_t v[64];
         if (n > 0) {
-          const uint32_t tA = tmem + 256 + 128 * which + lane_off + 64 * hc;
+          const uint32_t tA = tmem + 256 + 128 * which + lane_off + 64 * wg;
           tmem_ld32(tA, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
           tmem_ld32(tA + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
           tmem_ld_wait();
@@ -583,7 +595,7 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
           pk[which][e] = pack_bf2(__uint_as_float(v[2 * e]) * sc, __uint_as_float(v[2 * e + 1]) * sc);
       }
       if (tok < p.L) {
-        const int64_t goff = (int64_t)b * p.g_sB + (int64_t)h * p.g_sH + (int64_t)tok * p.g_sT + 64 * hc;
+        const int64_t goff = (int64_t)b * p.g_sB + (int64_t)h * p.g_sH + (int64_t)tok * p.g_sT + 64 * wg;
 #pragma unroll
         for (int which = 0; which < 2; ++which) {
           uint4* dst = reinterpret_cast<uint4*>((which ? p.dk : p.dv) + goff);

@@ -725,10 +725,11 @@ int rola_b200_sparse_attn_bwd(const void* q, const void* k, int64_t qk_sB, int64
   ROLA_CHECK(aligned16(dq) && aligned16(dk) && aligned16(dv) && g_sB % 8 == 0 && g_sH % 8 == 0 && g_sT % 8 == 0,
              "sparse_attn_bwd: gradient rows must be 16-byte aligned");
   CUtensorMap tq, tk, tv, tdo;
-  ROLA_TRY(make_head_map(&tq, q, 128, qk_sB, qk_sH, qk_sT, L, H, B, "sparse_attn_bwd: q", blk));
-  ROLA_TRY(make_head_map(&tk, k, 128, qk_sB, qk_sH, qk_sT, L, H, B, "sparse_attn_bwd: k", blk));
-  ROLA_TRY(make_head_map(&tv, v, 128, v_sB, v_sH, v_sT, L, H, B, "sparse_attn_bwd: v", blk));
-  ROLA_TRY(make_head_map(&tdo, dout, 128, o_sB, o_sH, o_sT, L, H, B, "sparse_attn_bwd: dout", blk));
+  // 64-row boxes: the kernels stage 64-row steps and stack two boxes for the 128-row tiles
+  ROLA_TRY(make_head_map(&tq, q, 128, qk_sB, qk_sH, qk_sT, L, H, B, "sparse_attn_bwd: q", 64));
+  ROLA_TRY(make_head_map(&tk, k, 128, qk_sB, qk_sH, qk_sT, L, H, B, "sparse_attn_bwd: k", 64));
+  ROLA_TRY(make_head_map(&tv, v, 128, v_sB, v_sH, v_sT, L, H, B, "sparse_attn_bwd: v", 64));
+  ROLA_TRY(make_head_map(&tdo, dout, 128, o_sB, o_sH, o_sT, L, H, B, "sparse_attn_bwd: dout", 64));
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   float* delta = reinterpret_cast<float*>(ws + f.delta);
   int32_t* inv = reinterpret_cast<int32_t*>(ws + f.inv);

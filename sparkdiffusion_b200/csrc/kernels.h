@@ -167,8 +167,9 @@ struct AttnBwdParams {
 int launch_attn_bwd_delta(const __nv_bfloat16* o, int64_t o_sB, int64_t o_sH, int64_t o_sT, const __nv_bfloat16* dout,
                           int64_t d_sB, int64_t d_sH, int64_t d_sT, int B, int H, int L, int Lpad, float* delta,
                           cudaStream_t s);
-// inverse of a selection lut [BH, NBq, topk]: per key tile the ascending list of the
-// query blocks that selected it (map: BH*NBq*NBk bytes of scratch; width = NBq + 2)
+// inverse of a selection lut [BH, NBq, topk]: per 128-row key tile the ascending list
+// of the query blocks that selected it, count first; block 64 entries carry two
+// selection bits (map: BH*NBq*NBk bytes of scratch; width >= NBq + 1)
 int launch_lut_invert(const int32_t* lut, int BH, int NBq, int NBk, int topk, int blk64, uint8_t* map, int32_t* inv,
                       int width, cudaStream_t s);
 // dq (query-stationary), then dk and dv (key-stationary); maps as the forward's (rows = block size)
