@@ -19,39 +19,48 @@
 // P before P.V); every accumulation is fp32 in tensor memory.
 //
 // Both kernels keep a 128-row tile stationary (Q and dO of a query tile, or K
-// and V of a key tile) and walk the other side in steps of 64 rows: a 128-row
-// block is two steps, a 64-row block (block size 64) one step whose selection
-// bits say which 64-row half of the stationary tile selected it.  The S / dP
-// accumulators of a step are double-buffered in tensor memory, and the two
-// softmax warpgroups take alternate steps, so the MMA warp computes step i+1's
-// S and dP while step i's P and dS are computed, and two steps' exp2 work runs
-// at once.
+// and V of a key tile) and walk the other side in steps of 64 rows: a
+// 128-row block is two steps, a 64-row block (block size 64) one step whose
+// selection bits say which 64-row half of the stationary tile selected it.  The S / dP
+// accumulators of a step are multi-buffered in tensor memory, and the
+// softmax warpgroups take the steps in turn, so the MMA warp computes the
+// next steps' S and dP while step i's P and dS are computed, and several
+// steps' exp2 work runs at once.
 //
-// 384 threads.  Warp 0 lane 0: TMA producer (no multicast).  Warp 1: tensor
-// memory owner and MMA issuer (one elected thread).  Warpgroups 1 and 2: the
-// steps of even / odd index (thread = TMEM lane = stationary-tile row), then
-// the epilogue of one 64-column half of the accumulators each.  Every
-// mbarrier wait is bounded (error flag + abort, as in the forward).
+// Warp 0 lane 0: TMA producer (no multicast).  Warp 1: tensor memory owner
+// and MMA issuer (one elected thread).  The softmax warpgroups (thread = TMEM
+// lane = stationary-tile row) take the steps in turn: the dq kernel has three
+// (512 threads, three S / dP buffers, so the MMA warp runs two steps ahead),
+// the dkdv kernel two buffers (its two 128-column accumulators fill the rest
+// of the tensor memory) with both of its warpgroups on every step, 32
+// columns each.  Warpgroups 1 and 2 then store one 64-column half of the
+// accumulators each.  Every mbarrier wait is bounded (error flag + abort, as
+// in the forward).
 #include "common.cuh"
 #include "kernels.h"
 
 namespace rola {
 
 namespace bwd {
-constexpr int THREADS = 384;
+constexpr int DQ_THREADS = 512;      // dq kernel: three softmax warpgroups
+constexpr int DQ_NBUF = 3;           // dq kernel: S / dP buffers in tensor memory (steps in flight)
+constexpr int DQ_ACC = 128 * DQ_NBUF;  // dq kernel: TMEM column of the dQ accumulator
 constexpr int BOX = 8192;          // [64 rows x 64 bf16] box, 128-byte swizzle
 constexpr int HALF = 2 * BOX;      // 64 rows x 128 d: one step's operand
 constexpr int TILE = 2 * HALF;     // 128 rows x 128 d: the stationary operands
 constexpr int BOX128 = 2 * BOX;    // [128 rows x 64 bf16] (two 64-row boxes stacked)
-constexpr int STAGES = 4;
+constexpr int THREADS = 384;      // dkdv kernel: two softmax warpgroups, both on every step
+constexpr int KV_STAGES = 4;  // dkdv ring
+constexpr int DQ_STAGES = 5;  // dq ring
+constexpr int MAX_STAGES = 5;
 // dq kernel: Q and dO of the query tile, then the ring of (K, V) 64-row steps
 constexpr int DQ_OFF_Q = 0, DQ_OFF_DO = TILE, DQ_OFF_RING = 2 * TILE;
 constexpr int DQ_ENTRY = 2 * HALF;
-constexpr int DQ_OFF_BAR = DQ_OFF_RING + STAGES * DQ_ENTRY;  // 192 KB
+constexpr int DQ_OFF_BAR = DQ_OFF_RING + DQ_STAGES * DQ_ENTRY;  // 224 KB
 // dkdv kernel: K and V of the key tile, then the ring of (Q, dO, lse2, delta) 64-row steps
 constexpr int KV_OFF_K = 0, KV_OFF_V = TILE, KV_OFF_RING = 2 * TILE;
 constexpr int KV_ENTRY = 2 * HALF + 1024;  // + 64 lse2 + 64 delta (fp32), padded to keep 1024-byte alignment
-constexpr int KV_OFF_BAR = KV_OFF_RING + STAGES * KV_ENTRY;  // 196 KB
+constexpr int KV_OFF_BAR = KV_OFF_RING + KV_STAGES * KV_ENTRY;  // 196 KB
 constexpr int BAR_BYTES = 256;
 constexpr int DQ_SMEM = DQ_OFF_BAR + BAR_BYTES + 1024;
 constexpr int KV_SMEM = KV_OFF_BAR + BAR_BYTES + 1024;
@@ -63,13 +72,14 @@ constexpr float kSmScale = 0.08838834764831845f;  // 128^-1/2
 enum : int {
   G_TILE = 0,                        // stationary tiles loaded
   G_FULL0,                           // ring entry s loaded: G_FULL0 + s
-  G_EMPTY0 = G_FULL0 + bwd::STAGES,  // ring entry s consumed (MMA commit)
-  G_SF0 = G_EMPTY0 + bwd::STAGES,    // S and dP of a step in TMEM buffer b: G_SF0 + b
-  G_DS0 = G_SF0 + 2,                 // dS (and P) of a step in TMEM buffer b, 4 warp arrivals: G_DS0 + b
-  G_ACC = G_DS0 + 2,                 // accumulators final
+  G_EMPTY0 = G_FULL0 + bwd::MAX_STAGES,  // ring entry s consumed (MMA commit)
+  G_SF0 = G_EMPTY0 + bwd::MAX_STAGES,    // S and dP of a step in TMEM buffer b: G_SF0 + b
+  G_DS0 = G_SF0 + 3,                     // dS (and P) of a step in TMEM buffer b, 4 warp arrivals: G_DS0 + b
+  G_ACC = G_DS0 + 3,                     // accumulators final
   G_COUNT
 };
 static_assert(8 * G_COUNT + 16 <= bwd::BAR_BYTES, "barrier region too small");
+static_assert(bwd::DQ_NBUF <= 3, "barrier slots for three buffers");
 
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
@@ -202,15 +212,16 @@ __global__ void lut_invert_kernel(const uint8_t* __restrict__ map, int BH, int N
   if (lane == 0) out[0] = n;
 }
 
-// Tensor memory of both kernels (512 columns): S (or S^T) of buffer b at
-// [128 b, 128 b + 64), dP (or dP^T) at [128 b + 64, 128 b + 128); P^T and dS
-// (dS^T) packed bf16 over the first 32 columns of those; accumulators at
-// [256, 384) (dQ, or dV) and [384, 512) (dK).
+// Tensor memory (512 columns): S (or S^T) of buffer b at [128 b, 128 b + 64),
+// dP (or dP^T) at [128 b + 64, 128 b + 128); P^T and dS (dS^T) packed bf16
+// over the first 32 columns of those.  dq kernel: three buffers, dQ at
+// [384, 512).  dkdv kernel: two buffers (each warpgroup packs its 32 columns'
+// P^T / dS^T over the first 16 of them), dV at [256, 384), dK at [384, 512).
 
 // ---------------------------------------------------------------------------
 // dq kernel: one CTA per (128-row query tile, b*h)
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(bwd::THREADS, 1)
+__global__ void __launch_bounds__(bwd::DQ_THREADS, 1)
     attn_bwd_dq_tcgen05(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
                         const AttnBwdParams p) {
@@ -240,11 +251,11 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar(G_TILE), 1);
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < DQ_STAGES; ++s) {
       mbar_init(bar(G_FULL0 + s), 1);
       mbar_init(bar(G_EMPTY0 + s), 1);
     }
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < DQ_NBUF; ++t) {
       mbar_init(bar(G_SF0 + t), 1);
       mbar_init(bar(G_DS0 + t), 4);
     }
@@ -272,8 +283,8 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
       load_tile(base + DQ_OFF_Q, &tq, bar(G_TILE), 128 * m, h, b);
       load_tile(base + DQ_OFF_DO, &tdo, bar(G_TILE), 128 * m, h, b);
       for (int i = 0; i < n; ++i) {
-        const int s = i % STAGES;
-        if (!mbar_wait(bar(G_EMPTY0 + s), ((i / STAGES) & 1) ^ 1, abort_flag, kDevTimeoutMma)) break;
+        const int s = i % DQ_STAGES;
+        if (!mbar_wait(bar(G_EMPTY0 + s), ((i / DQ_STAGES) & 1) ^ 1, abort_flag, kDevTimeoutMma)) break;
         const uint32_t dst = base + DQ_OFF_RING + s * DQ_ENTRY;
         mbar_expect_tx(bar(G_FULL0 + s), 2 * HALF);
         const int r0 = step_key(i);
@@ -283,47 +294,48 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
       // drain: no TMA may still target shared memory when the CTA exits
       const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
       bool drained = mbar_wait_until(bar(G_TILE), 0, deadline);
-      for (int i = max(0, n - STAGES); i < n && drained; ++i)
-        drained = mbar_wait_until(bar(G_FULL0 + i % STAGES), (i / STAGES) & 1, deadline);
+      for (int i = max(0, n - DQ_STAGES); i < n && drained; ++i)
+        drained = mbar_wait_until(bar(G_FULL0 + i % DQ_STAGES), (i / DQ_STAGES) & 1, deadline);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA
-    // order: S_i, dP_i, then dQ += dS_{i-1} K_{i-1} once step i-1's dS is in
-    // TMEM, so the tensor core computes S_i / dP_i during step i-1's softmax
+    // order: S_i, dP_i, then dQ += dS_{i-2} K_{i-2} once step i-2's dS is in
+    // TMEM, so the tensor core computes S_i / dP_i while steps i-2 and i-1
+    // are in the softmax (three buffers, three softmax warpgroups)
     if (elect_one()) {
       const uint32_t id_s = idesc_bf16_f32(128, 64, false, false);
       const uint32_t id_q = idesc_bf16_f32(128, 128, false, true);
       bool ok = mbar_wait(bar(G_TILE), 0, abort_flag, kDevTimeoutLoad);
       auto issue_dq = [&](int i) {
-        if (!mbar_wait(bar(G_DS0 + (i & 1)), (i >> 1) & 1, abort_flag, kDevTimeoutSoftmax)) {
+        if (!mbar_wait(bar(G_DS0 + i % DQ_NBUF), (i / DQ_NBUF) & 1, abort_flag, kDevTimeoutSoftmax)) {
           ok = false;
           return;
         }
         tc_fence_after();
-        const uint32_t sk = base + DQ_OFF_RING + (i % STAGES) * DQ_ENTRY;
-        mma_step_ts(tmem + 256, tmem + 128 * (i & 1), sk, id_q, i > 0);  // dQ += dS K
-        mma_commit(bar(G_EMPTY0 + i % STAGES));
+        const uint32_t sk = base + DQ_OFF_RING + (i % DQ_STAGES) * DQ_ENTRY;
+        mma_step_ts(tmem + DQ_ACC, tmem + 128 * (i % DQ_NBUF), sk, id_q, i > 0);  // dQ += dS K
+        mma_commit(bar(G_EMPTY0 + i % DQ_STAGES));
       };
       for (int i = 0; i < n && ok; ++i) {
-        const int s = i % STAGES;
-        if (!mbar_wait(bar(G_FULL0 + s), (i / STAGES) & 1, abort_flag, kDevTimeoutLoad)) {
+        const int s = i % DQ_STAGES;
+        if (!mbar_wait(bar(G_FULL0 + s), (i / DQ_STAGES) & 1, abort_flag, kDevTimeoutLoad)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t sk = base + DQ_OFF_RING + s * DQ_ENTRY, sv = sk + HALF;
-        const uint32_t tb = tmem + 128 * (i & 1);
+        const uint32_t tb = tmem + 128 * (i % DQ_NBUF);
         mma_step_ss(tb, base + DQ_OFF_Q, sk, id_s);        // S  = Q K^T
         mma_step_ss(tb + 64, base + DQ_OFF_DO, sv, id_s);  // dP = dO V^T
-        mma_commit(bar(G_SF0 + (i & 1)));
-        if (i > 0) issue_dq(i - 1);
+        mma_commit(bar(G_SF0 + i % DQ_NBUF));
+        if (i >= DQ_NBUF - 1) issue_dq(i - (DQ_NBUF - 1));
       }
-      if (ok) issue_dq(n - 1);
+      for (int i = max(0, n - (DQ_NBUF - 1)); i < n && ok; ++i) issue_dq(i);
       mma_commit(bar(G_ACC));
     }
   } else if (warp >= 4) {
     // -------------------------------------- dS of alternate steps, then the dQ epilogue
-    const int wg = (warp - 4) >> 2;  // steps i with i % 2 == wg; epilogue columns [64 wg, 64 wg + 64)
+    const int wg = (warp - 4) >> 2;  // steps i with i % 3 == wg; warpgroups 0 and 1: epilogue columns [64 wg, 64 wg + 64)
     const int q = warp & 3;
     const int r = q * 32 + lane;  // query row of the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
@@ -333,8 +345,8 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
     const float dlt = p.delta[(int64_t)bh * p.Lpad + tok];
     const uint64_t sc2 = f2_pack(p.qk_scale, p.qk_scale), nl2 = f2_pack(-lse, -lse);
     bool ok = true;
-    for (int i = wg; i < n; i += 2) {
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(G_SF0 + wg), (i >> 1) & 1, abort_flag, kDevTimeoutMma))) {
+    for (int i = wg; i < n; i += DQ_NBUF) {
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(G_SF0 + wg), (i / DQ_NBUF) & 1, abort_flag, kDevTimeoutMma))) {
         ok = false;
         break;
       }
@@ -369,10 +381,11 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(G_DS0 + wg));
     }
+    if (wg == 2) ok = false;  // the third warpgroup has no epilogue columns
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(G_ACC), 0, abort_flag, kDevTimeoutMma));
     tc_fence_after();
     if (ok) {
-      const uint32_t tQ = tmem + 256 + lane_off + 64 * wg;
+      const uint32_t tQ = tmem + DQ_ACC + lane_off + 64 * wg;
       uint32_t v[64];
       tmem_ld32(tQ, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
       tmem_ld32(tQ + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
@@ -401,7 +414,10 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
-// dk/dv kernel: one CTA per (128-row key tile, b*h)
+// dk/dv kernel: one CTA per (128-row key tile, b*h).  Both softmax
+// warpgroups work on every step, 32 query columns each, so a step's P^T /
+// dS^T take half the time on the chain (S^T, dP^T) -> softmax -> (dV, dK);
+// the two S^T / dP^T buffers let the next step's S^T and dP^T run meanwhile.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(bwd::THREADS, 1)
     attn_bwd_dkdv_tcgen05(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -432,13 +448,13 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar(G_TILE), 1);
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < KV_STAGES; ++s) {
       mbar_init(bar(G_FULL0 + s), 1);
       mbar_init(bar(G_EMPTY0 + s), 1);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(G_SF0 + t), 1);
-      mbar_init(bar(G_DS0 + t), 4);
+      mbar_init(bar(G_DS0 + t), 8);
     }
     mbar_init(bar(G_ACC), 1);
     *abort_flag = 0;
@@ -466,8 +482,8 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
       const float* lse_row = p.lse + (int64_t)bh * p.Lpad;
       const float* dlt_row = p.delta + (int64_t)bh * p.Lpad;
       for (int i = 0; i < n; ++i) {
-        const int s = i % STAGES;
-        if (!mbar_wait(bar(G_EMPTY0 + s), ((i / STAGES) & 1) ^ 1, abort_flag, kDevTimeoutMma)) break;
+        const int s = i % KV_STAGES;
+        if (!mbar_wait(bar(G_EMPTY0 + s), ((i / KV_STAGES) & 1) ^ 1, abort_flag, kDevTimeoutMma)) break;
         const uint32_t dst = base + KV_OFF_RING + s * KV_ENTRY;
         mbar_expect_tx(bar(G_FULL0 + s), 2 * HALF + 512);
         const int r0 = step_query(i);
@@ -478,8 +494,8 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
       }
       const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
       bool drained = mbar_wait_until(bar(G_TILE), 0, deadline);
-      for (int i = max(0, n - STAGES); i < n && drained; ++i)
-        drained = mbar_wait_until(bar(G_FULL0 + i % STAGES), (i / STAGES) & 1, deadline);
+      for (int i = max(0, n - KV_STAGES); i < n && drained; ++i)
+        drained = mbar_wait_until(bar(G_FULL0 + i % KV_STAGES), (i / KV_STAGES) & 1, deadline);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA
@@ -493,15 +509,20 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
           return;
         }
         tc_fence_after();
-        const uint32_t sq = base + KV_OFF_RING + (i % STAGES) * KV_ENTRY, sdo = sq + HALF;
+        const uint32_t sq = base + KV_OFF_RING + (i % KV_STAGES) * KV_ENTRY, sdo = sq + HALF;
         const uint32_t tb = tmem + 128 * (i & 1);
-        mma_step_ts(tmem + 256, tb, sdo, id_a, i > 0);      // dV += P^T dO
-        mma_step_ts(tmem + 384, tb + 64, sq, id_a, i > 0);  // dK += dS^T Q
-        mma_commit(bar(G_EMPTY0 + i % STAGES));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {  // dV += P^T dO, dK += dS^T Q; queries 16 kk.. of warpgroup kk / 2
+          const uint32_t a = 32 * (kk >> 1) + 8 * (kk & 1);
+          mma_bf16_ts(tmem + 256, tb + a, sdesc_sw128(sdo + kk * 2048, BOX, 1024), id_a, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ts(tmem + 384, tb + 64 + a, sdesc_sw128(sq + kk * 2048, BOX, 1024), id_a,
+                      (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(bar(G_EMPTY0 + i % KV_STAGES));
       };
       for (int i = 0; i < n && ok; ++i) {
-        const int s = i % STAGES;
-        if (!mbar_wait(bar(G_FULL0 + s), (i / STAGES) & 1, abort_flag, kDevTimeoutLoad)) {
+        const int s = i % KV_STAGES;
+        if (!mbar_wait(bar(G_FULL0 + s), (i / KV_STAGES) & 1, abort_flag, kDevTimeoutLoad)) {
           ok = false;
           break;
         }
@@ -517,19 +538,19 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
       mma_commit(bar(G_ACC));
     }
   } else if (warp >= 4) {
-    // ---------------------------------- P^T, dS^T of alternate steps, then the dK/dV epilogue
+    // ---------- P^T, dS^T of query columns [32 wg, 32 wg + 32) of every step, then the dK/dV epilogue
     const int wg = (warp - 4) >> 2;
     const int q = warp & 3;
     const int r = q * 32 + lane;  // key row of the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    const uint32_t tS = tmem + lane_off + 128 * wg, tdP = tS + 64;
     const uint64_t sc2 = f2_pack(p.qk_scale, p.qk_scale);
     bool ok = true;
-    for (int i = wg; i < n; i += 2) {
-      const int s = i % STAGES;
-      bool got = mbar_wait(bar(G_SF0 + wg), (i >> 1) & 1, abort_flag, kDevTimeoutMma);
+    for (int i = 0; i < n; ++i) {
+      const int s = i % KV_STAGES;
+      const uint32_t tS = tmem + lane_off + 128 * (i & 1) + 32 * wg, tdP = tS + 64;
+      bool got = mbar_wait(bar(G_SF0 + (i & 1)), (i >> 1) & 1, abort_flag, kDevTimeoutMma);
       // the step's lse2 / delta (bulk copies) are visible once its load barrier completed
-      got = got && mbar_wait(bar(G_FULL0 + s), (i / STAGES) & 1, abort_flag, kDevTimeoutLoad);
+      got = got && mbar_wait(bar(G_FULL0 + s), (i / KV_STAGES) & 1, abort_flag, kDevTimeoutLoad);
       if (!__all_sync(0xffffffffu, got)) {
         ok = false;
         break;
@@ -540,19 +561,18 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
         const int32_t e = ents[i];
         sel = e >= 0 && ((e >> (28 + (r >> 6))) & 1);
       }
-      const float* lse_s = reinterpret_cast<const float*>(gbase + KV_OFF_RING + s * KV_ENTRY + 2 * HALF);
+      const float* lse_s = reinterpret_cast<const float*>(gbase + KV_OFF_RING + s * KV_ENTRY + 2 * HALF) + 32 * wg;
       const float* dlt_s = lse_s + 64;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      {
         uint32_t sv[32], dv[32];
-        tmem_ld32(tS + 32 * c, sv);
-        tmem_ld32(tdP + 32 * c, dv);
+        tmem_ld32(tS, sv);
+        tmem_ld32(tdP, dv);
         tmem_ld_wait();
         uint32_t wp[16], wd[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float2 l2 = *reinterpret_cast<const float2*>(lse_s + 32 * c + 2 * e);
-          const float2 d2 = *reinterpret_cast<const float2*>(dlt_s + 32 * c + 2 * e);
+          const float2 l2 = *reinterpret_cast<const float2*>(lse_s + 2 * e);
+          const float2 d2 = *reinterpret_cast<const float2*>(dlt_s + 2 * e);
           float x0, x1;
           f2_unpack(fma_f32x2(f2_pack(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sc2,
                               f2_pack(-l2.x, -l2.y)),
@@ -562,13 +582,13 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
           wp[e] = pack_bf2(p0, p1);
           wd[e] = pack_bf2(p0 * (__uint_as_float(dv[2 * e]) - d2.x), p1 * (__uint_as_float(dv[2 * e + 1]) - d2.y));
         }
-        tmem_st16(tS + 16 * c, wp);   // packed P^T over the first 32 S^T columns of the buffer
-        tmem_st16(tdP + 16 * c, wd);  // packed dS^T over the first 32 dP^T columns
+        tmem_st16(tS, wp);   // packed P^T over the first 16 of this warpgroup's S^T columns
+        tmem_st16(tdP, wd);  // packed dS^T over the first 16 of its dP^T columns
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(G_DS0 + wg));
+      if (lane == 0) mbar_arrive(bar(G_DS0 + (i & 1)));
     }
     if (ok && n > 0) ok = __all_sync(0xffffffffu, mbar_wait(bar(G_ACC), 0, abort_flag, kDevTimeoutMma));
     tc_fence_after();
@@ -640,7 +660,7 @@ int launch_attn_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensor
   using namespace bwd;
   cudaFuncSetAttribute(attn_bwd_dq_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize, DQ_SMEM);
   cudaFuncSetAttribute(attn_bwd_dkdv_tcgen05, cudaFuncAttributeMaxDynamicSharedMemorySize, KV_SMEM);
-  attn_bwd_dq_tcgen05<<<dim3(p.NQT, p.B * p.H), THREADS, DQ_SMEM, s>>>(tq, tk, tv, tdo, p);
+  attn_bwd_dq_tcgen05<<<dim3(p.NQT, p.B * p.H), DQ_THREADS, DQ_SMEM, s>>>(tq, tk, tv, tdo, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return (int)e;
   attn_bwd_dkdv_tcgen05<<<dim3(p.NKT, p.B * p.H), THREADS, KV_SMEM, s>>>(tq, tk, tv, tdo, p);
