@@ -165,7 +165,9 @@ int rola_b200_qk_norm_scatter(const rola_scatter_args* args, int compact, rola_s
 /* rola_b200_qkv_gemm on rows of this chunk while four spare warps of every
  * GEMM CTA run the scatter `side` of an earlier chunk (B == 1, ssq given):
  * the NVLink traffic of the exchange hides under the tensor-core work of the
- * next projection.  No counterpart in the reference. */
+ * next projection.  side == NULL: the same single-SM persistent GEMM with no
+ * side job (rola_b200_qkv_gemm may pick the SM-pair kernel instead).  No
+ * counterpart in the reference. */
 int rola_b200_qkv_gemm_scatter(const void* x, const void* w, const void* bias, void* out, float* ssq, int64_t M,
                                int64_t N, int64_t K, const rola_scatter_args* side, rola_stream_t stream);
 

@@ -162,7 +162,7 @@ int rola_b200_device_status(int clear) {
 }
 
 static int qkv_gemm_impl(const void* x, const void* w, const void* bias, void* out, float* ssq, int64_t M, int64_t N,
-                         int64_t K, const NormRopeParams* side, rola_stream_t stream) {
+                         int64_t K, const NormRopeParams* side, rola_stream_t stream, bool allow_pairs = true) {
   ROLA_CHECK(x && w && out, "qkv_gemm: null pointer");
   ROLA_CHECK(M > 0 && M < (1ll << 31), "qkv_gemm: M out of range");
   ROLA_CHECK(N > 0 && N % 256 == 0 && N <= 65536, "qkv_gemm: N must be a positive multiple of 256");
@@ -175,7 +175,7 @@ static int qkv_gemm_impl(const void* x, const void* w, const void* bias, void* o
     const uint32_t box[2] = {64, 128};
     ROLA_TRY(make_map(&ta, x, 2, dims, strides, box, "qkv_gemm: x"));
   }
-  const bool pairs = side == nullptr && M >= 256;  // the two-SM kernel (no side job)
+  const bool pairs = allow_pairs && side == nullptr && M >= 256;  // the two-SM kernel (no side job)
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
     const uint64_t strides[1] = {(uint64_t)K * 2};
@@ -408,6 +408,9 @@ int rola_b200_qk_norm_scatter(const rola_scatter_args* args, int compact, rola_s
 
 int rola_b200_qkv_gemm_scatter(const void* x, const void* w, const void* bias, void* out, float* ssq, int64_t M,
                                int64_t N, int64_t K, const rola_scatter_args* side, rola_stream_t stream) {
+  // no side job: the same single-SM persistent kernel without spare-warp work
+  // (the first chunk of an overlapped exchange runs on the kernel of the others)
+  if (side == nullptr) return qkv_gemm_impl(x, w, bias, out, ssq, M, N, K, nullptr, stream, false);
   NormRopeParams p{};
   ROLA_TRY(scatter_params(side, true, &p, "qkv_gemm_scatter"));
   ROLA_CHECK(side->B == 1 && side->ssq != nullptr, "qkv_gemm_scatter: the side job needs B == 1 and the GEMM sums");

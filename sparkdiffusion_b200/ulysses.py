@@ -157,8 +157,10 @@ def _gemm_scatter_overlapped(x_local, w_qkv, b_qkv, nwq, nwk, gw, gb, xc, H, p, 
             t0, t1 = t1, t1 + n
             r0, r1 = b * Ls + t0, b * Ls + t1
             if prev is None:
-                _lib.call("rola_b200_qkv_gemm", _ptr(x2d[r0]), _ptr(w), _ptr(bias), _ptr(qkv[r0]), _ptr(ssq[r0]),
-                          r1 - r0, 3 * dim, dim, st)
+                # the first chunk on the single-SM kernel too (side job NULL): every chunk of
+                # the overlapped exchange runs on one GEMM kernel
+                _lib.call("rola_b200_qkv_gemm_scatter", _ptr(x2d[r0]), _ptr(w), _ptr(bias), _ptr(qkv[r0]),
+                          _ptr(ssq[r0]), r1 - r0, 3 * dim, dim, None, st)
             else:
                 _lib.call("rola_b200_qkv_gemm_scatter", _ptr(x2d[r0]), _ptr(w), _ptr(bias), _ptr(qkv[r0]),
                           _ptr(ssq[r0]), r1 - r0, 3 * dim, dim, ctypes.byref(prev), st)
