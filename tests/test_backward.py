@@ -185,3 +185,42 @@ def test_rola_layer_training_step(blk, monkeypatch):
     for n, g in grads.items():
         assert_bf16_close(g, dict(layer.named_parameters())[n].grad, f"blk{blk} d{n}", max_tol=LAYER_MAX,
                           mean_tol=LAYER_MEAN)
+
+
+def test_backward_identities_at_full_c4_size():
+    """Size-independent identities of the exact gradient at C4's full shape
+    (L = 75600, 40 heads, top-18 of 591 blocks of 128), where the oracle is too
+    slow: every query row's softmax weights sum to 1, so the sum of dV over all
+    key rows equals the sum of dO over all query rows (per head and dimension);
+    and sum_i q_i . dQ_i = sum_j k_j . dK_j = D^-1/2 sum_ij dS_ij (q_i . k_j), one
+    side from each backward kernel.  Bounds: 1e-2 of the natural scale
+    (sqrt of the sum of squares of the summed terms); bf16 rounding of the
+    outputs and of P / dS stays orders of magnitude below it."""
+    B, H, L, blk = 1, 40, 75600, 128
+    g = torch.Generator(device="cuda").manual_seed(21)
+
+    def mk():
+        return torch.randn(B, L, H, 128, device="cuda", generator=g).to(torch.bfloat16).transpose(1, 2)
+
+    q, k, v, do = mk(), mk(), mk(), mk()
+    lut, topk, _ = train.select_blocks(q, k, 18.5 / 591, blk)
+    assert topk == 18
+    o, lse = ops.sparse_attention_fwd_lse(q, k, v, lut, blk, topk)
+    dq, dk, dv = ops.sparse_attention_bwd(q, k, v, o, do, lut, None, lse, blk, topk)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    for t in (dq, dk, dv):
+        assert torch.isfinite(t).all()
+    # (1) sum over key rows of dV == sum over query rows of dO, per (head, d)
+    s_dv = dv.float().sum(dim=2)
+    s_do = do.float().sum(dim=2)
+    scale_v = dv.float().pow(2).sum(dim=2).sqrt()
+    worst_v = ((s_dv - s_do).abs() / scale_v).max().item()
+    assert worst_v <= 1e-2, f"sum dV vs sum dO: {worst_v:.3e} of the scale"
+    # (2) sum_i q_i . dQ_i == sum_j k_j . dK_j, per head (the dq and dkdv kernels against each other)
+    qdq = (q.float() * dq.float()).sum(-1)  # [B, H, L]
+    kdk = (k.float() * dk.float()).sum(-1)
+    lhs, rhs = qdq.sum(-1), kdk.sum(-1)
+    scale_s = torch.maximum(qdq.pow(2).sum(-1).sqrt(), kdk.pow(2).sum(-1).sqrt())
+    worst_s = ((lhs - rhs).abs() / scale_s).max().item()
+    assert worst_s <= 1e-2, f"sum q.dQ vs sum k.dK: {worst_s:.3e} of the scale"
