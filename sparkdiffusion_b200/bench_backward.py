@@ -13,6 +13,13 @@ dQ).  The kernels recompute S and dP in both backward kernels (seven GEMMs
 executed, ``tflops_executed``), which the algorithmic figure does not credit.
 
     python -m sparkdiffusion_b200.bench_backward --seq 75600 --heads 40 --blk 128
+
+``--dense``: dense attention (every key block selected) forward + backward
+against PyTorch SDPA with the cuDNN backend, which the reference's dense layers
+train through (sparkdiffusion/utils/attention.py:122-186), on the same inputs;
+FLOPs 4*L^2*D*H*B forward, 2.5x that backward.
+
+    python -m sparkdiffusion_b200.bench_backward --dense --seq 32760 --heads 40
 """
 
 from __future__ import annotations
@@ -45,7 +52,10 @@ def main(argv=None) -> None:
     ap.add_argument("--topk-ratio", type=float, default=18.5 / 591)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--dense", action="store_true")
     args = ap.parse_args(argv)
+    if args.dense:
+        return dense(args)
     B, H, L, blk = args.batch, args.heads, args.seq, args.blk
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
@@ -81,6 +91,63 @@ def main(argv=None) -> None:
            "bwd": {"ms": tb, "tflops_algorithmic": flops_bwd / tb / 1e9, "frac": flops_bwd / tb / 1e9 / peak,
                    "tflops_executed": 3.5 * flops_fwd / tb / 1e9},
            "peak_tflops": peak, "peak_kind": kind}
+    print(json.dumps(res))
+
+
+def dense(args) -> None:
+    B, H, L = args.batch, args.heads, args.seq
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def mk():
+        return torch.randn(B, H, L, 128, device=dev, generator=g).to(torch.bfloat16)
+
+    q0, k0, v0, do = mk(), mk(), mk(), mk()
+    flops = 4.0 * B * H * L * L * 128
+    peak, kind = _peak()
+
+    def run(fn):
+        q, k, v = (t.detach().clone().requires_grad_(True) for t in (q0, k0, v0))
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
+        o = fn(q, k, v)
+        ev[1].record()
+        o.backward(do)
+        ev[2].record()
+        torch.cuda.synchronize()
+        return ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), (o.detach(), q.grad, k.grad, v.grad)
+
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    def sdpa(q, k, v):
+        with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+            return torch.nn.functional.scaled_dot_product_attention(q, k, v)
+
+    res = {"what": "dense attention forward + backward, bf16, [B, H, L, 128], no mask", "B": B, "H": H, "L": L,
+           "fwd_tflop": flops / 1e12, "peak_tflops": peak, "peak_kind": kind}
+    outs = {}
+    for name, fn in (("ours", train.dense_attention), ("sdpa_cudnn", sdpa)):
+        try:
+            for _ in range(args.warmup):
+                run(fn)
+            ts = [run(fn) for _ in range(args.steps)]
+        except RuntimeError as exc:  # backend not available for this shape / build
+            res[name] = {"unavailable": str(exc).splitlines()[0][:200]}
+            continue
+        tf = sorted(t[0] for t in ts)[len(ts) // 2]
+        tb = sorted(t[1] for t in ts)[len(ts) // 2]
+        outs[name] = ts[-1][2]
+        res[name] = {"fwd_ms": tf, "bwd_ms": tb, "fwd_tflops": flops / tf / 1e9, "bwd_tflops": 2.5 * flops / tb / 1e9}
+    if len(outs) == 2:
+        rows = torch.randint(0, L, (512,), generator=torch.Generator().manual_seed(1)).to(dev)
+        cmp = {}
+        for i, n in enumerate(("o", "dq", "dk", "dv")):
+            a, r = outs["ours"][i][:, :, rows].float(), outs["sdpa_cudnn"][i][:, :, rows].float()
+            rms = r.pow(2).mean().sqrt()
+            cmp[n] = {"max_rel": ((a - r).abs().max() / rms).item(), "mean_rel": ((a - r).abs().mean() / rms).item()}
+        res["ours_vs_sdpa"] = cmp
+    if _lib.device_status() != 0:
+        raise RuntimeError(f"device error {_lib.device_status()}")
     print(json.dumps(res))
 
 
