@@ -9,6 +9,20 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 
+def reference_path(allow_checkout: bool = True):
+    """Directory from which the SparkDiffusion reference imports: ``SPARKDIFFUSION_REF``,
+    the installed copy ``baseline/_ref``, or (CPU tests in the build container only,
+    ``allow_checkout``) the read-only source checkout; None when none exists (the GPU box
+    has only the installed copy)."""
+    cands = [os.environ.get("SPARKDIFFUSION_REF", ""), os.path.join(ROOT, "baseline", "_ref")]
+    if allow_checkout:
+        cands.append("/root/reference")
+    for p in cands:
+        if p and os.path.isdir(os.path.join(p, "sparkdiffusion", "networks")):
+            return p
+    return None
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA (B200, sm_100a) device")
 

@@ -14,23 +14,17 @@ The reference is imported from ``SPARKDIFFUSION_REF``, ``baseline/_ref`` or the
 read-only checkout; the tests skip where none of them exists (the GPU box).
 """
 
-import os
 import sys
 
 import pytest
 import torch
 
+from conftest import reference_path
 from sparkdiffusion_b200 import registry
 from sparkdiffusion_b200.layer import WanSelfAttentionRoLaB200
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-
-
 def _reference_path():
-    for p in (os.environ.get("SPARKDIFFUSION_REF", ""), os.path.join(ROOT, "baseline", "_ref"), "/root/reference"):
-        if p and os.path.isdir(os.path.join(p, "sparkdiffusion", "networks")):
-            return p
-    return None
+    return reference_path(allow_checkout=True)
 
 
 @pytest.fixture(scope="module")

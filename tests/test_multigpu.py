@@ -192,11 +192,9 @@ MODEL_ROLA = dict(rola_topk_ratio=0.25, rola_rank=64, rola_blkq=128, rola_blkk=1
 def _reference_package_path():
     """The installed reference (``baseline/_ref`` or ``SPARKDIFFUSION_REF``); the
     read-only source checkout is not used here."""
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    for p in (os.environ.get("SPARKDIFFUSION_REF", ""), os.path.join(root, "baseline", "_ref")):
-        if p and os.path.isdir(os.path.join(p, "sparkdiffusion", "networks")):
-            return p
-    return None
+    from conftest import reference_path
+
+    return reference_path(allow_checkout=False)
 
 
 def _model_case(ref_path, dev):
