@@ -23,6 +23,7 @@ from conftest import reference_path
 from sparkdiffusion_b200 import registry
 from sparkdiffusion_b200.layer import WanSelfAttentionRoLaB200
 
+
 def _reference_path():
     return reference_path(allow_checkout=True)
 

@@ -25,6 +25,7 @@ from sparkdiffusion_b200 import train
 from sparkdiffusion_b200.layer import WanSelfAttentionRoLaB200
 from sparkdiffusion_b200.rope import wan_rope_freqs
 
+
 def _reference_path():
     return reference_path(allow_checkout=True)
 
