@@ -64,16 +64,21 @@ def assert_bf16_close(got, ref, name="", max_tol=BF16_MAX, mean_tol=BF16_MEAN, u
         mx, mn = rel_err(got, ref)
         assert mx <= max_tol and mn <= mean_tol, f"{name}: max-abs/rms={mx:.3e} mean-abs/rms={mn:.3e}"
         return
+    worst, mx, mn = bf16_bound_ratio(got, ref, max_tol, steps)
+    assert worst <= 1.0 and mn <= mean_tol, (f"{name}: max-abs/rms={mx:.3e} ({worst:.2f} of the per-element bound "
+                                             f"max({max_tol:g}*rms, {steps:g} bf16 step)), mean-abs/rms={mn:.3e}")
+
+
+def bf16_bound_ratio(got, ref, max_tol=BF16_MAX, steps=1.0):
+    """(worst element's |got - ref| over its bound max(``max_tol`` * RMS,
+    ``steps`` bf16 steps of the element), max-abs / RMS, mean-abs / RMS)."""
     g = got.detach().float().cpu()
     r = ref.detach().float().cpu()
     rms = r.pow(2).mean().sqrt().clamp_min(1e-30)
     d = (g - r).abs()
     step = torch.exp2(torch.floor(torch.log2(r.abs().clamp_min(1e-30))) - 7)
     bound = torch.maximum(max_tol * rms, steps * step)
-    worst = (d / bound).max().item()
-    mx, mn = (d.max() / rms).item(), (d.mean() / rms).item()
-    assert worst <= 1.0 and mn <= mean_tol, (f"{name}: max-abs/rms={mx:.3e} ({worst:.2f} of the per-element bound "
-                                             f"max({max_tol:g}*rms, {steps:g} bf16 step)), mean-abs/rms={mn:.3e}")
+    return (d / bound).max().item(), (d.max() / rms).item(), (d.mean() / rms).item()
 
 
 def assert_ulp_close(got, ref, name="", ulps=2, max_frac=1e-3, mean_tol=BF16_MEAN):

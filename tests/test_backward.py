@@ -15,7 +15,11 @@ bf16 steps of the element's own magnitude:
   P / dS terms);
 * against the exact gradient: max(2e-2 of the RMS, 4 steps), mean-abs <=
   3e-3 of the RMS (delta from the rounded forward output moves dS where
-  dP - delta cancels: ~0.5 % at the worst element);
+  dP - delta cancels: ~0.5 % at the worst element).  Where the algorithm
+  itself sits further from the exact gradient -- rows whose softmax runs over
+  two keys (a 2-row key block selected alone), where dS = P1 P2 (dP1 - dP2)
+  cancels and the bf16 output's delta moves it by up to ~4 bounds -- the
+  kernel may sit at most 1.25x as far from it as the staged oracle does;
 * lse within 1e-3 absolute (log2 units);
 * a whole layer's training step (fp32 parameters, the attention in bf16)
   against the same layer with the oracle's fp64 attention: max-abs <= 5e-2
@@ -25,7 +29,7 @@ bf16 steps of the element's own magnitude:
 import pytest
 import torch
 
-from conftest import assert_bf16_close
+from conftest import assert_bf16_close, bf16_bound_ratio
 from oracle import rola_oracle as orc
 from sparkdiffusion_b200 import _lib, ops, train
 
@@ -81,6 +85,10 @@ CASES = {
     "b128_batch2": (2, 1, 768, 128, 2),
     # block 64, even block count
     "b64_even": (1, 1, 768, 64, 4),
+    # short sequences: one full and one 36-row block of 64 (a single 128-row tile), top-1
+    "b64_short": (1, 1, 100, 64, 1),
+    # a 2-row last block of 128, top-1
+    "b128_short": (1, 1, 130, 128, 1),
 }
 
 
@@ -103,8 +111,11 @@ def test_sparse_attention_backward_matches_oracle(case):
     for name, got, ref, rs in zip(("dq", "dk", "dv"), (dq, dk, dv), exact, staged):
         assert_bf16_close(got, rs, f"{case} {name} (staged)", max_tol=STAGED_MAX, mean_tol=STAGED_MEAN,
                           ulp_floor=True, steps=STAGED_STEPS)
-        assert_bf16_close(got, ref, f"{case} {name} (exact)", max_tol=GRAD_MAX, mean_tol=GRAD_MEAN, ulp_floor=True,
-                          steps=GRAD_STEPS)
+        algo_worst, _, algo_mean = bf16_bound_ratio(rs, ref, GRAD_MAX, GRAD_STEPS)
+        worst, mx, mn = bf16_bound_ratio(got, ref, GRAD_MAX, GRAD_STEPS)
+        assert worst <= max(1.0, 1.25 * algo_worst) and mn <= max(GRAD_MEAN, 1.25 * algo_mean), (
+            f"{case} {name} (exact): max-abs/rms={mx:.3e} ({worst:.2f} of the per-element bound, the staged "
+            f"oracle {algo_worst:.2f}), mean-abs/rms={mn:.3e} (staged oracle {algo_mean:.3e})")
 
 
 def test_backward_deterministic_and_unselected_key_block_zero():
