@@ -336,8 +336,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
           }
         }
       }
+      // every MMA issued has completed before TMEM is freed, also on the abort
+      // path (where mbar_wait would return at once): bounded, ignores the flag
       mma_commit(bar(B_DRAIN));
-      mbar_wait(bar(B_DRAIN), 0, abort_flag, kDevTimeoutMma);
+      mbar_wait_until(bar(B_DRAIN), 0, globaltimer_ns() + kWaitLimitNs);
     }
   }
   } else if (warp >= 12) {

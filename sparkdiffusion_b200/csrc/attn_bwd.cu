@@ -332,6 +332,8 @@ __global__ void __launch_bounds__(bwd::DQ_THREADS, 1)
       }
       for (int i = max(0, n - (DQ_NBUF - 1)); i < n && ok; ++i) issue_dq(i);
       mma_commit(bar(G_ACC));
+      // every MMA issued has completed before TMEM is freed, also on the abort path
+      mbar_wait_until(bar(G_ACC), 0, globaltimer_ns() + kWaitLimitNs);
     }
   } else if (warp >= 4) {
     // -------------------------------------- dS of alternate steps, then the dQ epilogue
@@ -536,6 +538,8 @@ __global__ void __launch_bounds__(bwd::THREADS, 1)
       }
       if (ok && n > 0) issue_acc(n - 1);
       mma_commit(bar(G_ACC));
+      // every MMA issued has completed before TMEM is freed, also on the abort path
+      mbar_wait_until(bar(G_ACC), 0, globaltimer_ns() + kWaitLimitNs);
     }
   } else if (warp >= 4) {
     // ---------- P^T, dS^T of query columns [32 wg, 32 wg + 32) of every step, then the dK/dV epilogue

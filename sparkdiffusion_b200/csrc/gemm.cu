@@ -167,8 +167,10 @@ __global__ void __launch_bounds__(gemm::THREADS_SIDE, 1)
         }
         if (ok) mma_commit(acc_full(a));
       }
+      // every MMA issued has completed before TMEM is freed, also on the abort
+      // path (where mbar_wait would return at once): bounded, ignores the flag
       mma_commit(drain);
-      mbar_wait(drain, 0, abort_flag, kDevTimeoutMma);
+      mbar_wait_until(drain, 0, globaltimer_ns() + kWaitLimitNs);
     }
   } else if (warp < 6) {
     // epilogue warps 2..5: TMEM lane quadrant = warp % 4
@@ -483,8 +485,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(gemm2::THREADS, 1)
         }
         if (ok) mma_commit_pair(acc_full(a));
       }
+      // every MMA of the pair has completed before either CTA frees its TMEM
+      // (the cluster barrier below), also on the abort path
       mma_commit_pair_local(drain);
-      mbar_wait(drain, 0, abort_flag, kDevTimeoutMma);
+      mbar_wait_until(drain, 0, globaltimer_ns() + kWaitLimitNs);
     }
   } else {
     // ------------------------------------------------- epilogue warps 2..5
