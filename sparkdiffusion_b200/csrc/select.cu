@@ -395,7 +395,8 @@ int launch_select_fused(const __nv_bfloat16* pq, const __nv_bfloat16* pk, int BH
   else if (per <= 8) ROLA_SEL_RW(8);
   else if (per <= 16) ROLA_SEL_RW(16);
   else if (per <= 20) ROLA_SEL_RW(20);
-  else ROLA_SEL_RW(24);
+  else if (rw == 2) ROLA_SEL(24, 2);  // rw <= 2 here (no 4 x 24 instantiation)
+  else ROLA_SEL(24, 1);
 #undef ROLA_SEL_RW
 #undef ROLA_SEL
   return (int)cudaGetLastError();
