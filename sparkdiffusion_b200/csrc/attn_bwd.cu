@@ -33,9 +33,12 @@
 // (512 threads, three S / dP buffers, so the MMA warp runs two steps ahead),
 // the dkdv kernel two buffers (its two 128-column accumulators fill the rest
 // of the tensor memory) with both of its warpgroups on every step, 32
-// columns each.  Warpgroups 1 and 2 then store one 64-column half of the
-// accumulators each.  Every mbarrier wait is bounded (error flag + abort, as
-// in the forward).
+// columns each.  The CTA's warpgroups 1 and 2 (the first two softmax
+// warpgroups; warps 0-3 are the producer, the MMA issuer and two idle warps)
+// then store one 64-column half of the accumulators each.  Every mbarrier wait
+// is bounded (error flag + abort, as in the forward); on the abort path the
+// producer still drains its loads and the MMA issuer its MMAs (bounded waits
+// that ignore the abort flag) before the tensor memory is freed.
 #include "common.cuh"
 #include "kernels.h"
 
