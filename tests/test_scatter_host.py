@@ -157,8 +157,8 @@ def test_overlapped_exchange_writes_every_element_once(monkeypatch, B, Ls, H, p,
     """Every element of every rank's q / gate buffer is written exactly once,
     by the rank that owns its token, from the qkv row of that token, after
     the GEMM chunk that produced the row (the plan of the 2-GPU case with
-    chunks of 768 + 672 rows per rank, its unchunked counterpart, batch 2,
-    and the 8- and 4-rank plans)."""
+    chunks of 768 + 672 rows per rank, the same routine with one chunk, batch
+    2, the 8- and 4-rank plans, and C4 on 2 ranks)."""
     written, bases, dim, L, hpc, plans = _replay_exchange(monkeypatch, B, Ls, H, p, chunks)
     if (B, Ls, p, chunks) == (1, 1440, 2, None):  # the case that differed on 2 GPUs
         assert plans == [[(768, False), (672, True)]] * 2
